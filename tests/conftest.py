@@ -1,0 +1,24 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for sub in ("", "oracle", "paddleocr-vl-webgpu_b200"):
+    p = os.path.join(ROOT, sub)
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def cuda_lib():
+    """The product library (CUDA path) on a GPU box; fails loudly if it cannot load."""
+    import torch
+    if not torch.cuda.is_available():
+        pytest.fail("gpu-marked test needs a CUDA device")
+    from pvlc_b200 import abi
+    return abi.lib()
