@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention backend (one JSON line on rank 0).
+
+Headline workload (the one quoted at 1/2/4/8 GPUs):
+batched GQA decode sweep, 64 independent sequences per GPU, Q16/KV2/D128,
+18 layers of fp16 KV cache, context lengths U[512, 8192] (seeded), each step
+appends one token to every sequence of every layer.  A bench "step" is one
+decode step: 18 launches of the decode kernel (one per layer), each over the
+64 sequences.  Metric: decode-attention HBM GB/s (algorithmic bytes: K/V rows
+read + q/out + appended row, per launch) and tokens/s/GPU.  The KV caches
+(~10 GB per GPU) are far larger than the 126 MB L2, so no flush is needed.
+
+Components (rank 0): vision varlen prefill (configs[1], TFLOP/s) and decoder
+causal prefill (configs[2], TFLOP/s), each timed with CUDA events.
+
+--impl reference times the reference's algorithm on the host cores (the C++
+restatement of pvlc-cpu-ref in oracle/, because the Rust reference cannot be
+built here) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "paddleocr-vl-webgpu_b200"))
+
+QH, KVH, HD = 16, 2, 128
+LAYERS = 18
+SEQS_PER_GPU = 64
+L_MIN, L_MAX = 512, 8192
+METRIC = "decode-attn HBM GB/s (64 seqs x 18 layers, L~U[512,8192])"
+UNIT = "GB/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic_decode_bytes(lengths_after_append):
+    # K and V rows (2 heads x 128 fp16 each) + q + out (16 x 128 fp16) + appended K/V row
+    return sum(1024 * n + 8192 + 1024 for n in lengths_after_append)
+
+
+# --------------------------------------------------------------------- GPU arm
+def run_gpu(args, rank, world, local_rank, dist):
+    import numpy as np
+    import torch
+
+    from pvlc_b200 import abi, ops, positions
+
+    abi.check(abi.lib().pvlc_attn_device_check(), "device check")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    hbm_peak, tf_peak, peak_src = peaks()
+
+    # ---- synthetic workload (seeded per rank: this rank's request shard)
+    rng = np.random.default_rng(1 + rank)
+    L0 = rng.integers(L_MIN, L_MAX + 1, size=SEQS_PER_GPU).astype(np.int64)
+    steps, warm = args.steps, args.warmup
+    cap = int(L0.max()) + warm + steps + 8
+    B = SEQS_PER_GPU
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    kc = torch.empty((LAYERS, B, cap, KVH, HD), dtype=torch.float16, device=dev)
+    vc = torch.empty_like(kc)
+    kc.normal_(generator=g)
+    vc.normal_(generator=g)
+    kp = [torch.tensor([kc[l, b].data_ptr() for b in range(B)], dtype=torch.int64, device=dev)
+          for l in range(LAYERS)]
+    vp = [torch.tensor([vc[l, b].data_ptr() for b in range(B)], dtype=torch.int64, device=dev)
+          for l in range(LAYERS)]
+    q = torch.randn((LAYERS, B, QH, HD), generator=g, device=dev).half()
+    kn = torch.randn((LAYERS, B, KVH, HD), generator=g, device=dev).half()
+    vn = torch.randn((LAYERS, B, KVH, HD), generator=g, device=dev).half()
+    out = torch.empty((LAYERS, B, QH, HD), dtype=torch.float16, device=dev)
+    cos_np, sin_np = positions.linear_rope_tables(cap)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    ct0 = torch.tensor(L0, dtype=torch.int32, device=dev)
+    ws = [ops.DecodeWorkspace(B, dev) for _ in range(LAYERS)]
+
+    def step(ct, max_ct, ev=None):
+        for l in range(LAYERS):
+            if ev is not None:
+                ev[l][0].record(stream)
+            ops.decode(q[l], kn[l], vn[l], cos, sin, kp[l], vp[l], ct, cap, max_ct, ws[l],
+                       out=out[l])
+            if ev is not None:
+                ev[l][1].record(stream)
+        ct += 1
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    ct = ct0.clone()
+    max_ct = int(L0.max())
+    for i in range(warm):
+        step(ct, max_ct + i)
+    barrier()
+    # ---- timed region: device-only (inputs resident in HBM)
+    lengths = []
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    kevs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+             for _ in range(LAYERS)] for _ in range(steps)]
+    barrier()
+    t_start.record(stream)
+    for s in range(steps):
+        step(ct, max_ct + warm + s, kevs[s])
+        lengths.extend([int(x) + warm + s + 1 for x in L0] * LAYERS)
+    t_end.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    dev_ms = t_start.elapsed_time(t_end)
+    kernel_ms = [a.elapsed_time(b) for st in kevs for a, b in st]
+    flags = sum(w.errors() for w in ws)
+    if flags:
+        raise RuntimeError(f"decode kernels raised fault flags {flags:#x}")
+    bytes_rank = algorithmic_decode_bytes(lengths)
+    launches = steps * LAYERS
+
+    # ---- e2e: same steps through the public API with host buffers
+    qh = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    knh = torch.empty(kn.shape, dtype=kn.dtype, pin_memory=True)
+    vnh = torch.empty(vn.shape, dtype=vn.dtype, pin_memory=True)
+    qh.copy_(q)
+    knh.copy_(kn)
+    vnh.copy_(vn)
+    outh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    e2e_steps = steps
+    e_lengths = []
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    base = warm + steps
+    e0.record(stream)
+    for s in range(e2e_steps):
+        q.copy_(qh, non_blocking=True)
+        kn.copy_(knh, non_blocking=True)
+        vn.copy_(vnh, non_blocking=True)
+        step(ct, max_ct + base + s)
+        outh.copy_(out, non_blocking=True)
+        e_lengths.extend([int(x) + base + s + 1 for x in L0] * LAYERS)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    e_bytes_rank = algorithmic_decode_bytes(e_lengths)
+    h2d = (q.numel() + kn.numel() + vn.numel()) * 2
+    d2h = out.numel() * 2
+
+    # ---- aggregate over ranks: max time, summed bytes
+    t = torch.tensor([dev_ms, e2e_ms, bytes_rank, e_bytes_rank], dtype=torch.float64, device=dev)
+    if dist is not None:
+        tmax = t[:2].clone()
+        tsum = t[2:].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        dev_ms, e2e_ms = tmax.tolist()
+        bytes_all, e_bytes_all = tsum.tolist()
+    else:
+        bytes_all, e_bytes_all = bytes_rank, e_bytes_rank
+    value = bytes_all / (dev_ms * 1e-3) / 1e9
+    e2e_value = e_bytes_all / (e2e_ms * 1e-3) / 1e9
+    tok_per_s_per_gpu = B * steps / (dev_ms * 1e-3)
+    avg_kernel_ms = statistics.mean(kernel_ms)
+    achieved = (bytes_rank / launches) / (avg_kernel_ms * 1e-3) / 1e9
+
+    components = {}
+    if rank == 0 and not args.skip_components:
+        components = run_components(args, dev, tf_peak, peak_src)
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(dev_ms / steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16 caches/q/k/v; per-rank request shard)",
+        "config": {"workload": "configs[3] batched GQA decode sweep",
+                   "seqs_per_gpu": B, "layers": LAYERS, "heads": "Q16/KV2/D128",
+                   "context": f"U[{L_MIN},{L_MAX}] seed 1+rank, +1 row per step",
+                   "parallelism": f"dp{world} (requests sharded, no hot-path collective)",
+                   "l2": "inputs larger than L2 (~10 GB KV per GPU)"},
+        "tokens_per_s_per_gpu": round(tok_per_s_per_gpu, 1),
+        "gpu_launches": launches,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "pvlc_b200.ops.decode -> C ABI pvlc_attn_decode, pinned host q/k/v in, out back"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_source": peak_src, "kernel": "pvlc::decode::decode_kernel",
+                     "avg_launch_ms": round(avg_kernel_ms, 5),
+                     "traffic": args.traffic_bytes},
+        "clocks": clocks,
+        "components": components,
+    }
+    if not args.skip_cpu:
+        line["cpu_baseline"] = cpu_decode_baseline(args.cpu_seconds)
+    return line
+
+
+def run_components(args, dev, tf_peak, peak_src):
+    import numpy as np
+    import torch
+
+    from pvlc_b200 import ops, positions
+
+    res = {}
+    stream = torch.cuda.current_stream()
+
+    def timeit(fn, iters, warm=3):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(iters)]
+        for a, b in evs:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    # vision varlen prefill, configs[1]
+    grids = [(1, 32, 32), (1, 48, 48), (1, 24, 24), (1, 64, 64)]
+    cu = [0, 1024, 3328, 3904, 8000]
+    T = 8000
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    nrot = 8   # rotate input sets so consecutive launches do not hit the same L2 lines
+    qs = [torch.randn((T, 16, 72), generator=g, device=dev).half() for _ in range(nrot)]
+    ks = [torch.randn((T, 16, 72), generator=g, device=dev).half() for _ in range(nrot)]
+    vs = [torch.randn((T, 16, 72), generator=g, device=dev).half() for _ in range(nrot)]
+    c_np, s_np = positions.vision_rope_tables(grids)
+    vcos, vsin = torch.from_numpy(c_np).to(dev), torch.from_numpy(s_np).to(dev)
+    vout = torch.empty_like(qs[0])
+    it = [0]
+
+    def vis():
+        i = it[0] % nrot
+        it[0] += 1
+        ops.vision_varlen_attention(qs[i], ks[i], vs[i], cu, vcos, vsin, out=vout)
+
+    ms = timeit(vis, 20)
+    flops = 4.0 * 72 * 16 * sum((cu[i + 1] - cu[i]) ** 2 for i in range(4))
+    tf = flops / (ms * 1e-3) / 1e12
+    res["vision_prefill"] = {"workload": "configs[1] 8000 tokens, segments 1024/2304/576/4096, H16 D72, 2-D RoPE",
+                             "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+                             "roofline": {"bound": "tensor", "achieved": round(tf, 2),
+                                          "peak": tf_peak, "unit": "TFLOP/s",
+                                          "frac": round(tf / tf_peak, 4),
+                                          "peak_source": peak_src},
+                             "kernel": "pvlc::vision::vision_mma_kernel"}
+
+    # decoder causal prefill, configs[2]
+    ids = [7] * 19 + [101305] + [100295] * 1480 + [9] * 64
+    pos, delta = positions.mrope_position_ids(ids, [(1, 80, 74)])
+    Tp = len(ids)
+    pc, ps = positions.mrope_tables(pos, delta, Tp + 256)
+    pcos, psin = torch.from_numpy(pc).to(dev), torch.from_numpy(ps).to(dev)
+    g.manual_seed(3)
+    pq = [torch.randn((Tp, 16, 128), generator=g, device=dev).half() for _ in range(nrot)]
+    pk = [torch.randn((Tp, 2, 128), generator=g, device=dev).half() for _ in range(nrot)]
+    pv = [torch.randn((Tp, 2, 128), generator=g, device=dev).half() for _ in range(nrot)]
+    kcache = torch.empty((Tp + 256, 2, 128), dtype=torch.float16, device=dev)
+    vcache = torch.empty_like(kcache)
+    pout = torch.empty_like(pq[0])
+
+    def pre():
+        i = it[0] % nrot
+        it[0] += 1
+        ops.decoder_prefill(pq[i], pk[i], pv[i], pcos, psin, kcache, vcache, out=pout)
+
+    ms = timeit(pre, 20)
+    flops = 4.0 * 128 * 16 * Tp * (Tp + 1) / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    res["decoder_prefill"] = {"workload": "configs[2] T=1564 (20 text + 40x37 image + 64 text), Q16/KV2/D128, M-RoPE",
+                              "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+                              "roofline": {"bound": "tensor", "achieved": round(tf, 2),
+                                           "peak": tf_peak, "unit": "TFLOP/s",
+                                           "frac": round(tf / tf_peak, 4),
+                                           "peak_source": peak_src},
+                              "kernel": "pvlc::prefill::prefill_mma_kernel"}
+    return res
+
+
+# --------------------------------------------------------------- CPU (oracle)
+def cpu_decode_baseline(seconds: float):
+    """The C++ restatement of pvlc-cpu-ref's decode step on the host cores, over a
+    bounded sample of the decode-sweep workload (same length distribution)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    from pvlc_b200 import positions
+
+    rng = np.random.default_rng(1)
+    L0 = rng.integers(L_MIN, L_MAX + 1, size=SEQS_PER_GPU)
+    cap = L_MAX + 64
+    cos, sin = positions.linear_rope_tables(cap)
+    data_rng = np.random.default_rng(5)
+    kc = data_rng.standard_normal((cap, KVH, HD)).astype(np.float16).astype(np.float32)
+    vc = data_rng.standard_normal((cap, KVH, HD)).astype(np.float16).astype(np.float32)
+    q = data_rng.standard_normal((QH * HD,)).astype(np.float32)
+    kn = data_rng.standard_normal((KVH * HD,)).astype(np.float32)
+    vn = data_rng.standard_normal((KVH * HD,)).astype(np.float32)
+    done_bytes, calls = 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        L = int(L0[calls % len(L0)])
+        O.decode_step(q, kn, vn, cos, sin, L, kc, vc, L)
+        done_bytes += 1024 * (L + 1) + 8192 + 1024
+        calls += 1
+    el = time.perf_counter() - t0
+    return {"value": round(done_bytes / el / 1e9, 4), "unit": UNIT, "cores": O.threads(),
+            "kind": "port",
+            "sample": f"{calls} sequence-layer decode steps (L from the seed-1 U[512,8192] draw), "
+                      f"{el:.1f} s, OpenMP over query heads",
+            "tokens_per_s": round(calls / el / LAYERS, 3)}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return None
+    base = cpu_decode_baseline(args.cpu_seconds)
+    return {"impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "configs[3] batched GQA decode sweep (bounded CPU sample)"},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference is Rust (no cargo/rustc here); its f32 algorithm is timed via the "
+                    "C++ restatement in oracle/"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-components", action="store_true")
+    ap.add_argument("--traffic-bytes", type=float, default=None,
+                    help="ncu dram bytes per decode launch, when measured")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+    else:
+        if world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as tdist
+            torch.cuda.set_device(local_rank)
+            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                     device_id=torch.device("cuda", local_rank))
+            dist = tdist
+        line = run_gpu(args, rank, world, local_rank, dist)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,205 @@
+/*
+ * pvlc_cuda_attn.h -- C ABI of the B200 (sm_100a) attention backend for the
+ * PaddleOCR-VL engine.
+ *
+ * This library replaces the attention subset of the reference engine's
+ * operator contract (crate pvlc-runtime-core, KernelId / KernelInvocation /
+ * descriptor -> plan) and the WGSL kernels that implement it (crate
+ * pvlc-wgsl).  Every entry point:
+ *   - validates its arguments on the host first and returns a nonzero status
+ *     with no device effect when they are invalid (the reference's
+ *     "preflight, no effect" rule, crates/pvlc-runtime-core/src/lib.rs:5335-5395);
+ *   - takes caller-owned device pointers and performs no allocation;
+ *   - enqueues work asynchronously on the caller's stream (`stream` is a
+ *     cudaStream_t passed as void*; NULL means the legacy default stream);
+ *   - is thread-safe as long as concurrent calls use distinct output buffers
+ *     and workspaces.
+ * Plain C types only, so a Rust `extern "C"` block, cgo or ctypes can bind it.
+ *
+ * Tensor layout is token-major throughout, as in the reference
+ * (crates/pvlc-cpu-ref/src/lib.rs:3424-3432): element (token, head, dim) of a
+ * [tokens, heads, head_dim] tensor sits at (token*heads + head)*head_dim + dim.
+ * The decoder KV cache of one layer is [capacity, 2, 128]
+ * (crates/pvlc-runtime-core/src/lib.rs:883-888).  pvlc_half is IEEE binary16.
+ */
+#ifndef PVLC_CUDA_ATTN_H
+#define PVLC_CUDA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t pvlc_half;
+
+/* Status codes.  1..15 mirror InvocationErrorCode in declaration order
+ * (crates/pvlc-runtime-core/src/lib.rs:5335-5351); 64+ are CUDA-side. */
+enum pvlc_status {
+  PVLC_OK = 0,
+  PVLC_ZERO_DIMENSION = 1,
+  PVLC_LENGTH_MISMATCH = 2,
+  PVLC_ARITHMETIC_OVERFLOW = 3,
+  PVLC_INVALID_ROTARY_DIMENSION = 5,
+  PVLC_INVALID_ROPE_BASE = 6,
+  PVLC_UNSUPPORTED_HEAD_DIMENSION = 7,
+  PVLC_INVALID_DECODER_GEOMETRY = 8,
+  PVLC_INVALID_VISION_GEOMETRY = 9,
+  PVLC_INVALID_SEQUENCE_BOUNDARIES = 11,
+  PVLC_NON_FINITE_INPUT = 15,
+  PVLC_NULL_POINTER = 64,
+  PVLC_MISALIGNED_POINTER = 65,
+  PVLC_WORKSPACE_TOO_SMALL = 66,
+  PVLC_CAPACITY_EXHAUSTED = 67,
+  PVLC_CUDA_ERROR = 68,
+  PVLC_DEVICE_UNSUPPORTED = 69,
+  PVLC_DEVICE_FAULT_FLAG = 70
+};
+
+/* Pinned geometry (crates/pvlc-cpu-ref/src/lib.rs:544-553,
+ * crates/pvlc-runtime-core/src/lib.rs:179-180). */
+#define PVLC_DECODER_QUERY_HEADS 16u
+#define PVLC_DECODER_KV_HEADS 2u
+#define PVLC_DECODER_HEAD_DIM 128u
+#define PVLC_VISION_MAX_HEAD_DIM 72u
+#define PVLC_VISION_MAX_SEGMENTS 256u
+#define PVLC_DECODE_MAX_BATCH 2048u
+
+/* Human-readable name of a status code (static storage). */
+const char* pvlc_attn_status_string(int status);
+
+/* Library / device identification: returns PVLC_OK when the current device is
+ * an sm_100 part this library was built for. */
+int pvlc_attn_device_check(void);
+
+/* ----------------------------------------------------------------------------
+ * Path 1: vision-encoder bidirectional varlen attention with fused 2-D RoPE.
+ *
+ * Replaces KernelId::VisionRope2dF16 followed by KernelId::VisionAttentionF16
+ * (crates/pvlc-runtime-core/src/lib.rs:65-79, invocation :248-256 plan
+ * :443-478; WGSL crates/pvlc-wgsl/src/lib.rs:2309-2454,2553-2596; call site
+ * crates/pvlc-runtime-web/src/web.rs:4797-4803).
+ *
+ * q, k, v, out: device [tokens, heads, head_dim] fp16.
+ * cu_seqlens_host: HOST array of segments+1 packed-image boundaries (starts at
+ *   0, strictly increasing, ends at tokens; validate_sequence_boundaries,
+ *   crates/pvlc-cpu-ref/src/lib.rs:3393-3405).  Copied into the launch, so it
+ *   may be reused as soon as the call returns.
+ * rope_cos, rope_sin: device [tokens, head_dim/2] f32 tables (the reference's
+ *   visionRope2dTables, web/engine/multimodal_ocr.mjs:98-155), or both NULL
+ *   for no rotation.  Pair p of a head rotates dims (p, p + head_dim/2).
+ * Attention never crosses a segment boundary; scale is 1/sqrt(head_dim).
+ * head_dim must be 72 (the pinned vision head); heads <= 64.
+ */
+int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                            const uint32_t* cu_seqlens_host, uint32_t segments,
+                            uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                            const float* rope_cos, const float* rope_sin, pvlc_half* out,
+                            void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Path 2: decoder causal GQA prefill with fused 3-section M-RoPE and in-place
+ * fp16 KV-cache write, for one layer of the pinned decoder (Q16/KV2/D128).
+ *
+ * Replaces KernelId::DecoderPrefillMropeF32 -> DecoderKvAppendRangeF32 ->
+ * DecoderPrefillGqaF32 (crates/pvlc-runtime-core/src/lib.rs:51-55, stage
+ * order :2613-2629, plan :2592-2596,2637-2642; WGSL
+ * crates/pvlc-wgsl/src/lib.rs:1262-1416).
+ *
+ * q: device [tokens, 16, 128] fp16 (before RoPE); k, v: device [tokens, 2, 128]
+ * fp16 (k before RoPE).  rope_cos/rope_sin: device [3, rope_rows, 128] f32
+ * axis-major tables (ropeTables, web/engine/multimodal_ocr.mjs:937-986); rows
+ * [0, tokens) are used, dim d takes axis 0/1/2 for (d mod 64) in [0,16) /
+ * [16,40) / [40,64).  k_cache, v_cache: device [cache_capacity, 2, 128] fp16;
+ * rows [0, tokens) receive the rotated key and the raw value.  out: device
+ * [tokens, 16, 128] fp16.  Requires tokens <= cache_capacity, tokens <= rope_rows.
+ */
+int pvlc_attn_decoder_prefill(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                              const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                              uint32_t tokens, uint32_t cache_capacity, pvlc_half* k_cache,
+                              pvlc_half* v_cache, pvlc_half* out, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Path 3: batched single-token GQA decode against per-sequence fp16 KV caches
+ * (split-KV flash decoding with an in-kernel combine), with the decode M-RoPE
+ * and the KV append fused.
+ *
+ * Replaces, per sequence, KernelId::DecoderMropeF32 -> DecoderKvAppendF32 ->
+ * DecoderGqaSplitPartialF32 -> DecoderGqaSplitMergeF32
+ * (crates/pvlc-runtime-core/src/lib.rs:39-47; split plan :2861-2979; session
+ * step crates/pvlc-runtime-native/src/decoder_kv_session.rs:548-768).
+ *
+ * q: device [batch, 16, 128] fp16 (before RoPE); k_new, v_new: device
+ *   [batch, 2, 128] fp16 (k before RoPE).
+ * rope_cos/rope_sin: device [3, rope_rows, 128] f32; sequence b rotates with
+ *   row rope_row[b] (device array), or row cache_tokens[b] when rope_row is NULL.
+ * k_cache, v_cache: device arrays of `batch` device pointers, each to a
+ *   [cache_capacity, 2, 128] fp16 cache (16-byte aligned).
+ * cache_tokens: device [batch] rows already in each cache (before the append).
+ *   The rotated k_new and v_new are written at row cache_tokens[b] and the
+ *   attention runs over cache_tokens[b] + 1 rows.  The caller advances
+ *   cache_tokens after the call.
+ * max_cache_tokens: host upper bound of cache_tokens[b]; must be < cache_capacity.
+ *   A sequence whose device value exceeds it (or rope row out of range) is
+ *   skipped and flagged; read flags with pvlc_attn_decode_errors.
+ * workspace: device scratch of pvlc_attn_decode_workspace_bytes(batch) bytes,
+ *   zeroed once with pvlc_attn_decode_workspace_init before first use; it
+ *   is reusable across calls on the same stream without re-initialisation.
+ * out: device [batch, 16, 128] fp16.
+ */
+size_t pvlc_attn_decode_workspace_bytes(uint32_t batch);
+int pvlc_attn_decode_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half* v_new,
+                     const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                     const uint32_t* rope_row, pvlc_half* const* k_cache,
+                     pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                     uint32_t cache_capacity, uint32_t max_cache_tokens, uint32_t batch,
+                     void* workspace, size_t workspace_bytes, pvlc_half* out, void* stream);
+/* Synchronously reads and clears the device-side fault flags of a decode
+ * workspace (bit 0: cache row out of range, bit 1: rope row out of range,
+ * bit 2: misaligned cache pointer, bit 3: pipeline wait timed out).  Returns
+ * PVLC_OK when no flag was set, PVLC_DEVICE_FAULT_FLAG otherwise. */
+int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Plans: the host-side half of the contract, callable without a GPU.
+ * They run the same validation as the launch entry points and report the
+ * launch geometry the library will use.
+ */
+typedef struct pvlc_plan {
+  uint32_t grid[3];
+  uint32_t block[3];
+  uint32_t shared_bytes;
+  uint32_t work_items;       /* tiles or (sequence, chunk) units */
+  uint64_t output_elements;
+  uint64_t output_bytes;
+  uint64_t workspace_bytes;
+  double flops;              /* algorithmic FLOPs (unpadded) */
+  double hbm_bytes;          /* algorithmic bytes */
+} pvlc_plan;
+
+/* Mirrors KernelInvocation::VisionAttentionF32::plan
+ * (crates/pvlc-runtime-core/src/lib.rs:443-478). */
+int pvlc_plan_vision_varlen(const uint32_t* cu_seqlens_host, uint32_t segments, uint32_t tokens,
+                            uint32_t heads, uint32_t head_dim, pvlc_plan* plan);
+/* Mirrors the prefill geometry checks of plan_decoder_stack_prefill_geometry
+ * (crates/pvlc-runtime-core/src/lib.rs:2500-2653). */
+int pvlc_plan_decoder_prefill(uint32_t tokens, uint32_t cache_capacity, uint32_t rope_rows,
+                              pvlc_plan* plan);
+/* Mirrors DecoderKvSessionDescriptor / plan_decoder_kv_session_geometry and
+ * plan_cache_transition (crates/pvlc-runtime-core/src/lib.rs:980-1159):
+ * pinned Q16/KV2/D128, prefix_tokens < cache_capacity. */
+int pvlc_plan_decoder_kv_session(uint32_t query_heads, uint32_t kv_heads, uint32_t head_dim,
+                                 uint32_t prefix_tokens, uint32_t cache_capacity,
+                                 pvlc_plan* plan);
+/* Batched decode launch plan for a batch whose cache rows (before append)
+ * are cache_tokens_host[0..batch). */
+int pvlc_plan_decode(const uint32_t* cache_tokens_host, uint32_t batch, uint32_t cache_capacity,
+                     pvlc_plan* plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PVLC_CUDA_ATTN_H */

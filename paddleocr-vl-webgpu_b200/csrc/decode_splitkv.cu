@@ -1,0 +1,541 @@
+// decode_splitkv.cu -- batched single-token GQA decode (pinned Q16/KV2/D128)
+// against per-sequence fp16 KV caches, for B200 (sm_100a).
+//
+// Reference path replaced (one launch per layer step for the whole batch):
+//   DecoderMropeF32 -> DecoderKvAppendF32 -> DecoderGqaSplitPartialF32 ->
+//   DecoderGqaSplitMergeF32
+//   (crates/pvlc-runtime-native/src/decoder_kv_session.rs:548-768;
+//    arithmetic crates/pvlc-cpu-ref/src/lib.rs:858-927,1420-1450).
+//
+// Design (HBM-bound: ~8 FLOP per byte of KV):
+//   * Stream-K split: the batch's KV rows, cut into 32-row tiles, are laid
+//     end to end and split evenly over one CTA per SM, so every SM streams the
+//     same number of bytes whatever the per-sequence lengths are.  A CTA's
+//     range may cover the tail of one sequence and the head of the next.
+//   * One producer warp streams 512-byte cache rows (both KV heads) into a
+//     4-stage shared-memory ring with 1-D bulk async copies signalled on
+//     mbarriers; rows land at a 528-byte pitch so ldmatrix is conflict free.
+//   * Eight consumer warps (2 tile-parity groups x 2 KV heads x 2 row halves)
+//     run the 8 query heads of a KV group as the N=8 side of mma.m16n8k16:
+//     S^T = K Q^T (keys on M), online softmax over keys in f32 (exp2 domain),
+//     P^T transposed in registers with movmatrix, O^T += V^T P^T.
+//   * Decode M-RoPE of q is applied while building the Q fragments; the new
+//     key is rotated, patched into the staged tile and written to the cache
+//     row cache_tokens[b] by the one warp that owns that row.
+//   * Per-sequence partials (unnormalised O, running max, running sum) are
+//     merged across warps in shared memory; a sequence split over several
+//     CTAs is combined by the last CTA to finish it (atomic ticket, no
+//     spinning), which also resets the ticket for the next launch.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+#include "pvlc_common.cuh"
+#include "pvlc_internal.h"
+
+namespace pvlc {
+namespace decode {
+
+constexpr int HD = 128;
+constexpr int KVH = 2;
+constexpr int QH = 16;
+constexpr int GROUP = 8;
+constexpr int TILE = 32;          // cache rows per pipeline stage
+constexpr int STAGES = 4;
+constexpr int ROW_BYTES = KVH * HD * 2;   // 512
+constexpr int ROW_PITCH = ROW_BYTES + 16; // 528: conflict-free ldmatrix rows
+constexpr int STAGE_BYTES = TILE * ROW_PITCH;
+constexpr int CONSUMER_WARPS = 8;
+constexpr int THREADS = (CONSUMER_WARPS + 1) * 32;
+constexpr int CONSUMER_THREADS = CONSUMER_WARPS * 32;
+constexpr int MAX_BATCH = 2048;
+constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]
+
+// shared memory map (bytes)
+constexpr int SM_K = 0;
+constexpr int SM_V = SM_K + STAGES * STAGE_BYTES;
+constexpr int SM_MERGE_ACC = SM_V + STAGES * STAGE_BYTES;          // [8 warps][8 heads][128]
+constexpr int SM_MERGE_M = SM_MERGE_ACC + CONSUMER_WARPS * GROUP * HD * 4;
+constexpr int SM_MERGE_L = SM_MERGE_M + CONSUMER_WARPS * GROUP * 4;
+constexpr int SM_TILE_OFF = SM_MERGE_L + CONSUMER_WARPS * GROUP * 4;  // [MAX_BATCH+1]
+constexpr int SM_BARS = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
+constexpr int SM_MISC = SM_BARS + 2 * STAGES * 8;
+constexpr int SMEM_BYTES = SM_MISC + 64;
+
+static_assert(SMEM_BYTES <= 227 * 1024, "decode shared memory exceeds the sm_100 limit");
+
+struct Params {
+  const __half* q;
+  const __half* k_new;
+  const __half* v_new;
+  const float* rope_cos;
+  const float* rope_sin;
+  const uint32_t* rope_row;
+  __half* const* k_cache;
+  __half* const* v_cache;
+  const uint32_t* cache_tokens;
+  uint32_t rope_rows;
+  uint32_t capacity;
+  uint32_t max_cache_tokens;
+  uint32_t batch;
+  uint32_t* flags;
+  uint32_t* tickets;
+  float* partials;
+  __half* out;
+};
+
+// Number of 32-row tiles of sequence b after the append, 0 when the sequence
+// is invalid (and then flagged by block 0).
+__device__ __forceinline__ uint32_t seq_tiles(const Params& p, uint32_t b, bool report) {
+  const uint32_t ct = __ldg(p.cache_tokens + b);
+  uint32_t bad = 0;
+  if (ct > p.max_cache_tokens || ct >= p.capacity) bad |= kFlagCacheRow;
+  const uint32_t rr = p.rope_row ? __ldg(p.rope_row + b) : ct;
+  if (rr >= p.rope_rows) bad |= kFlagRopeRow;
+  const uintptr_t kp = reinterpret_cast<uintptr_t>(p.k_cache[b]);
+  const uintptr_t vp = reinterpret_cast<uintptr_t>(p.v_cache[b]);
+  if ((kp | vp) & 15u) bad |= kFlagMisaligned;
+  if (bad) {
+    if (report) atomicOr(p.flags, bad);
+    return 0;
+  }
+  return (ct + 1 + TILE - 1) / TILE;
+}
+
+// max{i : floor(i*NT/G) <= x}: the CTA whose tile range holds global tile x.
+__device__ __forceinline__ uint32_t owner_cta(uint64_t x, uint64_t G, uint64_t NT) {
+  return static_cast<uint32_t>(((x + 1) * G + NT - 1) / NT - 1);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* tile_off = reinterpret_cast<uint32_t*>(smem + SM_TILE_OFF);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM_BARS);
+  uint64_t* empty_bar = full_bar + STAGES;
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
+  // misc[0]: abort flag, misc[1]: "this CTA combines" flag
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint32_t B = p.batch;
+
+  // ---- schedule: exclusive prefix sum of per-sequence tile counts (warp 0)
+  if (warp == 0) {
+    const uint32_t per = (B + 31) / 32;
+    const uint32_t b0 = min(B, lane * per), b1 = min(B, b0 + per);
+    uint32_t s = 0;
+    for (uint32_t b = b0; b < b1; ++b) s += seq_tiles(p, b, false);
+    uint32_t incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    uint32_t run = incl - s;
+    for (uint32_t b = b0; b < b1; ++b) {
+      tile_off[b] = run;
+      run += seq_tiles(p, b, blockIdx.x == 0);
+    }
+    if (lane == 31) tile_off[B] = incl;
+  }
+  if (tid == 0) {
+    misc[0] = 0;
+    misc[1] = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 4);
+    }
+    fence_mbar_init();
+  }
+  // zero the staging ring once: rows past a sequence end are never copied and
+  // must hold finite values (P = 0 there, and 0 * NaN would poison O)
+  {
+    uint4* z = reinterpret_cast<uint4*>(smem + SM_K);
+    const int n16 = 2 * STAGES * STAGE_BYTES / 16;
+    for (int i = tid; i < n16; i += THREADS) z[i] = make_uint4(0, 0, 0, 0);
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+
+  const uint64_t NT = tile_off[B];
+  // Block 0 zero-fills the outputs of sequences that were rejected.
+  if (blockIdx.x == 0) {
+    for (uint32_t b = warp; b < B; b += THREADS / 32) {
+      if (tile_off[b] == tile_off[b + 1]) {
+        uint2* o = reinterpret_cast<uint2*>(p.out + (size_t)b * QH * HD);
+        for (int i = lane; i < QH * HD / 4; i += 32) o[i] = make_uint2(0, 0);
+      }
+    }
+  }
+  if (NT == 0) return;
+  const uint64_t G = umin64(gridDim.x, NT);
+  if (blockIdx.x >= G) return;
+  const uint64_t t0 = blockIdx.x * NT / G;
+  const uint64_t t1 = (blockIdx.x + 1) * NT / G;
+
+  // first sequence touching t0: last b with tile_off[b] <= t0 < tile_off[b+1]
+  auto seq_of = [&](uint64_t t) -> uint32_t {
+    uint32_t lo = 0, hi = B;  // invariant: tile_off[lo] <= t < tile_off[hi]
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (tile_off[mid] <= t) lo = mid; else hi = mid;
+    }
+    return lo;
+  };
+
+  if (warp == CONSUMER_WARPS) {
+    // ======================= producer warp =======================
+    uint32_t b = seq_of(t0);
+    const __half* kc = p.k_cache[b];
+    const __half* vc = p.v_cache[b];
+    uint32_t L = __ldg(p.cache_tokens + b) + 1;
+    uint32_t issued[STAGES] = {0, 0, 0, 0};
+    bool aborted = false;
+    for (uint64_t it = 0; it < t1 - t0; ++it) {
+      const uint64_t gt = t0 + it;
+      if (gt >= tile_off[b + 1]) {
+        while (gt >= tile_off[b + 1]) ++b;
+        kc = p.k_cache[b];
+        vc = p.v_cache[b];
+        L = __ldg(p.cache_tokens + b) + 1;
+      }
+      const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
+      const uint32_t n = umin32(TILE, L - row0);
+      const int stage = static_cast<int>(it % STAGES);
+      const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+      if (misc[0] || !mbar_wait(&empty_bar[stage], ph ^ 1u)) {
+        aborted = true;
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&full_bar[stage], n * 2u * ROW_BYTES);
+      __syncwarp();
+      if (lane < static_cast<int>(n)) {
+        const size_t row = row0 + lane;
+        bulk_g2s(smem + SM_K + stage * STAGE_BYTES + lane * ROW_PITCH, kc + row * (KVH * HD),
+                 ROW_BYTES, &full_bar[stage]);
+        bulk_g2s(smem + SM_V + stage * STAGE_BYTES + lane * ROW_PITCH, vc + row * (KVH * HD),
+                 ROW_BYTES, &full_bar[stage]);
+      }
+      issued[stage] = static_cast<uint32_t>(it / STAGES) + 1;
+    }
+    if (aborted) {
+      if (lane == 0) atomicOr(p.flags, kFlagTimeout);
+      misc[0] = 1;
+    }
+    // never leave the CTA with bulk copies in flight
+    for (int s = 0; s < STAGES; ++s)
+      if (issued[s]) mbar_wait(&full_bar[s], (issued[s] - 1) & 1u);
+    return;
+  }
+
+  // ======================= consumer warps =======================
+  const int grp = warp >> 2;          // tile parity handled by this warp
+  const int kvh = (warp >> 1) & 1;    // KV head
+  const int half = warp & 1;          // rows [16*half, 16*half+16) of a tile
+  const int g = lane >> 2;            // fragment row group
+  const int c = lane & 3;             // fragment column pair
+  const float qk_scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));  // log2(e)/sqrt(d)
+
+  float* merge_acc = reinterpret_cast<float*>(smem + SM_MERGE_ACC);
+  float* merge_m = reinterpret_cast<float*>(smem + SM_MERGE_M);
+  float* merge_l = reinterpret_cast<float*>(smem + SM_MERGE_L);
+
+  uint32_t b = seq_of(t0);
+  while (true) {
+    const uint64_t s0 = umax64(t0, tile_off[b]);
+    const uint64_t s1 = umin64(t1, tile_off[b + 1]);
+    const uint32_t ct = __ldg(p.cache_tokens + b);
+    const uint32_t L = ct + 1;
+    const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + b) : ct;
+
+    // ---- rotated Q^T fragments (B operand: k = dim, n = head) for this KV group
+    uint32_t qf[8][2];
+    {
+      const __half* qrow = p.q + ((size_t)b * QH + kvh * GROUP + g) * HD;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float r[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int d = ks * 16 + hh * 8 + 2 * c + e;
+            const float x = __half2float(qrow[d]);
+            const float partner = d < 64 ? -__half2float(qrow[d + 64]) : __half2float(qrow[d - 64]);
+            const size_t ti = ((size_t)mrope_axis(d) * p.rope_rows + rrow) * HD + d;
+            r[e] = x * __ldg(p.rope_cos + ti) + partner * __ldg(p.rope_sin + ti);
+          }
+          qf[ks][hh] = pack_half2(r[0], r[1]);
+        }
+      }
+    }
+
+    float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F};
+    float l_run[2] = {0.f, 0.f};
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    for (uint64_t gt = s0 + (((s0 - t0) ^ grp) & 1); gt < s1; gt += 2) {
+      const uint64_t it = gt - t0;
+      const int stage = static_cast<int>(it % STAGES);
+      const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+      if (misc[0]) break;
+      if (!mbar_wait(&full_bar[stage], ph)) {
+        if (lane == 0) atomicOr(p.flags, kFlagTimeout);
+        misc[0] = 1;
+        break;
+      }
+      const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
+      const int n_valid = static_cast<int>(umin32(TILE, L - row0)) - half * 16;
+      uint8_t* kst = smem + SM_K + stage * STAGE_BYTES;
+      uint8_t* vst = smem + SM_V + stage * STAGE_BYTES;
+      if (n_valid > 0) {
+        // ---- the appended token lives in this warp's rows: rotate + patch
+        const int newrow = static_cast<int>(ct - row0);
+        if (newrow >= half * 16 && newrow < half * 16 + 16) {
+          const __half* kn = p.k_new + ((size_t)b * KVH + kvh) * HD;
+          const __half* vn = p.v_new + ((size_t)b * KVH + kvh) * HD;
+          __half kr[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int d = lane * 4 + e;
+            const float x = __half2float(kn[d]);
+            const float partner = d < 64 ? -__half2float(kn[d + 64]) : __half2float(kn[d - 64]);
+            const size_t ti = ((size_t)mrope_axis(d) * p.rope_rows + rrow) * HD + d;
+            kr[e] = __float2half_rn(x * __ldg(p.rope_cos + ti) + partner * __ldg(p.rope_sin + ti));
+          }
+          const uint2 kv = *reinterpret_cast<uint2*>(kr);
+          const uint2 vv = *reinterpret_cast<const uint2*>(vn + lane * 4);
+          *reinterpret_cast<uint2*>(kst + newrow * ROW_PITCH + kvh * HD * 2 + lane * 8) = kv;
+          *reinterpret_cast<uint2*>(vst + newrow * ROW_PITCH + kvh * HD * 2 + lane * 8) = vv;
+          *reinterpret_cast<uint2*>(p.k_cache[b] + (size_t)ct * KVH * HD + kvh * HD + lane * 4) = kv;
+          *reinterpret_cast<uint2*>(p.v_cache[b] + (size_t)ct * KVH * HD + kvh * HD + lane * 4) = vv;
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+
+        // ---- S^T[16 keys x 8 heads] = K[16 x 128] * Q^T[128 x 8]
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          // ldmatrix.x4 lanes: matrix j = lane/8: rows (keys) +8*(j&1), dims +8*(j>>1)
+          const int mrow = half * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const uint32_t kaddr = smem_u32(kst + mrow * ROW_PITCH + kvh * HD * 2 + (lane >> 4) * 16);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(a0, a1, a2, a3, kaddr + ks * 32);
+            mma_16816(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+          }
+        }
+        // s[0]: key g head 2c, s[1]: key g head 2c+1, s[2]/s[3]: key g+8
+        const bool v0 = g < n_valid, v1 = g + 8 < n_valid;
+        float x0 = v0 ? s[0] * qk_scale : -CUDART_INF_F;
+        float x1 = v0 ? s[1] * qk_scale : -CUDART_INF_F;
+        float x2 = v1 ? s[2] * qk_scale : -CUDART_INF_F;
+        float x3 = v1 ? s[3] * qk_scale : -CUDART_INF_F;
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+        const float al0 = fast_exp2(m_run[0] - mn0), al1 = fast_exp2(m_run[1] - mn1);
+        m_run[0] = mn0;
+        m_run[1] = mn1;
+        const float p0 = fast_exp2(x0 - mn0), p1 = fast_exp2(x1 - mn1);
+        const float p2 = fast_exp2(x2 - mn0), p3 = fast_exp2(x3 - mn1);
+        l_run[0] = l_run[0] * al0 + (p0 + p2);
+        l_run[1] = l_run[1] * al1 + (p1 + p3);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          acc[mt][0] *= al0;
+          acc[mt][1] *= al1;
+          acc[mt][2] *= al0;
+          acc[mt][3] *= al1;
+        }
+        // P^T as the B operand (k = key, n = head): transpose the two 8x8 blocks
+        const uint32_t pb0 = movmatrix_t(pack_half2(p0, p1));
+        const uint32_t pb1 = movmatrix_t(pack_half2(p2, p3));
+
+        // ---- O^T[128 x 8] += V^T[128 x 16 keys] * P^T[16 keys x 8 heads]
+        {
+          // ldmatrix.x4.trans lanes: matrix j: keys +8*(j>>1), dims +8*(j&1)
+          const int vrow = half * 16 + (lane & 7) + (lane >> 4) * 8;
+          const uint32_t vaddr =
+              smem_u32(vst + vrow * ROW_PITCH + kvh * HD * 2 + ((lane >> 3) & 1) * 16);
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(a0, a1, a2, a3, vaddr + mt * 32);
+            mma_16816(acc[mt], a0, a1, a2, a3, pb0, pb1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[stage]);
+    }
+
+    // ---- merge the four warps of each KV group for this sequence
+    {
+      float l0 = l_run[0], l1 = l_run[1];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+      }
+      if (g == 0) {
+        merge_m[warp * GROUP + 2 * c] = m_run[0];
+        merge_m[warp * GROUP + 2 * c + 1] = m_run[1];
+        merge_l[warp * GROUP + 2 * c] = l0;
+        merge_l[warp * GROUP + 2 * c + 1] = l1;
+      }
+      float* ma = merge_acc + warp * GROUP * HD;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        ma[(2 * c) * HD + mt * 16 + g] = acc[mt][0];
+        ma[(2 * c + 1) * HD + mt * 16 + g] = acc[mt][1];
+        ma[(2 * c) * HD + mt * 16 + g + 8] = acc[mt][2];
+        ma[(2 * c + 1) * HD + mt * 16 + g + 8] = acc[mt][3];
+      }
+    }
+    named_bar_sync(1, CONSUMER_THREADS);
+
+    const bool whole = (s0 == tile_off[b]) && (s1 == tile_off[b + 1]);
+    const uint32_t slot = blockIdx.x + b;
+    // thread -> (query head, 8 dims)
+    const int hq = tid >> 4;               // 0..15
+    const int d0 = (tid & 15) * 8;
+    const int kg = hq >> 3, hig = hq & 7;
+    const int wsrc[4] = {2 * kg, 2 * kg + 1, 2 * kg + 4, 2 * kg + 5};
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) M = fmaxf(M, merge_m[wsrc[i] * GROUP + hig]);
+    float f[4], Lsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float mi = merge_m[wsrc[i] * GROUP + hig];
+      f[i] = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - M);
+      Lsum += merge_l[wsrc[i] * GROUP + hig] * f[i];
+    }
+    float A[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a += merge_acc[(wsrc[i] * GROUP + hig) * HD + d0 + e] * f[i];
+      A[e] = a;
+    }
+    if (whole) {
+      const float inv = 1.f / Lsum;
+      __align__(16) __half o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[e] * inv);
+      *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+          *reinterpret_cast<uint4*>(o);
+    } else {
+      float* rec = p.partials + (size_t)slot * PART_FLOATS;
+      *reinterpret_cast<float4*>(rec + hq * HD + d0) = make_float4(A[0], A[1], A[2], A[3]);
+      *reinterpret_cast<float4*>(rec + hq * HD + d0 + 4) = make_float4(A[4], A[5], A[6], A[7]);
+      if ((tid & 15) == 0) {
+        rec[QH * HD + hq] = M;
+        rec[QH * HD + QH + hq] = Lsum;
+      }
+      __threadfence();
+    }
+    named_bar_sync(1, CONSUMER_THREADS);
+    if (!whole) {
+      if (tid == 0) {
+        const uint32_t first = owner_cta(tile_off[b], G, NT);
+        const uint32_t last = owner_cta(tile_off[b + 1] - 1, G, NT);
+        const uint32_t prev = atomicAdd(p.tickets + b, 1u);
+        const bool mine = prev == last - first;
+        if (mine) {
+          __threadfence();
+          p.tickets[b] = 0;  // ready for the next launch
+        }
+        misc[1] = mine ? 1u : 0u;
+        misc[2] = first;
+        misc[3] = last;
+      }
+      named_bar_sync(1, CONSUMER_THREADS);
+      if (misc[1]) {
+        // combine every CTA's record of sequence b in CTA (= token) order
+        const uint32_t first = misc[2], last = misc[3];
+        float Mc = -CUDART_INF_F;
+        for (uint32_t i = first; i <= last; ++i)
+          Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
+        float Lc = 0.f, Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (uint32_t i = first; i <= last; ++i) {
+          const float* rec = p.partials + (size_t)(i + b) * PART_FLOATS;
+          const float mi = __ldcg(rec + QH * HD + hq);
+          const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
+          Lc += __ldcg(rec + QH * HD + QH + hq) * fi;
+          const float4 u = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0));
+          const float4 w = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0 + 4));
+          Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
+          Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
+        }
+        const float inv = 1.f / Lc;
+        __align__(16) __half o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * inv);
+        *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+            *reinterpret_cast<uint4*>(o);
+      }
+      named_bar_sync(1, CONSUMER_THREADS);
+    }
+
+    if (s1 >= t1) break;
+    ++b;
+    while (tile_off[b + 1] <= s1) ++b;  // skip sequences with no tiles
+  }
+}
+
+}  // namespace decode
+
+// ----------------------------------------------------------------- launcher
+size_t decode_workspace_bytes(uint32_t batch, int num_sms) {
+  const size_t header = 256;
+  const size_t tickets = ((size_t)batch * 4 + 255) / 256 * 256;
+  const size_t parts = ((size_t)num_sms + batch) * decode::PART_FLOATS * sizeof(float);
+  return header + tickets + parts;
+}
+
+int decode_launch(const DecodeArgs& a, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             decode::SMEM_BYTES) != cudaSuccess)
+      return PVLC_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  decode::Params p;
+  p.q = reinterpret_cast<const __half*>(a.q);
+  p.k_new = reinterpret_cast<const __half*>(a.k_new);
+  p.v_new = reinterpret_cast<const __half*>(a.v_new);
+  p.rope_cos = a.rope_cos;
+  p.rope_sin = a.rope_sin;
+  p.rope_row = a.rope_row;
+  p.k_cache = reinterpret_cast<__half* const*>(a.k_cache);
+  p.v_cache = reinterpret_cast<__half* const*>(a.v_cache);
+  p.cache_tokens = a.cache_tokens;
+  p.rope_rows = a.rope_rows;
+  p.capacity = a.capacity;
+  p.max_cache_tokens = a.max_cache_tokens;
+  p.batch = a.batch;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a.workspace);
+  p.flags = reinterpret_cast<uint32_t*>(ws);
+  p.tickets = reinterpret_cast<uint32_t*>(ws + 256);
+  p.partials = reinterpret_cast<float*>(ws + 256 + ((size_t)a.batch * 4 + 255) / 256 * 256);
+  p.out = reinterpret_cast<__half*>(a.out);
+  decode::decode_kernel<<<a.num_ctas, decode::THREADS, decode::SMEM_BYTES, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
+}
+
+}  // namespace pvlc

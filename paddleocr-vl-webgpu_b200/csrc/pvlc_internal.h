@@ -1,0 +1,74 @@
+// pvlc_internal.h -- launchers shared between the C ABI layer (pvlc_abi.cu)
+// and the kernel translation units.  Not installed; not part of the ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/pvlc_cuda_attn.h"
+
+namespace pvlc {
+
+struct DecodeArgs {
+  const pvlc_half* q;
+  const pvlc_half* k_new;
+  const pvlc_half* v_new;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint32_t rope_rows;
+  const uint32_t* rope_row;
+  pvlc_half* const* k_cache;
+  pvlc_half* const* v_cache;
+  const uint32_t* cache_tokens;
+  uint32_t capacity;
+  uint32_t max_cache_tokens;
+  uint32_t batch;
+  void* workspace;
+  pvlc_half* out;
+  int num_ctas;
+};
+size_t decode_workspace_bytes(uint32_t batch, int num_sms);
+int decode_launch(const DecodeArgs& a, cudaStream_t stream);
+
+// Varlen vision schedule: work items (segment, 128-row query tile) sorted by
+// decreasing segment length so the longest tiles start first.
+constexpr int kVisionMaxItems = 1024;
+struct VisionSchedule {
+  uint32_t n_items;
+  uint32_t item_seg_start[kVisionMaxItems];  // first token of the item's segment
+  uint32_t item_seg_len[kVisionMaxItems];
+  uint32_t item_q0[kVisionMaxItems];         // first query token of the item
+};
+struct VisionArgs {
+  const pvlc_half* q;
+  const pvlc_half* k;
+  const pvlc_half* v;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint32_t tokens;
+  uint32_t heads;
+  pvlc_half* out;
+};
+int vision_query_tile();
+int vision_launch(const VisionArgs& a, const uint32_t* cu_seqlens, uint32_t segments,
+                  cudaStream_t stream);
+
+struct PrefillArgs {
+  const pvlc_half* q;
+  const pvlc_half* k;
+  const pvlc_half* v;
+  const float* rope_cos;
+  const float* rope_sin;
+  uint32_t rope_rows;
+  uint32_t tokens;
+  pvlc_half* k_cache;
+  pvlc_half* v_cache;
+  pvlc_half* out;
+};
+int prefill_query_tile();
+int prefill_launch(const PrefillArgs& a, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace pvlc

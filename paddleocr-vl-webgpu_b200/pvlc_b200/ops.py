@@ -1,0 +1,133 @@
+"""Torch-facing wrappers over the C ABI (device tensors in, device tensors out).
+
+Each function checks tensor placement, dtype and shape, then calls the C
+entry point on the current CUDA stream; the library itself re-validates the
+geometry and returns the reference's error code before any device effect.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import abi
+
+QH, KVH, HD = 16, 2, 128
+VISION_HD = 72
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t, dtype, shape=None, name="tensor"):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+
+
+def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, out=None):
+    """Bidirectional block-diagonal attention over packed images with fused 2-D RoPE.
+
+    q, k, v: [T, H, 72] fp16 CUDA; cu_seqlens: host sequence of segment boundaries;
+    rope_cos/rope_sin: [T, 36] f32 CUDA tables or None.  Returns [T, H, 72] fp16.
+    """
+    T, H, D = q.shape
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need(t, torch.float16, (T, H, D), name)
+    if rope_cos is not None:
+        _need(rope_cos, torch.float32, (T, D // 2), "rope_cos")
+        _need(rope_sin, torch.float32, (T, D // 2), "rope_sin")
+    cu = np.ascontiguousarray(np.asarray(cu_seqlens, dtype=np.uint32))
+    if out is None:
+        out = torch.empty_like(q)
+    st = abi.lib().pvlc_attn_vision_varlen(
+        _ptr(q), _ptr(k), _ptr(v), cu.ctypes.data_as(ctypes.c_void_p), max(len(cu) - 1, 0), T, H,
+        D, _ptr(rope_cos), _ptr(rope_sin), _ptr(out), _stream())
+    abi.check(st, "pvlc_attn_vision_varlen")
+    return out
+
+
+def decoder_prefill(q, k, v, rope_cos, rope_sin, k_cache, v_cache, out=None):
+    """Causal GQA prefill of one decoder layer; writes rotated K / raw V into the caches.
+
+    q: [T,16,128] fp16; k, v: [T,2,128] fp16; rope tables [3, R, 128] f32 (R >= T);
+    k_cache, v_cache: [capacity, 2, 128] fp16.  Returns [T,16,128] fp16.
+    """
+    T = q.shape[0]
+    _need(q, torch.float16, (T, QH, HD), "q")
+    _need(k, torch.float16, (T, KVH, HD), "k")
+    _need(v, torch.float16, (T, KVH, HD), "v")
+    R = rope_cos.shape[1]
+    _need(rope_cos, torch.float32, (3, R, HD), "rope_cos")
+    _need(rope_sin, torch.float32, (3, R, HD), "rope_sin")
+    cap = k_cache.shape[0]
+    _need(k_cache, torch.float16, (cap, KVH, HD), "k_cache")
+    _need(v_cache, torch.float16, (cap, KVH, HD), "v_cache")
+    if out is None:
+        out = torch.empty_like(q)
+    st = abi.lib().pvlc_attn_decoder_prefill(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(rope_cos), _ptr(rope_sin), R, T, cap, _ptr(k_cache),
+        _ptr(v_cache), _ptr(out), _stream())
+    abi.check(st, "pvlc_attn_decoder_prefill")
+    return out
+
+
+class DecodeWorkspace:
+    """Device scratch for batched decode (split partials + combine tickets + fault flags)."""
+
+    def __init__(self, batch: int, device=None):
+        self.batch = int(batch)
+        self.nbytes = int(abi.lib().pvlc_attn_decode_workspace_bytes(self.batch))
+        self.buffer = torch.empty(self.nbytes, dtype=torch.uint8,
+                                  device=device or torch.device("cuda"))
+        abi.check(abi.lib().pvlc_attn_decode_workspace_init(_ptr(self.buffer), self.nbytes,
+                                                            _stream()),
+                  "pvlc_attn_decode_workspace_init")
+
+    def errors(self) -> int:
+        flags = ctypes.c_uint32(0)
+        abi.lib().pvlc_attn_decode_errors(_ptr(self.buffer), ctypes.byref(flags), _stream())
+        return int(flags.value)
+
+
+def decode(q, k_new, v_new, rope_cos, rope_sin, k_cache_ptrs, v_cache_ptrs, cache_tokens,
+           capacity: int, max_cache_tokens: int, workspace: DecodeWorkspace, rope_row=None,
+           out=None):
+    """Batched single-token decode with fused M-RoPE and KV append.
+
+    q: [B,16,128] fp16; k_new/v_new: [B,2,128] fp16; rope tables [3, R, 128] f32;
+    k_cache_ptrs/v_cache_ptrs: int64 CUDA tensors of B device pointers to
+    [capacity, 2, 128] fp16 caches; cache_tokens: int32 CUDA [B] rows before the append;
+    rope_row: optional int32 CUDA [B] (defaults to cache_tokens).  Returns [B,16,128] fp16.
+    """
+    B = q.shape[0]
+    _need(q, torch.float16, (B, QH, HD), "q")
+    _need(k_new, torch.float16, (B, KVH, HD), "k_new")
+    _need(v_new, torch.float16, (B, KVH, HD), "v_new")
+    R = rope_cos.shape[1]
+    _need(rope_cos, torch.float32, (3, R, HD), "rope_cos")
+    _need(rope_sin, torch.float32, (3, R, HD), "rope_sin")
+    _need(k_cache_ptrs, torch.int64, (B,), "k_cache_ptrs")
+    _need(v_cache_ptrs, torch.int64, (B,), "v_cache_ptrs")
+    _need(cache_tokens, torch.int32, (B,), "cache_tokens")
+    if rope_row is not None:
+        _need(rope_row, torch.int32, (B,), "rope_row")
+    if out is None:
+        out = torch.empty_like(q)
+    st = abi.lib().pvlc_attn_decode(
+        _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(rope_cos), _ptr(rope_sin), R, _ptr(rope_row),
+        _ptr(k_cache_ptrs), _ptr(v_cache_ptrs), _ptr(cache_tokens), int(capacity),
+        int(max_cache_tokens), B, _ptr(workspace.buffer), workspace.nbytes, _ptr(out), _stream())
+    abi.check(st, "pvlc_attn_decode")
+    return out

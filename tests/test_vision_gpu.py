@@ -1,0 +1,122 @@
+"""Vision varlen attention parity: CUDA kernel (C ABI) vs the CPU oracle.
+
+Oracle: vision_rope_2d table form (crates/pvlc-wgsl/src/lib.rs:1691-1730) then
+materialized_segmented_attention_f32 (crates/pvlc-cpu-ref/src/lib.rs:2752-2802).
+Inputs are fp16-representable; tolerance max-abs <= 2e-3 on fp16 outputs
+(north-star), which is looser than the reference's f32-vs-f32 native policy
+(3e-4, crates/pvlc-testkit/src/m3_vision_attention.rs:13-21) by the fp16 output
+rounding and fp16 P/V operands.
+"""
+import numpy as np
+import pytest
+import torch
+
+import pvlc_oracle as O
+from test_oracle_kat import m3_case
+
+pytestmark = pytest.mark.gpu
+H, D = 16, 72
+ATOL = 2e-3
+
+
+def _gpu(q, k, v, cu, cos=None, sin=None):
+    from pvlc_b200 import ops
+    dev = torch.device("cuda")
+    T = q.shape[0]
+    tq = torch.from_numpy(q.astype(np.float16).reshape(T, H, D)).to(dev)
+    tk = torch.from_numpy(k.astype(np.float16).reshape(T, H, D)).to(dev)
+    tv = torch.from_numpy(v.astype(np.float16).reshape(T, H, D)).to(dev)
+    tc = torch.from_numpy(cos).to(dev) if cos is not None else None
+    ts = torch.from_numpy(sin).to(dev) if sin is not None else None
+    out = ops.vision_varlen_attention(tq, tk, tv, cu, tc, ts)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+M3_CASES = [(n, [0, n], 101 + i, None) for i, n in enumerate([8, 16, 31, 64, 127, 256])] + [
+    (31, [0, 3, 11, 31], 201, None), (17, [0, 3, 9, 17], 301, None),
+    (17, [0, 3, 9, 17], 301, 0), (17, [0, 3, 9, 17], 301, 1), (17, [0, 3, 9, 17], 301, 2)]
+
+
+@pytest.mark.parametrize("tokens,cu,seed,poison", M3_CASES)
+def test_m3_corpus(cuda_lib, tokens, cu, seed, poison):
+    """The reference's 11-case M3 vision attention corpus (no RoPE)."""
+    q, k, v = m3_case(tokens, cu, seed, poison)
+    ref = O.segmented_attention(q, k, v, tokens, H, D, cu).reshape(tokens, H, D)
+    got = _gpu(q, k, v, cu)
+    err = np.abs(got - ref).max()
+    # poisoned segments hold values up to ~130 in V: scale the bound by the value range
+    scale = max(1.0, float(np.abs(v).max()) / 2.0)
+    assert err <= ATOL * scale, f"max abs err {err}"
+
+
+def test_poisoned_segment_does_not_leak(cuda_lib):
+    cu = [0, 3, 9, 17]
+    q, k, v = m3_case(17, cu, 301)
+    base = _gpu(q, k, v, cu)
+    for seg in range(3):
+        qp, kp, vp = m3_case(17, cu, 301, seg)
+        got = _gpu(qp, kp, vp, cu)
+        for s2 in range(3):
+            rows = slice(cu[s2], cu[s2 + 1])
+            if s2 != seg:
+                np.testing.assert_array_equal(got[rows], base[rows])
+
+
+@pytest.mark.parametrize("grids", [
+    [(1, 4, 4)],
+    [(1, 8, 8), (1, 6, 10), (1, 2, 2)],
+    [(1, 12, 16), (1, 9, 7), (1, 16, 12)],
+])
+def test_packed_images_with_rope(cuda_lib, grids):
+    from pvlc_b200 import positions
+    rng = np.random.default_rng(len(grids))
+    lens = [t * h * w for t, h, w in grids]
+    cu = np.concatenate([[0], np.cumsum(lens)]).tolist()
+    T = cu[-1]
+    q = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    cos, sin = positions.vision_rope_tables(grids)
+    ocos, osin = O.vision_rope_tables(grids)
+    np.testing.assert_allclose(cos, ocos, atol=1e-7, rtol=0)
+    qr, kr = O.vision_rope_apply_tables(q, k, T, H, D, ocos, osin)
+    ref = O.segmented_attention(qr, kr, v, T, H, D, cu).reshape(T, H, D)
+    got = _gpu(q, k, v, cu, cos, sin)
+    err = np.abs(got - ref).max()
+    assert err <= ATOL, f"max abs err {err}"
+
+
+def test_config2_shape_sampled(cuda_lib):
+    """BASELINE config 2 geometry (8000 tokens, segments 1024/2304/576/4096) with RoPE;
+    the oracle checks every row of the two shorter images and a strided row sample."""
+    from pvlc_b200 import positions
+    grids = [(1, 32, 32), (1, 48, 48), (1, 24, 24), (1, 64, 64)]
+    cu = [0, 1024, 3328, 3904, 8000]
+    T = 8000
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    cos, sin = positions.vision_rope_tables(grids)
+    got = _gpu(q, k, v, cu, cos, sin)
+    assert np.isfinite(got).all()
+    qr, kr = O.vision_rope_apply_tables(q, k, T, H, D, cos, sin)
+    for s in (0, 2):
+        a, b = cu[s], cu[s + 1]
+        ref = O.segmented_attention(qr[a:b], kr[a:b], v[a:b], b - a, H, D, [0, b - a])
+        err = np.abs(got[a:b] - ref.reshape(b - a, H, D)).max()
+        assert err <= ATOL, f"segment {s} err {err}"
+
+
+def test_vision_validation_errors(cuda_lib):
+    from pvlc_b200 import abi
+    T = 8
+    z = torch.zeros((T, H, D), dtype=torch.float16, device="cuda")
+    from pvlc_b200 import ops
+    for cu, code in (([0, 4, 4, 8], abi.INVALID_SEQUENCE_BOUNDARIES),
+                     ([1, 8], abi.INVALID_SEQUENCE_BOUNDARIES),
+                     ([0, 7], abi.INVALID_SEQUENCE_BOUNDARIES)):
+        with pytest.raises(abi.PvlcError) as e:
+            ops.vision_varlen_attention(z, z, z, cu)
+        assert e.value.status == code
