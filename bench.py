@@ -124,7 +124,7 @@ def run_gpu(args, rank, world, local_rank, dist):
     rng = np.random.default_rng(1 + rank)
     L0 = rng.integers(L_MIN, L_MAX + 1, size=SEQS_PER_GPU).astype(np.int64)
     steps, warm = args.steps, args.warmup
-    cap = int(L0.max()) + warm + steps + 8
+    cap = int(L0.max()) + warm + 2 * steps + 8   # timed steps + e2e steps
     B = SEQS_PER_GPU
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
@@ -404,6 +404,7 @@ def run_reference(args, rank):
 
 
 def main():
+    global LAYERS, SEQS_PER_GPU, METRIC
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
@@ -414,8 +415,14 @@ def main():
     ap.add_argument("--skip-components", action="store_true")
     ap.add_argument("--traffic-bytes", type=float, default=None,
                     help="ncu dram bytes per decode launch, when measured")
+    ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
+                    help="sequences per GPU (profiling runs use a smaller case)")
+    ap.add_argument("--layers", type=int, default=LAYERS)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.seqs != SEQS_PER_GPU or args.layers != LAYERS:
+        METRIC = f"decode-attn HBM GB/s ({args.seqs} seqs x {args.layers} layers, reduced case)"
+    LAYERS, SEQS_PER_GPU = args.layers, args.seqs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

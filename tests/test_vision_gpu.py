@@ -22,7 +22,7 @@ ATOL = 2e-3
 def _gpu(q, k, v, cu, cos=None, sin=None):
     from pvlc_b200 import ops
     dev = torch.device("cuda")
-    T = q.shape[0]
+    T = q.size // (H * D)
     tq = torch.from_numpy(q.astype(np.float16).reshape(T, H, D)).to(dev)
     tk = torch.from_numpy(k.astype(np.float16).reshape(T, H, D)).to(dev)
     tv = torch.from_numpy(v.astype(np.float16).reshape(T, H, D)).to(dev)
@@ -42,6 +42,8 @@ M3_CASES = [(n, [0, n], 101 + i, None) for i, n in enumerate([8, 16, 31, 64, 127
 def test_m3_corpus(cuda_lib, tokens, cu, seed, poison):
     """The reference's 11-case M3 vision attention corpus (no RoPE)."""
     q, k, v = m3_case(tokens, cu, seed, poison)
+    # the kernel consumes fp16: give the oracle the same (fp16-rounded) operands
+    q, k, v = (x.astype(np.float16).astype(np.float32) for x in (q, k, v))
     ref = O.segmented_attention(q, k, v, tokens, H, D, cu).reshape(tokens, H, D)
     got = _gpu(q, k, v, cu)
     err = np.abs(got - ref).max()
