@@ -162,6 +162,34 @@ int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half
  * PVLC_OK when no flag was set, PVLC_DEVICE_FAULT_FLAG otherwise. */
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
 
+/* Allocation-free variant of pvlc_attn_decode.  It has no counterpart in the
+ * reference.  It serves callers that can pass input and output buffers but
+ * cannot allocate device memory -- a host whose device memory is planned once
+ * by a static arena, or a foreign-language binding with no handle on a CUDA
+ * allocator -- so it takes no workspace: its scratch is a fixed file-scope
+ * device array of PVLC_DECODE_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * this library holds until the process exits.  Same arguments and results as
+ * pvlc_attn_decode otherwise.
+ *   - batch may not exceed PVLC_DECODE_NOALLOC_MAX_BATCH; a larger batch (or a
+ *     device whose SM count needs more scratch) returns
+ *     PVLC_WORKSPACE_TOO_SMALL before any device effect.
+ *   - The first call on each device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - The call makes no cudaMalloc/cudaFree or other allocation; it clears the
+ *     array's flag and ticket words on `stream` before the kernel.
+ *   - All calls share the one array: calls that may overlap on the GPU (other
+ *     streams, other threads) race and must be serialised by the caller.
+ *   - Device-side fault flags of this variant are not readable; use
+ *     pvlc_attn_decode when they are needed. */
+#define PVLC_DECODE_NOALLOC_MAX_BATCH 256u
+#define PVLC_DECODE_NOALLOC_SCRATCH_BYTES (4u << 20)
+int pvlc_attn_decode_noalloc(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half* v_new,
+                             const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                             const uint32_t* rope_row, pvlc_half* const* k_cache,
+                             pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                             uint32_t cache_capacity, uint32_t max_cache_tokens, uint32_t batch,
+                             pvlc_half* out, void* stream);
+
 /* ----------------------------------------------------------------------------
  * Plans: the host-side half of the contract, callable without a GPU.
  * They run the same validation as the launch entry points and report the

@@ -34,6 +34,8 @@
 #include <math_constants.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "pvlc_common.cuh"
 #include "pvlc_internal.h"
 
@@ -547,4 +549,80 @@ int decode_launch(const DecodeArgs& a, cudaStream_t stream) {
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 
+// ------------------------------------------------ allocation-free decode
+// Some callers can hand us input and output buffers but cannot allocate device
+// memory themselves: a host whose device memory is planned once up front by a
+// static arena, or a foreign-language binding with no handle on a CUDA
+// allocator.  For them the split-KV scratch (fault flags, combine tickets and
+// per-CTA partial records) lives in this fixed file-scope device array instead
+// of a caller workspace.  Every GPU that loads this library holds the array
+// (PVLC_DECODE_NOALLOC_SCRATCH_BYTES) until the process exits.
+namespace {
+
+__device__ __align__(256) uint8_t g_decode_noalloc_scratch[PVLC_DECODE_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  In host code
+// `g_decode_noalloc_scratch` names a host-side stand-in, never the device
+// memory, so the address is looked up once per device (with that device
+// current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PVLC_CUDA_ERROR;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+      return PVLC_CUDA_ERROR;
+    g_noalloc_scratch_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return PVLC_OK;
+}
+
+bool aligned16_ptr(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
 }  // namespace pvlc
+
+extern "C" int pvlc_attn_decode_noalloc(const pvlc_half* q, const pvlc_half* k_new,
+                                        const pvlc_half* v_new, const float* rope_cos,
+                                        const float* rope_sin, uint32_t rope_rows,
+                                        const uint32_t* rope_row, pvlc_half* const* k_cache,
+                                        pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                                        uint32_t cache_capacity, uint32_t max_cache_tokens,
+                                        uint32_t batch, pvlc_half* out, void* stream) {
+  using namespace pvlc;
+  // same host-side checks and precedence as pvlc_attn_decode
+  if (batch == 0 || cache_capacity == 0 || rope_rows == 0) return PVLC_ZERO_DIMENSION;
+  if (batch > PVLC_DECODE_MAX_BATCH) return PVLC_INVALID_DECODER_GEOMETRY;
+  if (max_cache_tokens >= cache_capacity) return PVLC_CAPACITY_EXHAUSTED;
+  if ((uint64_t)cache_capacity * 512ull > (1ull << 40)) return PVLC_ARITHMETIC_OVERFLOW;
+  if (!q || !k_new || !v_new || !rope_cos || !rope_sin || !k_cache || !v_cache || !cache_tokens ||
+      !out)
+    return PVLC_NULL_POINTER;
+  if (!aligned16_ptr(q) || !aligned16_ptr(k_new) || !aligned16_ptr(v_new) || !aligned16_ptr(out) ||
+      !aligned16_ptr(rope_cos) || !aligned16_ptr(rope_sin))
+    return PVLC_MISALIGNED_POINTER;
+  // the fixed scratch bounds the batch
+  if (batch > PVLC_DECODE_NOALLOC_MAX_BATCH) return PVLC_WORKSPACE_TOO_SMALL;
+  const int sms = device_sm_count();
+  if (sms <= 0) return PVLC_CUDA_ERROR;
+  const size_t need = decode_workspace_bytes(batch, sms);
+  if (need > PVLC_DECODE_NOALLOC_SCRATCH_BYTES) return PVLC_WORKSPACE_TOO_SMALL;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st != PVLC_OK) return st;
+  // The array keeps the previous call's contents: the fault flags and the
+  // combine tickets must start at zero (the partial records need not).
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t zero_bytes = 256 + ((size_t)batch * 4 + 255) / 256 * 256;
+  if (cudaMemsetAsync(scratch, 0, zero_bytes, s) != cudaSuccess) return PVLC_CUDA_ERROR;
+  DecodeArgs a{q,       k_new,    v_new,   rope_cos,     rope_sin,       rope_rows,
+               rope_row, k_cache, v_cache, cache_tokens, cache_capacity, max_cache_tokens,
+               batch,   scratch,  out,     sms};
+  return decode_launch(a, s);
+}
