@@ -1,0 +1,459 @@
+// vision_tc.cu -- vision-encoder bidirectional varlen attention on the
+// Blackwell tensor cores (tcgen05 + TMEM + TMA), head_dim 72, with the 2-D
+// RoPE fused into the Q/K tiles.  sm_100a.
+//
+// Reference path replaced: VisionRope2dF16 followed by VisionAttentionF16
+// (crates/pvlc-wgsl/src/lib.rs:2309-2454,2553-2596; call site
+// crates/pvlc-runtime-web/src/web.rs:4797-4803); arithmetic
+// crates/pvlc-cpu-ref/src/lib.rs:472-542 (rotation) and :2752-2878
+// (segmented attention).  A CTA only visits keys of its own segment.
+//
+// One CTA = one (segment, 128-query tile, head) work item, two CTAs per SM.
+// head_dim 72 is split into a 64-dim block (128-byte rows, 128B swizzle) and
+// a 16-dim block (32-byte rows, 32B swizzle; TMA zero-fills dims 72..79 as
+// out of bounds), so every MMA has K = 16 and no shape is padded in HBM.
+//
+//   warp 8      TMA producer: Q once, then K/V tiles of 128 keys, 2 stages
+//   warps 0-3   rotation: thread r rotates key row r of the staged K tile in
+//               place (2-D RoPE from the [T,36] tables), then releases it
+//   warps 4-7   softmax: thread i owns query row i = TMEM lane i; rotates
+//               its Q row once; per tile reads S from TMEM, online softmax
+//               in f32 (exp2 domain), rescales O in TMEM when the row max
+//               moves, writes P (fp16) over S, and finally normalises O
+//   warp 9      MMA issuer (one thread): S = Q K^T (4 x K16 from the 64-dim
+//               block + 1 x K16 from the 16-dim block, M128 N128) and
+//               O += P V with P read from TMEM (8 x K16 steps, N64 + N16)
+// TMEM: S/P at columns [0,128), O at [128,208) of a 256-column allocation.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+#include <numeric>
+#include <vector>
+
+#include "pvlc_common.cuh"
+#include "pvlc_internal.h"
+#include "tcgen05.cuh"
+
+namespace pvlc {
+namespace vtc {
+
+constexpr int HD = 72;
+constexpr int PAIRS = 36;
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int THREADS = 320;
+constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr uint32_t SZ_B0 = 128 * 128;   // 128 rows x 64 dims fp16, 128B swizzle
+constexpr uint32_t SZ_B1 = 128 * 32;    // 128 rows x 16 dims fp16, 32B swizzle
+constexpr uint32_t OFF_Q0 = 0;
+constexpr uint32_t OFF_Q1 = OFF_Q0 + SZ_B0;
+constexpr uint32_t OFF_STAGE = OFF_Q1 + SZ_B1;
+constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_B0, ST_V0 = SZ_B0 + SZ_B1, ST_V1 = 2 * SZ_B0 + SZ_B1;
+constexpr uint32_t STAGE_BYTES = 2 * (SZ_B0 + SZ_B1);
+constexpr int STAGES = 2;
+constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
+// barriers: q_full, q_ready, s_full, p_full, o_done, kv_full[2], k_rot[2], kv_empty[2]
+constexpr int NBARS = 11;
+constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TCOL_S = 0;
+constexpr uint32_t TCOL_O = 128;
+
+struct Sched {
+  uint32_t n_segments;
+  uint32_t seg_start[MAX_SEG];
+  uint32_t seg_len[MAX_SEG];
+  uint32_t item_prefix[MAX_SEG + 1];
+};
+
+struct Maps {
+  CUtensorMap q0, q1, k0, k1, v0, v1;
+};
+
+struct Params {
+  const float* rope_cos;  // [T, 36] or null
+  const float* rope_sin;
+  __half* out;
+  uint32_t heads;
+  uint32_t tokens;
+};
+
+// Rotate one 72-dim row held in a (64-dim SW128, 16-dim SW32) pair of tiles,
+// in place.  Pair p rotates dims (p, p + 36) by table entry p.
+__device__ __forceinline__ void rotate_row(uint8_t* b0, uint8_t* b1, int r, const float* cs,
+                                           const float* sn) {
+  // w[k] holds dims (2k, 2k+1) as a half2; dims 72..79 of the row are padding
+  uint32_t w[36];
+#pragma unroll
+  for (int c = 0; c < 9; ++c) {
+    const uint8_t* src = c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4)
+                               : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
+  }
+#pragma unroll
+  for (int j = 0; j < PAIRS / 4; ++j) {   // pairs 4j..4j+3: words 2j,2j+1 and 18+2j,18+2j+1
+    const float4 c = __ldg(reinterpret_cast<const float4*>(cs) + j);
+    const float4 s = __ldg(reinterpret_cast<const float4*>(sn) + j);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float c0 = e ? c.z : c.x, c1 = e ? c.w : c.y;
+      const float s0 = e ? s.z : s.x, s1 = e ? s.w : s.y;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * j + e]));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[18 + 2 * j + e]));
+      w[2 * j + e] = pack_half2(a.x * c0 - b.x * s0, a.y * c1 - b.y * s1);
+      w[18 + 2 * j + e] = pack_half2(b.x * c0 + a.x * s0, b.y * c1 + a.y * s1);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 9; ++c) {
+    uint8_t* dst = c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4)
+                         : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 2)
+    vision_tc_kernel(const __grid_constant__ Maps maps, const Params p, const Sched sc) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* s_full = bars + 2;
+  uint64_t* p_full = bars + 3;
+  uint64_t* o_done = bars + 4;
+  uint64_t* kv_full = bars + 5;    // [2]
+  uint64_t* k_rot = bars + 7;      // [2]
+  uint64_t* kv_empty = bars + 9;   // [2]
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
+  // misc[0]: TMEM base, misc[1]: abort
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t head = blockIdx.x;
+  const uint32_t item = blockIdx.y;
+  uint32_t sg = 0;
+  while (sg + 1 < sc.n_segments && sc.item_prefix[sg + 1] <= item) ++sg;
+  const uint32_t seg0 = sc.seg_start[sg], seglen = sc.seg_len[sg];
+  const uint32_t q0 = seg0 + (item - sc.item_prefix[sg]) * BM;
+  const int nk = static_cast<int>((seglen + BN - 1) / BN);
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 4);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&k_rot[s], 4);
+      mbar_init(&kv_empty[s], 1);
+    }
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = misc[0];
+
+  if (warp == 8) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tc::tma_prefetch_desc(&maps.q0);
+      tc::tma_prefetch_desc(&maps.k0);
+      tc::tma_prefetch_desc(&maps.v0);
+      mbar_arrive_expect_tx(q_full, SZ_B0 + SZ_B1);
+      tc::tma_load_3d(smem + OFF_Q0, &maps.q0, 0, head, q0, q_full);
+      tc::tma_load_3d(smem + OFF_Q1, &maps.q1, 64, head, q0, q_full);
+      for (int j = 0; j < nk; ++j) {
+        const int s = j & 1;
+        const uint32_t use = j >> 1;
+        if (misc[1] || !mbar_wait(&kv_empty[s], (use & 1) ^ 1)) { misc[1] = 1; break; }
+        uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+        const int z = seg0 + j * BN;
+        mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
+        tc::tma_load_3d(st + ST_K0, &maps.k0, 0, head, z, &kv_full[s]);
+        tc::tma_load_3d(st + ST_K1, &maps.k1, 64, head, z, &kv_full[s]);
+        tc::tma_load_3d(st + ST_V0, &maps.v0, 0, head, z, &kv_full[s]);
+        tc::tma_load_3d(st + ST_V1, &maps.v1, 64, head, z, &kv_full[s]);
+      }
+      // drain: the last loads must land before the CTA may exit
+      for (int j = (nk > 2 ? nk - 2 : 0); j < nk; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------ K rotation
+    const int r = tid;  // key row of the tile
+    for (int j = 0; j < nk; ++j) {
+      const int s = j & 1;
+      if (misc[1] || !mbar_wait(&kv_full[s], (j >> 1) & 1)) { misc[1] = 1; break; }
+      uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+      const uint32_t key = j * BN + r;
+      if (p.rope_cos && key < seglen) {
+        const size_t t = seg0 + key;
+        rotate_row(st + ST_K0, st + ST_K1, r, p.rope_cos + t * PAIRS, p.rope_sin + t * PAIRS);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&k_rot[s]);
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------ softmax
+    const int i = tid - 128;            // query row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + TCOL_S;
+    const uint32_t tO = tmem + lane_base + TCOL_O;
+    bool ok = mbar_wait(q_full, 0);
+    if (ok && p.rope_cos && q0 + i < p.tokens) {
+      const size_t t = q0 + i;
+      rotate_row(smem + OFF_Q0, smem + OFF_Q1, i, p.rope_cos + t * PAIRS, p.rope_sin + t * PAIRS);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
+    if (!ok) misc[1] = 1;
+
+    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+    float m_run = -CUDART_INF_F, l_run = 0.f;
+    bool good = __all_sync(0xffffffffu, ok);
+    for (int j = 0; j < nk && good; ++j) {
+      // every lane of the warp takes the same path through the collective
+      // tcgen05.ld / tcgen05.st below
+      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(s_full, j & 1))) { good = false; break; }
+      tc::fence_after_sync();
+      const int kv = static_cast<int>(umin32(BN, seglen - j * BN));
+      // pass 1: row max of the scaled scores (32-column TMEM chunks)
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sv[32];
+        tc::tmem_ld32(tS + ch * 32, sv);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (ch * 32 + c < kv) mx = fmaxf(mx, __uint_as_float(sv[c]) * scale);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = fast_exp2(m_run - m_new);   // 0 on the first tile
+      if (j > 0) {
+        // O is complete for tiles < j; rescale it in TMEM when a row max moved
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1))) { good = false; break; }
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int cc = 0; cc < 80; cc += 16) {
+            uint32_t ov[16];
+            tc::tmem_ld16(tO + cc, ov);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tc::tmem_st16(tO + cc, ov);
+          }
+        }
+      }
+      // pass 2: P = exp2(x - m) as fp16 pairs over the first 64 columns of S;
+      // P chunk c lands in S columns already read (16c < 32(c+1))
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sv[32];
+        tc::tmem_ld32(tS + ch * 32, sv);
+        tc::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int k0 = ch * 32 + 2 * c;
+          const float a = k0 < kv ? fast_exp2(__uint_as_float(sv[2 * c]) * scale - m_new) : 0.f;
+          const float b = k0 + 1 < kv ? fast_exp2(__uint_as_float(sv[2 * c + 1]) * scale - m_new) : 0.f;
+          rs += a + b;
+          pk[c] = pack_half2(a, b);
+        }
+        tc::tmem_st16(tS + ch * 16, pk);
+      }
+      tc::tmem_wait_st();
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!good) misc[1] = 1;
+    // epilogue: O / l -> fp16 rows
+    if (__all_sync(0xffffffffu, good && mbar_wait(o_done, (nk - 1) & 1))) {
+      tc::fence_after_sync();
+      const bool store = q0 + i < seg0 + seglen;
+      const float inv = 1.f / l_run;
+      __half* orow = p.out + ((size_t)(q0 + i) * p.heads + head) * HD;
+#pragma unroll
+      for (int cc = 0; cc < 80; cc += 16) {
+        uint32_t ov[16];
+        tc::tmem_ld16(tO + cc, ov);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (cc + 8 * h >= HD) break;   // columns 72..79 are padding
+          uint4 v;
+          v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
+          v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
+          v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
+          v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
+          if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
+        }
+      }
+    } else {
+      misc[1] = 1;
+    }
+  } else {
+    // ------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
+      const uint32_t idesc_pv0 = tc::idesc_f16(128, 64, 0, 1);
+      const uint32_t idesc_pv1 = tc::idesc_f16(128, 16, 0, 1);
+      const uint32_t sq0 = smem_u32(smem + OFF_Q0), sq1 = smem_u32(smem + OFF_Q1);
+      const uint32_t tS = tmem + TCOL_S, tO = tmem + TCOL_O;
+      bool ok = mbar_wait(q_ready, 0);
+      tc::fence_after_sync();
+      int issued = 0;
+      for (int j = 0; j < nk && ok && !misc[1]; ++j) {
+        const int s = j & 1;
+        const uint32_t st = smem_u32(smem + OFF_STAGE + s * STAGE_BYTES);
+        if (!mbar_wait(&k_rot[s], (j >> 1) & 1)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(o_done, (j - 1) & 1)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_ss(tS, tc::smem_desc(sq0 + ks * 32, 16, 1024, tc::kSw128),
+                     tc::smem_desc(st + ST_K0 + ks * 32, 16, 1024, tc::kSw128), idesc_qk, ks > 0);
+        tc::mma_ss(tS, tc::smem_desc(sq1, 16, 256, tc::kSw32),
+                   tc::smem_desc(st + ST_K1, 16, 256, tc::kSw32), idesc_qk, 1);
+        tc::commit(s_full);
+        if (!mbar_wait(p_full, j & 1)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+          tc::mma_ts(tO, tS + ks * 8, tc::smem_desc(st + ST_V0 + ks * 2048, 16, 1024, tc::kSw128),
+                     idesc_pv0, acc);
+          tc::mma_ts(tO + 64, tS + ks * 8, tc::smem_desc(st + ST_V1 + ks * 512, 16, 256, tc::kSw32),
+                     idesc_pv1, acc);
+        }
+        tc::commit(o_done);
+        tc::commit(&kv_empty[s]);
+        issued = j + 1;
+      }
+      if (!ok) misc[1] = 1;
+      // never exit with MMAs in flight or commit arrivals still pending
+      if (issued > 0) mbar_wait(o_done, (issued - 1) & 1);
+      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+        mbar_wait(&kv_empty[j & 1], (j >> 1) & 1);
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 8) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------- host side
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// [tokens, heads, 72] fp16 viewed as a 3-D tensor {72, heads, tokens}; box
+// {inner, 1, 128} rows of one head.
+bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads, uint32_t inner,
+              CUtensorMapSwizzle sw) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {HD, heads, tokens};
+  const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)heads * HD * 2};
+  const cuuint32_t box[3] = {inner, 1, 128};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace vtc
+
+int vision_query_tile() { return vtc::BM; }
+
+int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
+                  cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(vtc::vision_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             vtc::SMEM_BYTES) != cudaSuccess)
+      return PVLC_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  vtc::Maps maps;
+  const bool ok = vtc::make_map(&maps.q0, a.q, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  vtc::make_map(&maps.q1, a.q, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
+                  vtc::make_map(&maps.k0, a.k, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  vtc::make_map(&maps.k1, a.k, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
+                  vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  vtc::make_map(&maps.v1, a.v, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (!ok) return PVLC_CUDA_ERROR;
+  vtc::Sched sc;
+  std::vector<uint32_t> order(segments);
+  std::iota(order.begin(), order.end(), 0u);
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t x, uint32_t y) {
+    return (cu[x + 1] - cu[x]) > (cu[y + 1] - cu[y]);
+  });
+  sc.n_segments = segments;
+  uint32_t items = 0;
+  for (uint32_t i = 0; i < segments; ++i) {
+    const uint32_t s = order[i];
+    sc.seg_start[i] = cu[s];
+    sc.seg_len[i] = cu[s + 1] - cu[s];
+    sc.item_prefix[i] = items;
+    items += (sc.seg_len[i] + vtc::BM - 1) / vtc::BM;
+  }
+  sc.item_prefix[segments] = items;
+  if (items > 65535u) return PVLC_INVALID_VISION_GEOMETRY;
+  vtc::Params p;
+  p.rope_cos = a.rope_cos;
+  p.rope_sin = a.rope_sin;
+  p.out = reinterpret_cast<__half*>(a.out);
+  p.heads = a.heads;
+  p.tokens = a.tokens;
+  dim3 grid(a.heads, items);
+  vtc::vision_tc_kernel<<<grid, vtc::THREADS, vtc::SMEM_BYTES, stream>>>(maps, p, sc);
+  return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
+}
+
+}  // namespace pvlc

@@ -258,9 +258,7 @@ __global__ void __launch_bounds__(THREADS) vision_mma_kernel(const Params p, con
 
 }  // namespace vision
 
-int vision_query_tile() { return vision::BM; }
-
-int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
+int vision_mma_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
                   cudaStream_t stream) {
   vision::Sched sc;
   std::vector<uint32_t> order(segments);
