@@ -8,22 +8,29 @@
 // crates/pvlc-cpu-ref/src/lib.rs:472-542 (rotation) and :2752-2878
 // (segmented attention).  A CTA only visits keys of its own segment.
 //
-// One CTA = one (segment, 128-query tile, head) work item, two CTAs per SM.
-// head_dim 72 is split into a 64-dim block (128-byte rows, 128B swizzle) and
-// a 16-dim block (32-byte rows, 32B swizzle; TMA zero-fills dims 72..79 as
-// out of bounds), so every MMA has K = 16 and no shape is padded in HBM.
+// One CTA = one (segment, 256-query pair of tiles, head) work item, one CTA
+// per SM.  head_dim 72 is split into a 64-dim block (128-byte rows, 128B
+// swizzle) and a 16-dim block (32-byte rows, 32B swizzle; TMA zero-fills dims
+// 72..79 as out of bounds), so every MMA has K = 16 and nothing is padded in HBM.
 //
-//   warp 8      TMA producer: Q once, then K/V tiles of 128 keys, 2 stages
-//   warps 0-3   rotation: thread r rotates key row r of the staged K tile in
-//               place (2-D RoPE from the [T,36] tables), then releases it
-//   warps 4-7   softmax: thread i owns query row i = TMEM lane i; rotates
-//               its Q row once; per tile reads S from TMEM, online softmax
-//               in f32 (exp2 domain), rescales O in TMEM when the row max
-//               moves, writes P (fp16) over S, and finally normalises O
-//   warp 9      MMA issuer (one thread): S = Q K^T (4 x K16 from the 64-dim
-//               block + 1 x K16 from the 16-dim block, M128 N128) and
-//               O += P V with P read from TMEM (8 x K16 steps, N64 + N16)
-// TMEM: S/P at columns [0,128), O at [128,208) of a 256-column allocation.
+//   warp 12      TMA producer: both Q tiles once, then K/V tiles of 128 keys
+//                through a 3-stage ring
+//   warps 0-3    rotation: thread r rotates key row r of a staged K tile in
+//                place (2-D RoPE from the [T,36] tables); one rotation serves
+//                both Q tiles
+//   warps 4-7,   softmax for Q tile 0 / Q tile 1: thread i owns query row i =
+//   warps 8-11   TMEM lane i; rotates its Q row once; per K tile reads S from
+//                TMEM, online softmax in f32 (exp2 domain), writes P (fp16)
+//                over S; the running max is only moved (and O rescaled in
+//                TMEM) when a row max grows by more than 8 (log2 units), so P
+//                stays <= 256 and the rescale is off the common path
+//   warp 13      MMA issuer (one thread), ping-pong over the two tiles:
+//                PV(t0, j), QK(t0, j+1), PV(t1, j), QK(t1, j+1), ... so the
+//                tensor pipe works on one tile while the other's softmax runs.
+//                S = Q K^T: 4 x K16 (64-dim block) + 1 x K16 (16-dim block),
+//                M128 N128; O += P V with P read from TMEM: 8 x K16, N64 + N16
+// TMEM (512 columns): S/P of tile t at [128t, 128t+128), O of tile t at
+// [256+128t, 256+128t+80).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,28 +51,32 @@ namespace vtc {
 
 constexpr int HD = 72;
 constexpr int PAIRS = 36;
-constexpr int BM = 128;
-constexpr int BN = 128;
-constexpr int THREADS = 320;
+constexpr int BM = 128;          // rows per Q tile
+constexpr int QT = 2;            // Q tiles per CTA
+constexpr int BN = 128;          // keys per K/V tile
+constexpr int THREADS = 16 * 32;  // 4 warpgroups: rotation, softmax 0, softmax 1, producer/MMA
+// Register split (setmaxnreg) against the 128 x 512 = 65536 registers of the launch:
+// 128 x 96 (rotation) + 256 x 176 (softmax) + 128 x 56 (producer/MMA) = 64512.
+constexpr uint32_t REGS_ROT = 96, REGS_SOFTMAX = 176, REGS_CTRL = 56;
+static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
 constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr uint32_t SZ_B0 = 128 * 128;   // 128 rows x 64 dims fp16, 128B swizzle
 constexpr uint32_t SZ_B1 = 128 * 32;    // 128 rows x 16 dims fp16, 32B swizzle
-constexpr uint32_t OFF_Q0 = 0;
-constexpr uint32_t OFF_Q1 = OFF_Q0 + SZ_B0;
-constexpr uint32_t OFF_STAGE = OFF_Q1 + SZ_B1;
+constexpr uint32_t Q_BYTES = SZ_B0 + SZ_B1;
+constexpr uint32_t OFF_Q = 0;           // tile t: [OFF_Q + t*Q_BYTES] block0 then block1
+constexpr uint32_t OFF_STAGE = QT * Q_BYTES;
 constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_B0, ST_V0 = SZ_B0 + SZ_B1, ST_V1 = 2 * SZ_B0 + SZ_B1;
 constexpr uint32_t STAGE_BYTES = 2 * (SZ_B0 + SZ_B1);
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
-// barriers: q_full, q_ready, s_full, p_full, o_done, kv_full[2], k_rot[2], kv_empty[2]
-constexpr int NBARS = 11;
+// q_full, q_ready, kv_full[3], k_rot[3], kv_empty[3], s_full[2], p_ready[2], o_done[2]
+constexpr int NBARS = 17;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t TCOL_S = 0;
-constexpr uint32_t TCOL_O = 128;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr float RESCALE_THRESHOLD = 8.0f;             // log2 units
 
 struct Sched {
   uint32_t n_segments;
@@ -121,7 +132,7 @@ __device__ __forceinline__ void rotate_row(uint8_t* b0, uint8_t* b1, int r, cons
   }
 }
 
-__global__ void __launch_bounds__(THREADS, 2)
+__global__ void __launch_bounds__(THREADS, 1)
     vision_tc_kernel(const __grid_constant__ Maps maps, const Params p, const Sched sc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -129,12 +140,12 @@ __global__ void __launch_bounds__(THREADS, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
   uint64_t* q_full = bars + 0;
   uint64_t* q_ready = bars + 1;
-  uint64_t* s_full = bars + 2;
-  uint64_t* p_full = bars + 3;
-  uint64_t* o_done = bars + 4;
-  uint64_t* kv_full = bars + 5;    // [2]
-  uint64_t* k_rot = bars + 7;      // [2]
-  uint64_t* kv_empty = bars + 9;   // [2]
+  uint64_t* kv_full = bars + 2;    // [3]
+  uint64_t* k_rot = bars + 5;      // [3]
+  uint64_t* kv_empty = bars + 8;   // [3]
+  uint64_t* s_full = bars + 11;    // [2]
+  uint64_t* p_ready = bars + 13;   // [2]
+  uint64_t* o_done = bars + 15;    // [2]
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
   // misc[0]: TMEM base, misc[1]: abort
 
@@ -144,24 +155,28 @@ __global__ void __launch_bounds__(THREADS, 2)
   uint32_t sg = 0;
   while (sg + 1 < sc.n_segments && sc.item_prefix[sg + 1] <= item) ++sg;
   const uint32_t seg0 = sc.seg_start[sg], seglen = sc.seg_len[sg];
-  const uint32_t q0 = seg0 + (item - sc.item_prefix[sg]) * BM;
+  const uint32_t q0 = seg0 + (item - sc.item_prefix[sg]) * (QT * BM);
+  const uint32_t seg_end = seg0 + seglen;
+  const bool has1 = q0 + BM < seg_end;       // second Q tile holds rows of this segment
   const int nk = static_cast<int>((seglen + BN - 1) / BN);
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_ready, 4);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
+    mbar_init(q_ready, 8);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&k_rot[s], 4);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
     misc[1] = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -170,18 +185,26 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc::fence_after_sync();
   const uint32_t tmem = misc[0];
 
-  if (warp == 8) {
+  // Registers follow the work (softmax rows hold 128 scores each); each
+  // warpgroup changes its budget at the head of its own branch.
+  const int wg = warp >> 2;
+  if (wg == 3) {
+    tc::regs_dec<REGS_CTRL>();
+   if (warp == 12) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       tc::tma_prefetch_desc(&maps.q0);
       tc::tma_prefetch_desc(&maps.k0);
       tc::tma_prefetch_desc(&maps.v0);
-      mbar_arrive_expect_tx(q_full, SZ_B0 + SZ_B1);
-      tc::tma_load_3d(smem + OFF_Q0, &maps.q0, 0, head, q0, q_full);
-      tc::tma_load_3d(smem + OFF_Q1, &maps.q1, 64, head, q0, q_full);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
+      for (int t = 0; t < (has1 ? 2 : 1); ++t) {
+        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES, &maps.q0, 0, head, q0 + t * BM, q_full);
+        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + SZ_B0, &maps.q1, 64, head, q0 + t * BM, q_full);
+      }
+      int issued = 0;
       for (int j = 0; j < nk; ++j) {
-        const int s = j & 1;
-        const uint32_t use = j >> 1;
+        const int s = j % STAGES;
+        const uint32_t use = j / STAGES;
         if (misc[1] || !mbar_wait(&kv_empty[s], (use & 1) ^ 1)) { misc[1] = 1; break; }
         uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
         const int z = seg0 + j * BN;
@@ -190,16 +213,78 @@ __global__ void __launch_bounds__(THREADS, 2)
         tc::tma_load_3d(st + ST_K1, &maps.k1, 64, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_V0, &maps.v0, 0, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_V1, &maps.v1, 64, head, z, &kv_full[s]);
+        issued = j + 1;
       }
-      // drain: the last loads must land before the CTA may exit
-      for (int j = (nk > 2 ? nk - 2 : 0); j < nk; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1);
+      // the last loads must land before the CTA may exit
+      for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+        mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
     }
-  } else if (warp < 4) {
+   } else if (warp == 13) {
+      // ------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        const uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
+        const uint32_t idesc_pv0 = tc::idesc_f16(128, 64, 0, 1);
+        const uint32_t idesc_pv1 = tc::idesc_f16(128, 16, 0, 1);
+        const int ntile = has1 ? 2 : 1;
+        auto qk = [&](int t, int j) {
+          const uint32_t st = smem_u32(smem + OFF_STAGE + (j % STAGES) * STAGE_BYTES);
+          const uint32_t sq = smem_u32(smem + OFF_Q + t * Q_BYTES);
+          const uint32_t tS = tmem + 128u * t;
+  #pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc::mma_ss(tS, tc::smem_desc(sq + ks * 32, 16, 1024, tc::kSw128),
+                       tc::smem_desc(st + ST_K0 + ks * 32, 16, 1024, tc::kSw128), idesc_qk, ks > 0);
+          tc::mma_ss(tS, tc::smem_desc(sq + SZ_B0, 16, 256, tc::kSw32),
+                     tc::smem_desc(st + ST_K1, 16, 256, tc::kSw32), idesc_qk, 1);
+          tc::commit(&s_full[t]);
+        };
+        auto pv = [&](int t, int j) {
+          const uint32_t st = smem_u32(smem + OFF_STAGE + (j % STAGES) * STAGE_BYTES);
+          const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
+  #pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+            tc::mma_ts(tO, tS + ks * 8, tc::smem_desc(st + ST_V0 + ks * 2048, 16, 1024, tc::kSw128),
+                       idesc_pv0, acc);
+            tc::mma_ts(tO + 64, tS + ks * 8, tc::smem_desc(st + ST_V1 + ks * 512, 16, 256, tc::kSw32),
+                       idesc_pv1, acc);
+          }
+          tc::commit(&o_done[t]);
+        };
+        bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
+        int done = 0;   // tiles whose PV was issued for every Q tile
+        if (ok) {
+          tc::fence_after_sync();
+          for (int t = 0; t < ntile; ++t) qk(t, 0);
+          for (int j = 0; j < nk && ok && !misc[1]; ++j) {
+            const bool more = j + 1 < nk;
+            if (more && !mbar_wait(&k_rot[(j + 1) % STAGES], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+            for (int t = 0; t < ntile; ++t) {
+              if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
+              tc::fence_after_sync();
+              pv(t, j);
+              if (t == ntile - 1) tc::commit(&kv_empty[j % STAGES]);
+              if (more) qk(t, j + 1);
+            }
+            if (ok) done = j + 1;
+          }
+        }
+        if (!ok) misc[1] = 1;
+        // never exit with MMAs in flight or commit arrivals still pending
+        if (done > 0) {
+          for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
+          for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
+            mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+        }
+      }
+   }
+  } else if (wg == 0) {
+    tc::regs_dec<REGS_ROT>();
     // ------------------------------------------------------ K rotation
     const int r = tid;  // key row of the tile
     for (int j = 0; j < nk; ++j) {
-      const int s = j & 1;
-      if (misc[1] || !mbar_wait(&kv_full[s], (j >> 1) & 1)) { misc[1] = 1; break; }
+      const int s = j % STAGES;
+      if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
       uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
       const uint32_t key = j * BN + r;
       if (p.rope_cos && key < seglen) {
@@ -210,49 +295,66 @@ __global__ void __launch_bounds__(THREADS, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&k_rot[s]);
     }
-  } else if (warp < 8) {
+  } else {
+    tc::regs_inc<REGS_SOFTMAX>();
     // ------------------------------------------------------ softmax
-    const int i = tid - 128;            // query row == TMEM lane
+    const int t = (warp - 4) >> 2;                 // Q tile of this warpgroup
+    const int i = tid - 128 - 128 * t;             // query row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + TCOL_S;
-    const uint32_t tO = tmem + lane_base + TCOL_O;
-    bool ok = mbar_wait(q_full, 0);
-    if (ok && p.rope_cos && q0 + i < p.tokens) {
-      const size_t t = q0 + i;
-      rotate_row(smem + OFF_Q0, smem + OFF_Q1, i, p.rope_cos + t * PAIRS, p.rope_sin + t * PAIRS);
+    const uint32_t tS = tmem + lane_base + 128u * t;
+    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+    const uint32_t row = q0 + t * BM + i;          // token of this query row
+    const bool active = t == 0 || has1;
+    bool ok = true;
+    if (active) {
+      ok = mbar_wait(q_full, 0);
+      if (ok && p.rope_cos && row < p.tokens) {
+        uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
+        rotate_row(qb, qb + SZ_B0, i, p.rope_cos + (size_t)row * PAIRS,
+                   p.rope_sin + (size_t)row * PAIRS);
+      }
+      fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
     if (!ok) misc[1] = 1;
 
-    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
-    float m_run = -CUDART_INF_F, l_run = 0.f;
-    bool good = __all_sync(0xffffffffu, ok);
-    for (int j = 0; j < nk && good; ++j) {
-      // every lane of the warp takes the same path through the collective
-      // tcgen05.ld / tcgen05.st below
-      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(s_full, j & 1))) { good = false; break; }
-      tc::fence_after_sync();
-      const int kv = static_cast<int>(umin32(BN, seglen - j * BN));
-      // pass 1: row max of the scaled scores (32-column TMEM chunks)
-      float mx = -CUDART_INF_F;
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sv[32];
-        tc::tmem_ld32(tS + ch * 32, sv);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (ch * 32 + c < kv) mx = fmaxf(mx, __uint_as_float(sv[c]) * scale);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = fast_exp2(m_run - m_new);   // 0 on the first tile
-      if (j > 0) {
-        // O is complete for tiles < j; rescale it in TMEM when a row max moved
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1))) { good = false; break; }
+    if (active) {
+      const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+      float m_run = -CUDART_INF_F, l_run = 0.f;
+      bool good = __all_sync(0xffffffffu, ok);
+      for (int j = 0; j < nk && good; ++j) {
+        // warp-uniform control flow around the collective tcgen05.ld / .st
+        if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], j & 1))) {
+          good = false;
+          break;
+        }
         tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        const int kv = static_cast<int>(umin32(BN, seglen - j * BN));
+        uint32_t sv[128];
+        tc::tmem_ld32(tS + 0, sv);
+        tc::tmem_ld32(tS + 32, sv + 32);
+        tc::tmem_ld32(tS + 64, sv + 64);
+        tc::tmem_ld32(tS + 96, sv + 96);
+        tc::tmem_wait_ld();
+        float mx = -CUDART_INF_F;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float x = c < kv ? __uint_as_float(sv[c]) * scale : -CUDART_INF_F;
+          sv[c] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+        // move the running max only when it grew past the threshold
+        const bool need = mx > m_run + RESCALE_THRESHOLD;
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2(m_run - mx);   // 0 on the first tile
+          m_run = mx;
+          l_run *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1))) { good = false; break; }
+          tc::fence_after_sync();
 #pragma unroll
           for (int cc = 0; cc < 80; cc += 16) {
             uint32_t ov[16];
@@ -263,108 +365,57 @@ __global__ void __launch_bounds__(THREADS, 2)
             tc::tmem_st16(tO + cc, ov);
           }
         }
-      }
-      // pass 2: P = exp2(x - m) as fp16 pairs over the first 64 columns of S;
-      // P chunk c lands in S columns already read (16c < 32(c+1))
-      float rs = 0.f;
+        float rs = 0.f;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sv[32];
-        tc::tmem_ld32(tS + ch * 32, sv);
-        tc::tmem_wait_ld();
-        uint32_t pk[16];
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int k0 = ch * 32 + 2 * c;
-          const float a = k0 < kv ? fast_exp2(__uint_as_float(sv[2 * c]) * scale - m_new) : 0.f;
-          const float b = k0 + 1 < kv ? fast_exp2(__uint_as_float(sv[2 * c + 1]) * scale - m_new) : 0.f;
-          rs += a + b;
-          pk[c] = pack_half2(a, b);
+          for (int c = 0; c < 16; ++c) {
+            const float a = fast_exp2(__uint_as_float(sv[32 * ch + 2 * c]) - m_run);
+            const float b = fast_exp2(__uint_as_float(sv[32 * ch + 2 * c + 1]) - m_run);
+            rs += a + b;
+            pk[c] = pack_half2(a, b);
+          }
+          tc::tmem_st16(tS + 16 * ch, pk);
         }
-        tc::tmem_st16(tS + ch * 16, pk);
+        tc::tmem_wait_st();
+        l_run += rs;
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
       }
-      tc::tmem_wait_st();
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (!good) misc[1] = 1;
-    // epilogue: O / l -> fp16 rows
-    if (__all_sync(0xffffffffu, good && mbar_wait(o_done, (nk - 1) & 1))) {
-      tc::fence_after_sync();
-      const bool store = q0 + i < seg0 + seglen;
-      const float inv = 1.f / l_run;
-      __half* orow = p.out + ((size_t)(q0 + i) * p.heads + head) * HD;
-#pragma unroll
-      for (int cc = 0; cc < 80; cc += 16) {
-        uint32_t ov[16];
-        tc::tmem_ld16(tO + cc, ov);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (cc + 8 * h >= HD) break;   // columns 72..79 are padding
-          uint4 v;
-          v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
-          v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
-          v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
-          v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
-          if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
-        }
-      }
-    } else {
-      misc[1] = 1;
-    }
-  } else {
-    // ------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
-      const uint32_t idesc_pv0 = tc::idesc_f16(128, 64, 0, 1);
-      const uint32_t idesc_pv1 = tc::idesc_f16(128, 16, 0, 1);
-      const uint32_t sq0 = smem_u32(smem + OFF_Q0), sq1 = smem_u32(smem + OFF_Q1);
-      const uint32_t tS = tmem + TCOL_S, tO = tmem + TCOL_O;
-      bool ok = mbar_wait(q_ready, 0);
-      tc::fence_after_sync();
-      int issued = 0;
-      for (int j = 0; j < nk && ok && !misc[1]; ++j) {
-        const int s = j & 1;
-        const uint32_t st = smem_u32(smem + OFF_STAGE + s * STAGE_BYTES);
-        if (!mbar_wait(&k_rot[s], (j >> 1) & 1)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(o_done, (j - 1) & 1)) { ok = false; break; }
+      if (!good) misc[1] = 1;
+      // epilogue: O / l -> fp16 rows
+      if (__all_sync(0xffffffffu, good && mbar_wait(&o_done[t], (nk - 1) & 1))) {
         tc::fence_after_sync();
+        const bool store = row < seg_end;
+        const float inv = 1.f / l_run;
+        __half* orow = p.out + ((size_t)row * p.heads + head) * HD;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_ss(tS, tc::smem_desc(sq0 + ks * 32, 16, 1024, tc::kSw128),
-                     tc::smem_desc(st + ST_K0 + ks * 32, 16, 1024, tc::kSw128), idesc_qk, ks > 0);
-        tc::mma_ss(tS, tc::smem_desc(sq1, 16, 256, tc::kSw32),
-                   tc::smem_desc(st + ST_K1, 16, 256, tc::kSw32), idesc_qk, 1);
-        tc::commit(s_full);
-        if (!mbar_wait(p_full, j & 1)) { ok = false; break; }
-        tc::fence_after_sync();
+        for (int cc = 0; cc < 80; cc += 16) {
+          uint32_t ov[16];
+          tc::tmem_ld16(tO + cc, ov);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-          tc::mma_ts(tO, tS + ks * 8, tc::smem_desc(st + ST_V0 + ks * 2048, 16, 1024, tc::kSw128),
-                     idesc_pv0, acc);
-          tc::mma_ts(tO + 64, tS + ks * 8, tc::smem_desc(st + ST_V1 + ks * 512, 16, 256, tc::kSw32),
-                     idesc_pv1, acc);
+          for (int h = 0; h < 2; ++h) {
+            if (cc + 8 * h >= HD) break;   // columns 72..79 are padding
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
+            v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
+            v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
+            v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
+            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
+          }
         }
-        tc::commit(o_done);
-        tc::commit(&kv_empty[s]);
-        issued = j + 1;
+      } else {
+        misc[1] = 1;
       }
-      if (!ok) misc[1] = 1;
-      // never exit with MMAs in flight or commit arrivals still pending
-      if (issued > 0) mbar_wait(o_done, (issued - 1) & 1);
-      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
-        mbar_wait(&kv_empty[j & 1], (j >> 1) & 1);
     }
   }
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 12) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -407,7 +458,7 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
 
 }  // namespace vtc
 
-int vision_query_tile() { return vtc::BM; }
+int vision_query_tile() { return vtc::QT * vtc::BM; }
 
 int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
                   cudaStream_t stream) {
@@ -441,7 +492,7 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
     sc.seg_start[i] = cu[s];
     sc.seg_len[i] = cu[s + 1] - cu[s];
     sc.item_prefix[i] = items;
-    items += (sc.seg_len[i] + vtc::BM - 1) / vtc::BM;
+    items += (sc.seg_len[i] + vtc::QT * vtc::BM - 1) / (vtc::QT * vtc::BM);
   }
   sc.item_prefix[segments] = items;
   if (items > 65535u) return PVLC_INVALID_VISION_GEOMETRY;
