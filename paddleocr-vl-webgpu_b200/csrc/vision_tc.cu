@@ -9,9 +9,12 @@
 // (segmented attention).  A CTA only visits keys of its own segment.
 //
 // One CTA = one (segment, 256-query pair of tiles, head) work item, one CTA
-// per SM.  head_dim 72 is split into a 64-dim block (128-byte rows, 128B
-// swizzle) and a 16-dim block (32-byte rows, 32B swizzle; TMA zero-fills dims
-// 72..79 as out of bounds), so every MMA has K = 16 and nothing is padded in HBM.
+// per SM.  head_dim 72 never gets padded in HBM: TMA zero-fills the columns
+// past dim 72 as out-of-bounds.
+//   Q, K (MMA K dimension): a 64-dim block (128-byte rows, 128B swizzle) and
+//     a 16-dim block (32-byte rows, 32B swizzle) -> 4 + 1 MMAs of K = 16.
+//   V (MMA N dimension): two 64-dim blocks of 128-byte rows (the second one
+//     holds dims 64..71 and zeros) -> one N = 80 MMA per K step.
 //
 //   warp 12      TMA producer: both Q tiles once, then K/V tiles of 128 keys
 //                through a 3-stage ring
@@ -20,17 +23,17 @@
 //                both Q tiles
 //   warps 4-7,   softmax for Q tile 0 / Q tile 1: thread i owns query row i =
 //   warps 8-11   TMEM lane i; rotates its Q row once; per K tile reads S from
-//                TMEM, online softmax in f32 (exp2 domain), writes P (fp16)
-//                over S; the running max is only moved (and O rescaled in
-//                TMEM) when a row max grows by more than 8 (log2 units), so P
-//                stays <= 256 and the rescale is off the common path
+//                TMEM, online softmax in f32 (exp2 domain, packed f32x2 math),
+//                writes P (fp16) over S; the running max only moves (and O
+//                is rescaled in TMEM) when a row max grows by more than 8 in
+//                log2 units, so P stays <= 256 and the rescale is rare
 //   warp 13      MMA issuer (one thread), ping-pong over the two tiles:
 //                PV(t0, j), QK(t0, j+1), PV(t1, j), QK(t1, j+1), ... so the
-//                tensor pipe works on one tile while the other's softmax runs.
-//                S = Q K^T: 4 x K16 (64-dim block) + 1 x K16 (16-dim block),
-//                M128 N128; O += P V with P read from TMEM: 8 x K16, N64 + N16
+//                tensor pipe works on one tile while the other's softmax runs
 // TMEM (512 columns): S/P of tile t at [128t, 128t+128), O of tile t at
 // [256+128t, 256+128t+80).
+// setmaxnreg moves registers from the rotation and control warpgroups to the
+// two softmax warpgroups.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -55,26 +58,27 @@ constexpr int BM = 128;          // rows per Q tile
 constexpr int QT = 2;            // Q tiles per CTA
 constexpr int BN = 128;          // keys per K/V tile
 constexpr int THREADS = 16 * 32;  // 4 warpgroups: rotation, softmax 0, softmax 1, producer/MMA
-// Register split (setmaxnreg) against the 128 x 512 = 65536 registers of the launch:
-// 128 x 96 (rotation) + 256 x 176 (softmax) + 128 x 56 (producer/MMA) = 64512.
+// Register split (setmaxnreg) against the 128 x 512 = 65536 registers of the launch.
 constexpr uint32_t REGS_ROT = 96, REGS_SOFTMAX = 176, REGS_CTRL = 56;
 static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
 constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
 
 // shared memory map (offsets from a 1024-aligned base)
-constexpr uint32_t SZ_B0 = 128 * 128;   // 128 rows x 64 dims fp16, 128B swizzle
-constexpr uint32_t SZ_B1 = 128 * 32;    // 128 rows x 16 dims fp16, 32B swizzle
-constexpr uint32_t Q_BYTES = SZ_B0 + SZ_B1;
-constexpr uint32_t OFF_Q = 0;           // tile t: [OFF_Q + t*Q_BYTES] block0 then block1
+constexpr uint32_t SZ_W = 128 * 128;    // 128 rows x 64 dims fp16, 128B swizzle
+constexpr uint32_t SZ_N = 128 * 32;     // 128 rows x 16 dims fp16, 32B swizzle
+constexpr uint32_t Q_BYTES = SZ_W + SZ_N;
+constexpr uint32_t OFF_Q = 0;           // tile t at OFF_Q + t * Q_BYTES: wide block, narrow block
 constexpr uint32_t OFF_STAGE = QT * Q_BYTES;
-constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_B0, ST_V0 = SZ_B0 + SZ_B1, ST_V1 = 2 * SZ_B0 + SZ_B1;
-constexpr uint32_t STAGE_BYTES = 2 * (SZ_B0 + SZ_B1);
+constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_W, ST_V0 = SZ_W + SZ_N, ST_V1 = 2 * SZ_W + SZ_N;
+constexpr uint32_t STAGE_BYTES = 3 * SZ_W + SZ_N;
 constexpr int STAGES = 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
 // q_full, q_ready, kv_full[3], k_rot[3], kv_empty[3], s_full[2], p_ready[2], o_done[2]
 constexpr int NBARS = 17;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 227 * 1024, "vision shared memory exceeds the sm_100 limit");
+static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "swizzle atoms need 1 KB alignment");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;             // log2 units
 
@@ -86,7 +90,7 @@ struct Sched {
 };
 
 struct Maps {
-  CUtensorMap q0, q1, k0, k1, v0, v1;
+  CUtensorMap q0, q1, k0, k1, v0;
 };
 
 struct Params {
@@ -130,6 +134,12 @@ __device__ __forceinline__ void rotate_row(uint8_t* b0, uint8_t* b1, int r, cons
                          : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
     *reinterpret_cast<uint4*>(dst) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
   }
+}
+
+__device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -190,16 +200,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int wg = warp >> 2;
   if (wg == 3) {
     tc::regs_dec<REGS_CTRL>();
-   if (warp == 12) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (warp == 12 && lane == 0) {
+      // ---------------------------------------------------- TMA producer
       tc::tma_prefetch_desc(&maps.q0);
       tc::tma_prefetch_desc(&maps.k0);
       tc::tma_prefetch_desc(&maps.v0);
       mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
       for (int t = 0; t < (has1 ? 2 : 1); ++t) {
         tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES, &maps.q0, 0, head, q0 + t * BM, q_full);
-        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + SZ_B0, &maps.q1, 64, head, q0 + t * BM, q_full);
+        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + SZ_W, &maps.q1, 64, head, q0 + t * BM, q_full);
       }
       int issued = 0;
       for (int j = 0; j < nk; ++j) {
@@ -212,72 +221,74 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tma_load_3d(st + ST_K0, &maps.k0, 0, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_K1, &maps.k1, 64, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_V0, &maps.v0, 0, head, z, &kv_full[s]);
-        tc::tma_load_3d(st + ST_V1, &maps.v1, 64, head, z, &kv_full[s]);
+        tc::tma_load_3d(st + ST_V1, &maps.v0, 64, head, z, &kv_full[s]);
         issued = j + 1;
       }
       // the last loads must land before the CTA may exit
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
-    }
-   } else if (warp == 13) {
-      // ------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        const uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
-        const uint32_t idesc_pv0 = tc::idesc_f16(128, 64, 0, 1);
-        const uint32_t idesc_pv1 = tc::idesc_f16(128, 16, 0, 1);
-        const int ntile = has1 ? 2 : 1;
-        auto qk = [&](int t, int j) {
-          const uint32_t st = smem_u32(smem + OFF_STAGE + (j % STAGES) * STAGE_BYTES);
-          const uint32_t sq = smem_u32(smem + OFF_Q + t * Q_BYTES);
-          const uint32_t tS = tmem + 128u * t;
-  #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc::mma_ss(tS, tc::smem_desc(sq + ks * 32, 16, 1024, tc::kSw128),
-                       tc::smem_desc(st + ST_K0 + ks * 32, 16, 1024, tc::kSw128), idesc_qk, ks > 0);
-          tc::mma_ss(tS, tc::smem_desc(sq + SZ_B0, 16, 256, tc::kSw32),
-                     tc::smem_desc(st + ST_K1, 16, 256, tc::kSw32), idesc_qk, 1);
-          tc::commit(&s_full[t]);
-        };
-        auto pv = [&](int t, int j) {
-          const uint32_t st = smem_u32(smem + OFF_STAGE + (j % STAGES) * STAGE_BYTES);
-          const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
-  #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-            tc::mma_ts(tO, tS + ks * 8, tc::smem_desc(st + ST_V0 + ks * 2048, 16, 1024, tc::kSw128),
-                       idesc_pv0, acc);
-            tc::mma_ts(tO + 64, tS + ks * 8, tc::smem_desc(st + ST_V1 + ks * 512, 16, 256, tc::kSw32),
-                       idesc_pv1, acc);
+    } else if (warp == 13 && lane == 0) {
+      // ---------------------------------------------------- MMA issuer
+      // Descriptors are built once; each K step only adds a constant to the
+      // start-address field (address >> 4 in the low bits).
+      constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(128, 80, 0, 1);
+      const int ntile = has1 ? 2 : 1;
+      // Descriptors of tile t / stage s are the tile-0 / stage-0 descriptors
+      // plus the byte offset >> 4 in the start-address field (which never
+      // carries out of its 14 bits inside 227 KB of shared memory).
+      const uint32_t sq = smem_u32(smem + OFF_Q);
+      const uint32_t st0 = smem_u32(smem + OFF_STAGE);
+      const uint64_t dq_w = tc::smem_desc(sq, 16, 1024, tc::kSw128);
+      const uint64_t dq_n = tc::smem_desc(sq + SZ_W, 16, 256, tc::kSw32);
+      const uint64_t dk_w = tc::smem_desc(st0 + ST_K0, 16, 1024, tc::kSw128);
+      const uint64_t dk_n = tc::smem_desc(st0 + ST_K1, 16, 256, tc::kSw32);
+      // MN-major V: 64-column swizzle atoms ST_V1 - ST_V0 apart (LBO), 8-key groups 1 KB apart
+      const uint64_t dv = tc::smem_desc(st0 + ST_V0, ST_V1 - ST_V0, 1024, tc::kSw128);
+      auto qk = [&](int t, int s) {
+        const uint32_t tS = tmem + 128u * t;
+        const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4), so = (uint64_t)s * (STAGE_BYTES >> 4);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)   // 32 bytes (16 dims) per K step -> +2 in the address field
+          tc::mma_ss(tS, dq_w + qo + 2 * ks, dk_w + so + 2 * ks, idesc_qk, ks > 0);
+        tc::mma_ss(tS, dq_n + qo, dk_n + so, idesc_qk, 1);
+        tc::commit(&s_full[t]);
+      };
+      auto pv = [&](int t, int s, bool first) {
+        const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
+        const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)   // 16 keys = two 1 KB groups per K step -> +128
+          tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+        tc::commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
+      int done = 0;   // K tiles whose PV was issued for every Q tile
+      if (ok) {
+        tc::fence_after_sync();
+        for (int t = 0; t < ntile; ++t) qk(t, 0);
+        for (int j = 0; j < nk && ok && !misc[1]; ++j) {
+          const bool more = j + 1 < nk;
+          const int s = j % STAGES, s1 = (j + 1) % STAGES;
+          if (more && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+          for (int t = 0; t < ntile; ++t) {
+            if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
+            tc::fence_after_sync();
+            pv(t, s, j == 0);
+            if (t == ntile - 1) tc::commit(&kv_empty[s]);
+            if (more) qk(t, s1);
           }
-          tc::commit(&o_done[t]);
-        };
-        bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
-        int done = 0;   // tiles whose PV was issued for every Q tile
-        if (ok) {
-          tc::fence_after_sync();
-          for (int t = 0; t < ntile; ++t) qk(t, 0);
-          for (int j = 0; j < nk && ok && !misc[1]; ++j) {
-            const bool more = j + 1 < nk;
-            if (more && !mbar_wait(&k_rot[(j + 1) % STAGES], ((j + 1) / STAGES) & 1)) { ok = false; break; }
-            for (int t = 0; t < ntile; ++t) {
-              if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
-              tc::fence_after_sync();
-              pv(t, j);
-              if (t == ntile - 1) tc::commit(&kv_empty[j % STAGES]);
-              if (more) qk(t, j + 1);
-            }
-            if (ok) done = j + 1;
-          }
-        }
-        if (!ok) misc[1] = 1;
-        // never exit with MMAs in flight or commit arrivals still pending
-        if (done > 0) {
-          for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
-          for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
-            mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+          if (ok) done = j + 1;
         }
       }
-   }
+      if (!ok) misc[1] = 1;
+      // never exit with MMAs in flight or commit arrivals still pending
+      if (done > 0) {
+        for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
+        for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
+          mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+      }
+    }
   } else if (wg == 0) {
     tc::regs_dec<REGS_ROT>();
     // ------------------------------------------------------ K rotation
@@ -298,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
     // ------------------------------------------------------ softmax
-    const int t = (warp - 4) >> 2;                 // Q tile of this warpgroup
+    const int t = wg - 1;                          // Q tile of this warpgroup
     const int i = tid - 128 - 128 * t;             // query row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128u * t;
@@ -310,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       ok = mbar_wait(q_full, 0);
       if (ok && p.rope_cos && row < p.tokens) {
         uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
-        rotate_row(qb, qb + SZ_B0, i, p.rope_cos + (size_t)row * PAIRS,
+        rotate_row(qb, qb + SZ_W, i, p.rope_cos + (size_t)row * PAIRS,
                    p.rope_sin + (size_t)row * PAIRS);
       }
       fence_proxy_async_smem();
@@ -321,6 +332,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (active) {
       const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+      const uint64_t scale2 = f2_pack(scale, scale);
       float m_run = -CUDART_INF_F, l_run = 0.f;
       bool good = __all_sync(0xffffffffu, ok);
       for (int j = 0; j < nk && good; ++j) {
@@ -337,13 +349,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tmem_ld32(tS + 64, sv + 64);
         tc::tmem_ld32(tS + 96, sv + 96);
         tc::tmem_wait_ld();
-        float mx = -CUDART_INF_F;
+        if (kv < BN) {   // last tile of the segment: keys past its end score -inf
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float x = c < kv ? __uint_as_float(sv[c]) * scale : -CUDART_INF_F;
-          sv[c] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          for (int c = 0; c < 128; ++c)
+            if (c >= kv) sv[c] = __float_as_uint(-CUDART_INF_F);
         }
+        float mx = __uint_as_float(sv[0]);
+#pragma unroll
+        for (int c = 1; c < 127; c += 2)
+          mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+        mx = fmaxf(mx, __uint_as_float(sv[127])) * scale;
         // move the running max only when it grew past the threshold
         const bool need = mx > m_run + RESCALE_THRESHOLD;
         float alpha = 1.f;
@@ -365,21 +380,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_st16(tO + cc, ov);
           }
         }
-        float rs = 0.f;
+        const uint64_t negm2 = f2_pack(-m_run, -m_run);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const float a = fast_exp2(__uint_as_float(sv[32 * ch + 2 * c]) - m_run);
-            const float b = fast_exp2(__uint_as_float(sv[32 * ch + 2 * c + 1]) - m_run);
-            rs += a + b;
+            const int k = 32 * ch + 2 * c;
+            const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
+            const float a = fast_exp2(x.x), b = fast_exp2(x.y);
+            sum2 = f2_add(sum2, f2_pack(a, b));
             pk[c] = pack_half2(a, b);
           }
           tc::tmem_st16(tS + 16 * ch, pk);
         }
         tc::tmem_wait_st();
-        l_run += rs;
+        const float2 sum = f2_unpack(sum2);
+        l_run += sum.x + sum.y;
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[t]);
@@ -476,8 +494,7 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
                   vtc::make_map(&maps.q1, a.q, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
                   vtc::make_map(&maps.k0, a.k, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
                   vtc::make_map(&maps.k1, a.k, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
-                  vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  vtc::make_map(&maps.v1, a.v, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B);
+                  vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return PVLC_CUDA_ERROR;
   vtc::Sched sc;
   std::vector<uint32_t> order(segments);
