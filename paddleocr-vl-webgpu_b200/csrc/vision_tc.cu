@@ -101,6 +101,45 @@ struct Params {
   uint32_t tokens;
 };
 
+// The 36 (cos, sin) table entries of one token, held in registers.
+struct RopeRow {
+  float4 c[PAIRS / 4], s[PAIRS / 4];
+};
+
+__device__ __forceinline__ void load_rope_row(RopeRow& t, const float* cs, const float* sn) {
+#pragma unroll
+  for (int j = 0; j < PAIRS / 4; ++j) {
+    t.c[j] = __ldg(reinterpret_cast<const float4*>(cs) + j);
+    t.s[j] = __ldg(reinterpret_cast<const float4*>(sn) + j);
+  }
+}
+
+// Element (row r, 16-byte chunk c) of a 72-dim row split into a 64-dim
+// 128B-swizzled block and a 16-dim 32B-swizzled block.
+__device__ __forceinline__ uint8_t* row_chunk(uint8_t* b0, uint8_t* b1, int r, int c) {
+  return c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4) : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
+}
+
+// Rotate one row in place with tables already in registers.  Quad j holds
+// pairs 4j..4j+3: dims 4j..4j+3 (8 bytes) and their partners 36+4j..39+4j.
+__device__ __forceinline__ void rotate_row_regs(uint8_t* b0, uint8_t* b1, int r, const RopeRow& t) {
+#pragma unroll
+  for (int j = 0; j < PAIRS / 4; ++j) {
+    uint2* lo = reinterpret_cast<uint2*>(row_chunk(b0, b1, r, j >> 1) + 8 * (j & 1));
+    uint2* hi = reinterpret_cast<uint2*>(row_chunk(b0, b1, r, (j + 9) >> 1) + 8 * ((j + 9) & 1));
+    const uint2 a = *lo, b = *hi;
+    const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
+    const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
+    const float2 b0v = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
+    const float2 b1v = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
+    const float4 c = t.c[j], s = t.s[j];
+    *lo = make_uint2(pack_half2(a0.x * c.x - b0v.x * s.x, a0.y * c.y - b0v.y * s.y),
+                     pack_half2(a1.x * c.z - b1v.x * s.z, a1.y * c.w - b1v.y * s.w));
+    *hi = make_uint2(pack_half2(b0v.x * c.x + a0.x * s.x, b0v.y * c.y + a0.y * s.y),
+                     pack_half2(b1v.x * c.z + a1.x * s.z, b1v.y * c.w + a1.y * s.w));
+  }
+}
+
 // Rotate one 72-dim row held in a (64-dim SW128, 16-dim SW32) pair of tiles,
 // in place.  Pair p rotates dims (p, p + 36) by table entry p.
 __device__ __forceinline__ void rotate_row(uint8_t* b0, uint8_t* b1, int r, const float* cs,
@@ -270,13 +309,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = 0; j < nk && ok && !misc[1]; ++j) {
           const bool more = j + 1 < nk;
           const int s = j % STAGES, s1 = (j + 1) % STAGES;
-          if (more && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
           for (int t = 0; t < ntile; ++t) {
             if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
             tc::fence_after_sync();
             pv(t, s, j == 0);
             if (t == ntile - 1) tc::commit(&kv_empty[s]);
-            if (more) qk(t, s1);
+            if (more) {
+              // only the next QK needs the next rotated K tile
+              if (t == 0 && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+              tc::fence_after_sync();
+              qk(t, s1);
+            }
           }
           if (ok) done = j + 1;
         }
@@ -292,19 +335,27 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (wg == 0) {
     tc::regs_dec<REGS_ROT>();
     // ------------------------------------------------------ K rotation
+    // Software-pipelined: the table row of the next tile is fetched right
+    // after the current tile is rotated, so its L2 latency overlaps the wait
+    // for the next K tile.
     const int r = tid;  // key row of the tile
+    const bool rope = p.rope_cos != nullptr;
+    RopeRow tab;
+    if (rope && (uint32_t)r < seglen)
+      load_rope_row(tab, p.rope_cos + (size_t)(seg0 + r) * PAIRS,
+                    p.rope_sin + (size_t)(seg0 + r) * PAIRS);
     for (int j = 0; j < nk; ++j) {
       const int s = j % STAGES;
       if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
       uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-      const uint32_t key = j * BN + r;
-      if (p.rope_cos && key < seglen) {
-        const size_t t = seg0 + key;
-        rotate_row(st + ST_K0, st + ST_K1, r, p.rope_cos + t * PAIRS, p.rope_sin + t * PAIRS);
-      }
+      if (rope && j * BN + r < seglen) rotate_row_regs(st + ST_K0, st + ST_K1, r, tab);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&k_rot[s]);
+      const uint32_t next = (j + 1) * BN + r;
+      if (rope && next < seglen)
+        load_rope_row(tab, p.rope_cos + (size_t)(seg0 + next) * PAIRS,
+                      p.rope_sin + (size_t)(seg0 + next) * PAIRS);
     }
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
