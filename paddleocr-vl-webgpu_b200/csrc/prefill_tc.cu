@@ -1,0 +1,493 @@
+// prefill_tc.cu -- decoder causal GQA prefill (pinned Q16/KV2/D128) on the
+// Blackwell tensor cores (tcgen05 + TMEM + TMA) with the 3-section
+// multimodal RoPE fused into the Q/K tiles and the rotated key / raw value
+// written into the fp16 KV cache in place.  sm_100a.
+//
+// Reference path replaced: DecoderPrefillMropeF32 -> DecoderKvAppendRangeF32
+// -> DecoderPrefillGqaF32 (crates/pvlc-wgsl/src/lib.rs:1262-1416; stage order
+// crates/pvlc-runtime-core/src/lib.rs:2613-2629); arithmetic
+// crates/pvlc-cpu-ref/src/lib.rs:562-672 (M-RoPE), :976-991 (KV write),
+// :782-853 (causal GQA).
+//
+// GQA packing: a Q tile is 16 tokens x the 8 query heads of one KV group =
+// 128 MMA rows (row r = token r/8, head r%8), loaded by one 3-D TMA box, so a
+// K/V tile of 128 keys serves all 8 heads.  One CTA = (KV head, two
+// consecutive 16-token blocks); its two Q tiles ping-pong on the MMA warp.
+// Causal: K tiles 0 .. last needed only, masking inside the tiles that cross
+// the diagonal.  head_dim 128 = two 64-dim blocks of 128-byte rows (128B
+// swizzle); QK = 8 x K16 steps (M128 N128), PV = 8 x K16 steps (M128 N128,
+// V as an MN-major operand spanning both blocks).
+//
+//   warp 12      TMA producer: both Q tiles, then K/V tiles (2-stage ring)
+//   warps 0-3    rotation: thread r rotates key row r of a staged K tile in
+//                place with M-RoPE, then writes the rotated key and raw value
+//                rows of this CTA's own tokens into the KV cache
+//   warps 4-11   softmax for Q tile 0 / 1: thread i owns row i = TMEM lane i
+//   warp 13      MMA issuer (one thread)
+// TMEM (512 columns): S/P of tile t at [128t, 128t+128), O at [256+128t, +128).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "pvlc_common.cuh"
+#include "pvlc_internal.h"
+#include "tcgen05.cuh"
+
+namespace pvlc {
+namespace ptc {
+
+constexpr int HD = 128;
+constexpr int QH = 16;
+constexpr int KVH = 2;
+constexpr int GROUP = 8;
+constexpr int TOK = 16;          // tokens per Q tile (x 8 heads = 128 rows)
+constexpr int QT = 2;            // Q tiles per CTA
+constexpr int BN = 128;          // keys per K/V tile
+constexpr int THREADS = 16 * 32;
+constexpr uint32_t REGS_ROT = 96, REGS_SOFTMAX = 176, REGS_CTRL = 56;
+static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
+
+constexpr uint32_t SZ_W = 128 * 128;          // 128 rows x 64 dims fp16, 128B swizzle
+constexpr uint32_t Q_BYTES = 2 * SZ_W;        // two 64-dim blocks
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_STAGE = QT * Q_BYTES;
+constexpr uint32_t ST_K = 0, ST_V = 2 * SZ_W;
+constexpr uint32_t STAGE_BYTES = 4 * SZ_W;
+constexpr int STAGES = 2;
+constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
+// q_full, q_ready, kv_full[2], k_rot[2], kv_empty[2], s_full[2], p_ready[2], o_done[2]
+constexpr int NBARS = 14;
+constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
+static_assert(SMEM_BYTES <= 227 * 1024, "prefill shared memory exceeds the sm_100 limit");
+constexpr uint32_t TMEM_COLS = 512;
+constexpr float RESCALE_THRESHOLD = 8.0f;
+
+struct Maps {
+  CUtensorMap q, k, v;
+};
+
+struct Params {
+  const float* rope_cos;  // [3, rope_rows, 128]
+  const float* rope_sin;
+  uint32_t rope_rows;
+  uint32_t tokens;
+  __half* k_cache;        // [capacity, 2, 128]
+  __half* v_cache;
+  __half* out;            // [T, 16, 128]
+};
+
+__device__ __forceinline__ uint8_t* chunk_addr(uint8_t* blk, int r, int c) {
+  return blk + r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+// M-RoPE of one 128-dim row held in two 128B-swizzled 64-dim blocks, in
+// place (crates/pvlc-cpu-ref/src/lib.rs:645-668): dim d < 64 becomes
+// x[d] cos[d] - x[d+64] sin[d], dim d+64 becomes x[d+64] cos[d+64] + x[d] sin[d+64];
+// cos/sin come from axis plane 0/1/2 for (d mod 64) in [0,16)/[16,40)/[40,64).
+__device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const Params& p,
+                                          uint32_t token) {
+#pragma unroll 2
+  for (int c = 0; c < 8; ++c) {          // dims 8c..8c+7 and 64+8c..64+8c+7
+    const uint32_t axis = mrope_axis(8 * c);   // sections are multiples of 8
+    const size_t tb = ((size_t)axis * p.rope_rows + token) * HD + 8 * c;
+    const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + tb);
+    const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + tb);
+    const float4 cl0 = __ldg(cs), cl1 = __ldg(cs + 1), ch0 = __ldg(cs + 16), ch1 = __ldg(cs + 17);
+    const float4 sl0 = __ldg(sn), sl1 = __ldg(sn + 1), sh0 = __ldg(sn + 16), sh1 = __ldg(sn + 17);
+    uint4* pa = reinterpret_cast<uint4*>(chunk_addr(b0, r, c));
+    uint4* pb = reinterpret_cast<uint4*>(chunk_addr(b1, r, c));
+    const uint4 a = *pa, b = *pb;
+    const float cl[8] = {cl0.x, cl0.y, cl0.z, cl0.w, cl1.x, cl1.y, cl1.z, cl1.w};
+    const float chh[8] = {ch0.x, ch0.y, ch0.z, ch0.w, ch1.x, ch1.y, ch1.z, ch1.w};
+    const float sl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
+    const float shh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t ra[4], rb[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&aw[e]));
+      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&bw[e]));
+      ra[e] = pack_half2(x.x * cl[2 * e] + (-y.x) * sl[2 * e], x.y * cl[2 * e + 1] + (-y.y) * sl[2 * e + 1]);
+      rb[e] = pack_half2(y.x * chh[2 * e] + x.x * shh[2 * e], y.y * chh[2 * e + 1] + x.y * shh[2 * e + 1]);
+    }
+    *pa = make_uint4(ra[0], ra[1], ra[2], ra[3]);
+    *pb = make_uint4(rb[0], rb[1], rb[2], rb[3]);
+  }
+}
+
+__device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_tc_kernel(const __grid_constant__ Maps maps, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* kv_full = bars + 2;    // [2]
+  uint64_t* k_rot = bars + 4;      // [2]
+  uint64_t* kv_empty = bars + 6;   // [2]
+  uint64_t* s_full = bars + 8;     // [2]
+  uint64_t* p_ready = bars + 10;   // [2]
+  uint64_t* o_done = bars + 12;    // [2]
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t g = blockIdx.x;                      // KV head
+  const uint32_t n_pairs = (p.tokens + QT * TOK - 1) / (QT * TOK);
+  const uint32_t pair = n_pairs - 1 - blockIdx.y;     // heaviest (latest) first
+  const uint32_t tok0 = pair * QT * TOK;              // first token of Q tile 0
+  const bool has1 = tok0 + TOK < p.tokens;
+  const uint32_t last_tok = umin32(tok0 + QT * TOK, p.tokens) - 1;
+  const int nk = static_cast<int>(last_tok / BN) + 1;  // K tiles 0 .. the diagonal
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 8);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&k_rot[s], 4);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < QT; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 12) {
+    tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = misc[0];
+
+  const int wg = warp >> 2;
+  if (wg == 3) {
+    tc::regs_dec<REGS_CTRL>();
+    if (warp == 12 && lane == 0) {
+      // ---------------------------------------------------- TMA producer
+      tc::tma_prefetch_desc(&maps.q);
+      tc::tma_prefetch_desc(&maps.k);
+      tc::tma_prefetch_desc(&maps.v);
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
+      for (int t = 0; t < (has1 ? 2 : 1); ++t)
+        for (int b = 0; b < 2; ++b)
+          tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + b * SZ_W, &maps.q, 64 * b, GROUP * g,
+                          tok0 + t * TOK, q_full);
+      int issued = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % STAGES;
+        if (misc[1] || !mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1)) { misc[1] = 1; break; }
+        uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
+        for (int b = 0; b < 2; ++b) {
+          tc::tma_load_3d(st + ST_K + b * SZ_W, &maps.k, 64 * b, g, j * BN, &kv_full[s]);
+          tc::tma_load_3d(st + ST_V + b * SZ_W, &maps.v, 64 * b, g, j * BN, &kv_full[s]);
+        }
+        issued = j + 1;
+      }
+      for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
+        mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
+    } else if (warp == 13 && lane == 0) {
+      // ---------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
+      const int ntile = has1 ? 2 : 1;
+      const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + OFF_STAGE);
+      const uint64_t dq = tc::smem_desc(sq, 16, 1024, tc::kSw128);
+      const uint64_t dk = tc::smem_desc(st0 + ST_K, 16, 1024, tc::kSw128);
+      // MN-major V: the two 64-dim blocks are SZ_W apart (LBO), 8-key groups 1 KB apart
+      const uint64_t dv = tc::smem_desc(st0 + ST_V, SZ_W, 1024, tc::kSw128);
+      auto qk = [&](int t, int s) {
+        const uint32_t tS = tmem + 128u * t;
+        const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4), so = (uint64_t)s * (STAGE_BYTES >> 4);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {   // block ks/4, 32 bytes per K step within a block
+          const uint64_t off = (uint64_t)(ks >> 2) * (SZ_W >> 4) + 2 * (ks & 3);
+          tc::mma_ss(tS, dq + qo + off, dk + so + off, idesc_qk, ks > 0);
+        }
+        tc::commit(&s_full[t]);
+      };
+      auto pv = [&](int t, int s, bool first) {
+        const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
+        const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)     // 16 keys = two 1 KB groups per K step
+          tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+        tc::commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
+      int done = 0;
+      if (ok) {
+        tc::fence_after_sync();
+        for (int t = 0; t < ntile; ++t) qk(t, 0);
+        for (int j = 0; j < nk && ok && !misc[1]; ++j) {
+          const bool more = j + 1 < nk;
+          const int s = j % STAGES, s1 = (j + 1) % STAGES;
+          for (int t = 0; t < ntile; ++t) {
+            if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
+            tc::fence_after_sync();
+            pv(t, s, j == 0);
+            if (t == ntile - 1) tc::commit(&kv_empty[s]);
+            if (more) {
+              if (t == 0 && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+              tc::fence_after_sync();
+              qk(t, s1);
+            }
+          }
+          if (ok) done = j + 1;
+        }
+      }
+      if (!ok) misc[1] = 1;
+      if (done > 0) {
+        for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
+        for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
+          mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+      }
+    }
+  } else if (wg == 0) {
+    tc::regs_dec<REGS_ROT>();
+    // ------------------------------------------------------ K rotation + cache write
+    const int r = tid;
+    const uint32_t own0 = tok0, own1 = umin32(tok0 + QT * TOK, p.tokens);  // tokens this CTA owns
+    for (int j = 0; j < nk; ++j) {
+      const int s = j % STAGES;
+      if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
+      uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+      const uint32_t token = j * BN + r;
+      if (token < p.tokens) {
+        mrope_row(st + ST_K, st + ST_K + SZ_W, r, p, token);
+        if (token >= own0 && token < own1) {
+          // in-place cache write of this token's rotated key and raw value
+          uint4* kd = reinterpret_cast<uint4*>(p.k_cache + ((size_t)token * KVH + g) * HD);
+          uint4* vd = reinterpret_cast<uint4*>(p.v_cache + ((size_t)token * KVH + g) * HD);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int b = c >> 3, cc = c & 7;
+            kd[c] = *reinterpret_cast<const uint4*>(chunk_addr(st + ST_K + b * SZ_W, r, cc));
+            vd[c] = *reinterpret_cast<const uint4*>(chunk_addr(st + ST_V + b * SZ_W, r, cc));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&k_rot[s]);
+    }
+  } else {
+    tc::regs_inc<REGS_SOFTMAX>();
+    // ------------------------------------------------------ softmax
+    const int t = wg - 1;
+    const int i = tid - 128 - 128 * t;               // row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + 128u * t;
+    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+    const uint32_t token = tok0 + t * TOK + (i >> 3);
+    const uint32_t head = GROUP * g + (i & 7);
+    const bool active = t == 0 || has1;
+    bool ok = true;
+    if (active) {
+      ok = mbar_wait(q_full, 0);
+      if (ok && token < p.tokens) {
+        uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
+        mrope_row(qb, qb + SZ_W, i, p, token);
+      }
+      fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_ready);
+    if (!ok) misc[1] = 1;
+
+    if (active) {
+      const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+      const uint64_t scale2 = f2_pack(scale, scale);
+      float m_run = -CUDART_INF_F, l_run = 0.f;
+      bool good = __all_sync(0xffffffffu, ok);
+      // first token of this warp's rows: rows 32w'..32w'+31 cover tokens +4w'..+4w'+3
+      const uint32_t warp_tok_lo = tok0 + t * TOK + ((warp & 3) * 32 >> 3);
+      for (int j = 0; j < nk && good; ++j) {
+        if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], j & 1))) {
+          good = false;
+          break;
+        }
+        tc::fence_after_sync();
+        uint32_t sv[128];
+        tc::tmem_ld32(tS + 0, sv);
+        tc::tmem_ld32(tS + 32, sv + 32);
+        tc::tmem_ld32(tS + 64, sv + 64);
+        tc::tmem_ld32(tS + 96, sv + 96);
+        tc::tmem_wait_ld();
+        // causal mask where this tile reaches past the warp's first token
+        if (j * BN + BN - 1 > warp_tok_lo) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (j * BN + c > token) sv[c] = __float_as_uint(-CUDART_INF_F);
+        }
+        float mx = __uint_as_float(sv[0]);
+#pragma unroll
+        for (int c = 1; c < 127; c += 2)
+          mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+        mx = fmaxf(mx, __uint_as_float(sv[127])) * scale;
+        const bool need = mx > m_run + RESCALE_THRESHOLD;
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2(m_run - mx);
+          m_run = mx;
+          l_run *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1))) { good = false; break; }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int cc = 0; cc < 128; cc += 16) {
+            uint32_t ov[16];
+            tc::tmem_ld16(tO + cc, ov);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tc::tmem_st16(tO + cc, ov);
+          }
+        }
+        // rows whose every key so far is masked keep m_run = -inf: use 0 so
+        // that exp2(-inf - 0) = 0 rather than NaN
+        const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
+        const uint64_t negm2 = f2_pack(-mm, -mm);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int k = 32 * ch + 2 * c;
+            const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
+            const float a = fast_exp2(x.x), b = fast_exp2(x.y);
+            sum2 = f2_add(sum2, f2_pack(a, b));
+            pk[c] = pack_half2(a, b);
+          }
+          tc::tmem_st16(tS + 16 * ch, pk);
+        }
+        tc::tmem_wait_st();
+        const float2 sum = f2_unpack(sum2);
+        l_run += sum.x + sum.y;
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
+      }
+      if (!good) misc[1] = 1;
+      if (__all_sync(0xffffffffu, good && mbar_wait(&o_done[t], (nk - 1) & 1))) {
+        tc::fence_after_sync();
+        const bool store = token < p.tokens;
+        const float inv = 1.f / l_run;
+        __half* orow = p.out + ((size_t)token * QH + head) * HD;
+#pragma unroll
+        for (int cc = 0; cc < 128; cc += 16) {
+          uint32_t ov[16];
+          tc::tmem_ld16(tO + cc, ov);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4 v;
+            v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
+            v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
+            v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
+            v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
+            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
+          }
+        }
+      } else {
+        misc[1] = 1;
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 12) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(ptr);
+  });
+  return fn;
+}
+
+// [tokens, heads, 128] fp16 as a 3-D tensor {128, heads, tokens}; box
+// {64 dims, box_heads, box_tokens}, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
+              uint32_t box_heads, uint32_t box_tokens) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {HD, heads, tokens};
+  const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)heads * HD * 2};
+  const cuuint32_t box[3] = {64, box_heads, box_tokens};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace ptc
+
+int prefill_query_tile() { return ptc::QT * ptc::TOK; }
+
+int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(ptc::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             ptc::SMEM_BYTES) != cudaSuccess)
+      return PVLC_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  ptc::Maps maps;
+  if (!ptc::make_map(&maps.q, a.q, a.tokens, ptc::QH, ptc::GROUP, ptc::TOK) ||
+      !ptc::make_map(&maps.k, a.k, a.tokens, ptc::KVH, 1, ptc::BN) ||
+      !ptc::make_map(&maps.v, a.v, a.tokens, ptc::KVH, 1, ptc::BN))
+    return PVLC_CUDA_ERROR;
+  ptc::Params p;
+  p.rope_cos = a.rope_cos;
+  p.rope_sin = a.rope_sin;
+  p.rope_rows = a.rope_rows;
+  p.tokens = a.tokens;
+  p.k_cache = reinterpret_cast<__half*>(a.k_cache);
+  p.v_cache = reinterpret_cast<__half*>(a.v_cache);
+  p.out = reinterpret_cast<__half*>(a.out);
+  const uint32_t n_pairs = (a.tokens + ptc::QT * ptc::TOK - 1) / (ptc::QT * ptc::TOK);
+  if (n_pairs > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
+  dim3 grid(ptc::KVH, n_pairs);
+  ptc::prefill_tc_kernel<<<grid, ptc::THREADS, ptc::SMEM_BYTES, stream>>>(maps, p);
+  return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
+}
+
+}  // namespace pvlc

@@ -66,7 +66,7 @@ int check_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_rows) {
   if (tokens == 0 || capacity == 0 || rope_rows == 0) return PVLC_ZERO_DIMENSION;
   if (tokens > capacity) return PVLC_CAPACITY_EXHAUSTED;
   if (tokens > rope_rows) return PVLC_INVALID_DECODER_GEOMETRY;
-  const uint64_t n_tiles = (tokens + 63) / 64;
+  const uint64_t n_tiles = (tokens + 31) / 32;
   if (n_tiles > 65535) return PVLC_INVALID_DECODER_GEOMETRY;
   return PVLC_OK;
 }
@@ -156,7 +156,7 @@ int pvlc_plan_vision_varlen(const uint32_t* cu, uint32_t segments, uint32_t toke
   plan->grid[0] = heads;
   plan->grid[1] = items;
   plan->grid[2] = 1;
-  plan->block[0] = 128;
+  plan->block[0] = 512;
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = items * heads;
   plan->output_elements = (uint64_t)tokens * heads * head_dim;
@@ -189,10 +189,10 @@ int pvlc_plan_decoder_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_
   if (!plan) return PVLC_NULL_POINTER;
   memset(plan, 0, sizeof(*plan));
   const uint32_t bm = (uint32_t)prefill_query_tile();
-  plan->grid[0] = PVLC_DECODER_QUERY_HEADS;
+  plan->grid[0] = PVLC_DECODER_KV_HEADS;   // one CTA per (KV group, 32-token block)
   plan->grid[1] = (tokens + bm - 1) / bm;
   plan->grid[2] = 1;
-  plan->block[0] = 128;
+  plan->block[0] = 512;
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = plan->grid[0] * plan->grid[1];
   plan->output_elements = (uint64_t)tokens * 16 * 128;
