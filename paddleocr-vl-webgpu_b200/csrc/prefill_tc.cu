@@ -1,7 +1,7 @@
 // prefill_tc.cu -- decoder causal GQA prefill (pinned Q16/KV2/D128) on the
-// Blackwell tensor cores (tcgen05 + TMEM + TMA) with the 3-section
-// multimodal RoPE fused into the Q/K tiles and the rotated key / raw value
-// written into the fp16 KV cache in place.  sm_100a.
+// Blackwell tensor cores (tcgen05 + TMEM + TMA), with the 3-section
+// multimodal RoPE applied to every key exactly once and the fp16 KV cache
+// written in place.  sm_100a.
 //
 // Reference path replaced: DecoderPrefillMropeF32 -> DecoderKvAppendRangeF32
 // -> DecoderPrefillGqaF32 (crates/pvlc-wgsl/src/lib.rs:1262-1416; stage order
@@ -9,21 +9,29 @@
 // crates/pvlc-cpu-ref/src/lib.rs:562-672 (M-RoPE), :976-991 (KV write),
 // :782-853 (causal GQA).
 //
+// Two launches on the caller's stream:
+//   1. kv_rope_kernel: M-RoPE of K fused with the KV-cache write -- each key
+//      row is rotated once and stored (with its raw value row) in the cache.
+//   2. prefill_attn_kernel: attention whose keys are TMA-loaded from that
+//      cache (already rotated) and whose Q M-RoPE is fused into the Q tile.
+// Rotating keys inside the attention CTAs instead would repeat the rotation
+// of every key tile in every query block that reads it (measured: 60 of
+// 100 us at T = 1564), while the cache row has to be written anyway.
+//
 // GQA packing: a Q tile is 16 tokens x the 8 query heads of one KV group =
 // 128 MMA rows (row r = token r/8, head r%8), loaded by one 3-D TMA box, so a
 // K/V tile of 128 keys serves all 8 heads.  One CTA = (KV head, two
 // consecutive 16-token blocks); its two Q tiles ping-pong on the MMA warp.
-// Causal: K tiles 0 .. last needed only, masking inside the tiles that cross
-// the diagonal.  head_dim 128 = two 64-dim blocks of 128-byte rows (128B
-// swizzle); QK = 8 x K16 steps (M128 N128), PV = 8 x K16 steps (M128 N128,
-// V as an MN-major operand spanning both blocks).
+// Causal: K tiles 0 .. diagonal only, masking inside tiles that cross it.
+// head_dim 128 = two 64-dim blocks of 128-byte rows (128B swizzle); QK = 8 x
+// K16 steps (M128 N128), PV = 8 x K16 steps (M128 N128, V MN-major across
+// both blocks), P from TMEM.
 //
-//   warp 12      TMA producer: both Q tiles, then K/V tiles (2-stage ring)
-//   warps 0-3    rotation: thread r rotates key row r of a staged K tile in
-//                place with M-RoPE, then writes the rotated key and raw value
-//                rows of this CTA's own tokens into the KV cache
-//   warps 4-11   softmax for Q tile 0 / 1: thread i owns row i = TMEM lane i
-//   warp 13      MMA issuer (one thread)
+//   warps 0-3, 4-7  softmax for Q tile 0 / 1: thread i owns row i = TMEM lane
+//                   i; rotates its Q row once (M-RoPE), then per K tile the
+//                   online softmax (f32, exp2 domain) and P (fp16) over S
+//   warp 8          TMA producer: both Q tiles, then K/V tiles (2 stages)
+//   warp 9          MMA issuer (one thread)
 // TMEM (512 columns): S/P of tile t at [128t, 128t+128), O at [256+128t, +128).
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -47,9 +55,10 @@ constexpr int GROUP = 8;
 constexpr int TOK = 16;          // tokens per Q tile (x 8 heads = 128 rows)
 constexpr int QT = 2;            // Q tiles per CTA
 constexpr int BN = 128;          // keys per K/V tile
-constexpr int THREADS = 16 * 32;
-constexpr uint32_t REGS_ROT = 96, REGS_SOFTMAX = 176, REGS_CTRL = 56;
-static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
+constexpr int THREADS = 12 * 32;
+// launch: 384 threads x 168 registers; softmax warpgroups take 200, control 56
+constexpr uint32_t REGS_SOFTMAX = 200, REGS_CTRL = 56;
+static_assert(256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 384 * 168, "register split");
 
 constexpr uint32_t SZ_W = 128 * 128;          // 128 rows x 64 dims fp16, 128B swizzle
 constexpr uint32_t Q_BYTES = 2 * SZ_W;        // two 64-dim blocks
@@ -59,8 +68,8 @@ constexpr uint32_t ST_K = 0, ST_V = 2 * SZ_W;
 constexpr uint32_t STAGE_BYTES = 4 * SZ_W;
 constexpr int STAGES = 2;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
-// q_full, q_ready, kv_full[2], k_rot[2], kv_empty[2], s_full[2], p_ready[2], o_done[2]
-constexpr int NBARS = 14;
+// q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2]
+constexpr int NBARS = 12;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "prefill shared memory exceeds the sm_100 limit");
@@ -68,7 +77,7 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 struct Maps {
-  CUtensorMap q, k, v;
+  CUtensorMap q, k, v;   // k maps the KV cache (rotated keys), v the raw values
 };
 
 struct Params {
@@ -76,24 +85,66 @@ struct Params {
   const float* rope_sin;
   uint32_t rope_rows;
   uint32_t tokens;
-  __half* k_cache;        // [capacity, 2, 128]
-  __half* v_cache;
   __half* out;            // [T, 16, 128]
 };
 
+// ------------------------------------------------------------------------
+// 1. M-RoPE of the keys fused with the KV-cache write.  Thread = (token, KV
+// head, chunk c): dims 8c..8c+7 and their partners 64+8c..64+8c+7.  Dim d of
+// a 128-wide head takes table plane 0/1/2 for (d mod 64) in [0,16)/[16,40)/
+// [40,64); d < 64 becomes x[d] cos[d] - x[d+64] sin[d] and d+64 becomes
+// x[d+64] cos[d+64] + x[d] sin[d+64] (crates/pvlc-cpu-ref/src/lib.rs:645-668).
+__global__ void __launch_bounds__(256) kv_rope_kernel(const __half* __restrict__ k,
+                                                      const __half* __restrict__ v,
+                                                      const float* __restrict__ rope_cos,
+                                                      const float* __restrict__ rope_sin,
+                                                      uint32_t rope_rows, uint32_t tokens,
+                                                      __half* __restrict__ k_cache,
+                                                      __half* __restrict__ v_cache) {
+  const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t c = gid & 7, head = (gid >> 3) & 1, token = gid >> 4;
+  if (token >= tokens) return;
+  const size_t row = ((size_t)token * KVH + head) * HD;
+  const size_t tb = ((size_t)mrope_axis(8 * c) * rope_rows + token) * HD + 8 * c;
+  const float4* cs = reinterpret_cast<const float4*>(rope_cos + tb);
+  const float4* sn = reinterpret_cast<const float4*>(rope_sin + tb);
+  const float4 cl0 = __ldg(cs), cl1 = __ldg(cs + 1), ch0 = __ldg(cs + 16), ch1 = __ldg(cs + 17);
+  const float4 sl0 = __ldg(sn), sl1 = __ldg(sn + 1), sh0 = __ldg(sn + 16), sh1 = __ldg(sn + 17);
+  const uint4 a = *reinterpret_cast<const uint4*>(k + row + 8 * c);
+  const uint4 b = *reinterpret_cast<const uint4*>(k + row + 64 + 8 * c);
+  const float cl[8] = {cl0.x, cl0.y, cl0.z, cl0.w, cl1.x, cl1.y, cl1.z, cl1.w};
+  const float chh[8] = {ch0.x, ch0.y, ch0.z, ch0.w, ch1.x, ch1.y, ch1.z, ch1.w};
+  const float sl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
+  const float shh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+  uint32_t ra[4], rb[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&aw[e]));
+    const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&bw[e]));
+    ra[e] = pack_half2(x.x * cl[2 * e] + (-y.x) * sl[2 * e], x.y * cl[2 * e + 1] + (-y.y) * sl[2 * e + 1]);
+    rb[e] = pack_half2(y.x * chh[2 * e] + x.x * shh[2 * e], y.y * chh[2 * e + 1] + x.y * shh[2 * e + 1]);
+  }
+  *reinterpret_cast<uint4*>(k_cache + row + 8 * c) = make_uint4(ra[0], ra[1], ra[2], ra[3]);
+  *reinterpret_cast<uint4*>(k_cache + row + 64 + 8 * c) = make_uint4(rb[0], rb[1], rb[2], rb[3]);
+  *reinterpret_cast<uint4*>(v_cache + row + 8 * c) =
+      *reinterpret_cast<const uint4*>(v + row + 8 * c);
+  *reinterpret_cast<uint4*>(v_cache + row + 64 + 8 * c) =
+      *reinterpret_cast<const uint4*>(v + row + 64 + 8 * c);
+}
+
+// ------------------------------------------------------------------------
+// 2. Attention.
 __device__ __forceinline__ uint8_t* chunk_addr(uint8_t* blk, int r, int c) {
   return blk + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-// M-RoPE of one 128-dim row held in two 128B-swizzled 64-dim blocks, in
-// place (crates/pvlc-cpu-ref/src/lib.rs:645-668): dim d < 64 becomes
-// x[d] cos[d] - x[d+64] sin[d], dim d+64 becomes x[d+64] cos[d+64] + x[d] sin[d+64];
-// cos/sin come from axis plane 0/1/2 for (d mod 64) in [0,16)/[16,40)/[40,64).
+// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in place.
 __device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const Params& p,
                                           uint32_t token) {
 #pragma unroll 2
-  for (int c = 0; c < 8; ++c) {          // dims 8c..8c+7 and 64+8c..64+8c+7
-    const uint32_t axis = mrope_axis(8 * c);   // sections are multiples of 8
+  for (int c = 0; c < 8; ++c) {
+    const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
     const size_t tb = ((size_t)axis * p.rope_rows + token) * HD + 8 * c;
     const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + tb);
     const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + tb);
@@ -127,7 +178,7 @@ __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-    prefill_tc_kernel(const __grid_constant__ Maps maps, const Params p) {
+    prefill_attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -135,11 +186,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* q_ready = bars + 1;
   uint64_t* kv_full = bars + 2;    // [2]
-  uint64_t* k_rot = bars + 4;      // [2]
-  uint64_t* kv_empty = bars + 6;   // [2]
-  uint64_t* s_full = bars + 8;     // [2]
-  uint64_t* p_ready = bars + 10;   // [2]
-  uint64_t* o_done = bars + 12;    // [2]
+  uint64_t* kv_empty = bars + 4;   // [2]
+  uint64_t* s_full = bars + 6;     // [2]
+  uint64_t* p_ready = bars + 8;    // [2]
+  uint64_t* o_done = bars + 10;    // [2]
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -156,7 +206,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(q_ready, 8);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&k_rot[s], 4);
       mbar_init(&kv_empty[s], 1);
     }
     for (int t = 0; t < QT; ++t) {
@@ -167,7 +216,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     misc[1] = 0;
     fence_mbar_init();
   }
-  if (warp == 12) {
+  if (warp == 8) {
     tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -177,9 +226,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = misc[0];
 
   const int wg = warp >> 2;
-  if (wg == 3) {
+  if (wg == 2) {
     tc::regs_dec<REGS_CTRL>();
-    if (warp == 12 && lane == 0) {
+    if (warp == 8 && lane == 0) {
       // ---------------------------------------------------- TMA producer
       tc::tma_prefetch_desc(&maps.q);
       tc::tma_prefetch_desc(&maps.k);
@@ -203,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
-    } else if (warp == 13 && lane == 0) {
+    } else if (warp == 9 && lane == 0) {
       // ---------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
@@ -231,7 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
         tc::commit(&o_done[t]);
       };
-      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&kv_full[0], 0);
       int done = 0;
       if (ok) {
         tc::fence_after_sync();
@@ -245,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             pv(t, s, j == 0);
             if (t == ntile - 1) tc::commit(&kv_empty[s]);
             if (more) {
-              if (t == 0 && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+              if (t == 0 && !mbar_wait(&kv_full[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
               tc::fence_after_sync();
               qk(t, s1);
             }
@@ -260,39 +309,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
       }
     }
-  } else if (wg == 0) {
-    tc::regs_dec<REGS_ROT>();
-    // ------------------------------------------------------ K rotation + cache write
-    const int r = tid;
-    const uint32_t own0 = tok0, own1 = umin32(tok0 + QT * TOK, p.tokens);  // tokens this CTA owns
-    for (int j = 0; j < nk; ++j) {
-      const int s = j % STAGES;
-      if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
-      uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-      const uint32_t token = j * BN + r;
-      if (token < p.tokens) {
-        mrope_row(st + ST_K, st + ST_K + SZ_W, r, p, token);
-        if (token >= own0 && token < own1) {
-          // in-place cache write of this token's rotated key and raw value
-          uint4* kd = reinterpret_cast<uint4*>(p.k_cache + ((size_t)token * KVH + g) * HD);
-          uint4* vd = reinterpret_cast<uint4*>(p.v_cache + ((size_t)token * KVH + g) * HD);
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int b = c >> 3, cc = c & 7;
-            kd[c] = *reinterpret_cast<const uint4*>(chunk_addr(st + ST_K + b * SZ_W, r, cc));
-            vd[c] = *reinterpret_cast<const uint4*>(chunk_addr(st + ST_V + b * SZ_W, r, cc));
-          }
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&k_rot[s]);
-    }
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
     // ------------------------------------------------------ softmax
-    const int t = wg - 1;
-    const int i = tid - 128 - 128 * t;               // row == TMEM lane
+    const int t = wg;
+    const int i = tid - 128 * t;                     // row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128u * t;
     const uint32_t tO = tmem + lane_base + 256u + 128u * t;
@@ -317,7 +338,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t scale2 = f2_pack(scale, scale);
       float m_run = -CUDART_INF_F, l_run = 0.f;
       bool good = __all_sync(0xffffffffu, ok);
-      // first token of this warp's rows: rows 32w'..32w'+31 cover tokens +4w'..+4w'+3
+      // rows 32w'..32w'+31 of this warp hold tokens +4w' .. +4w'+3
       const uint32_t warp_tok_lo = tok0 + t * TOK + ((warp & 3) * 32 >> 3);
       for (int j = 0; j < nk && good; ++j) {
         if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], j & 1))) {
@@ -331,7 +352,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tmem_ld32(tS + 64, sv + 64);
         tc::tmem_ld32(tS + 96, sv + 96);
         tc::tmem_wait_ld();
-        // causal mask where this tile reaches past the warp's first token
+        // causal mask where this tile reaches past the warp's first token;
+        // it also removes cache rows past the prompt (unwritten, any bits)
         if (j * BN + BN - 1 > warp_tok_lo) {
 #pragma unroll
           for (int c = 0; c < 128; ++c)
@@ -362,8 +384,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_st16(tO + cc, ov);
           }
         }
-        // rows whose every key so far is masked keep m_run = -inf: use 0 so
-        // that exp2(-inf - 0) = 0 rather than NaN
+        // a row can only be fully masked before its first key (never here:
+        // key 0 <= every token); guard the subtraction anyway
         const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
         const uint64_t negm2 = f2_pack(-mm, -mm);
         uint64_t sum2 = f2_pack(0.f, 0.f);
@@ -416,7 +438,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 8) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -441,15 +463,15 @@ EncodeTiled encoder() {
   return fn;
 }
 
-// [tokens, heads, 128] fp16 as a 3-D tensor {128, heads, tokens}; box
-// {64 dims, box_heads, box_tokens}, 128B swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
-              uint32_t box_heads, uint32_t box_tokens) {
+// [rows, heads, 128] fp16 as a 3-D tensor {128, heads, rows}; box
+// {64 dims, box_heads, box_rows}, 128B swizzle.
+bool make_map(CUtensorMap* m, const void* base, uint32_t rows, uint32_t heads,
+              uint32_t box_heads, uint32_t box_rows) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
-  const cuuint64_t dims[3] = {HD, heads, tokens};
+  const cuuint64_t dims[3] = {HD, heads, rows};
   const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)heads * HD * 2};
-  const cuuint32_t box[3] = {64, box_heads, box_tokens};
+  const cuuint32_t box[3] = {64, box_heads, box_rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -465,28 +487,34 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
   if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(ptc::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(ptc::prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ptc::SMEM_BYTES) != cudaSuccess)
       return PVLC_CUDA_ERROR;
     attr_set[dev] = true;
   }
   ptc::Maps maps;
+  // keys come from the cache (rotated by kv_rope_kernel); only rows < tokens
+  // are read as valid keys, rows past the cache capacity are TMA zero-fill
   if (!ptc::make_map(&maps.q, a.q, a.tokens, ptc::QH, ptc::GROUP, ptc::TOK) ||
-      !ptc::make_map(&maps.k, a.k, a.tokens, ptc::KVH, 1, ptc::BN) ||
+      !ptc::make_map(&maps.k, a.k_cache, a.capacity, ptc::KVH, 1, ptc::BN) ||
       !ptc::make_map(&maps.v, a.v, a.tokens, ptc::KVH, 1, ptc::BN))
     return PVLC_CUDA_ERROR;
+  const uint32_t n_pairs = (a.tokens + ptc::QT * ptc::TOK - 1) / (ptc::QT * ptc::TOK);
+  if (n_pairs > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
+  const uint32_t rope_threads = a.tokens * ptc::KVH * 8;
+  ptc::kv_rope_kernel<<<(rope_threads + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(a.k), reinterpret_cast<const __half*>(a.v), a.rope_cos,
+      a.rope_sin, a.rope_rows, a.tokens, reinterpret_cast<__half*>(a.k_cache),
+      reinterpret_cast<__half*>(a.v_cache));
+  if (cudaPeekAtLastError() != cudaSuccess) return PVLC_CUDA_ERROR;
   ptc::Params p;
   p.rope_cos = a.rope_cos;
   p.rope_sin = a.rope_sin;
   p.rope_rows = a.rope_rows;
   p.tokens = a.tokens;
-  p.k_cache = reinterpret_cast<__half*>(a.k_cache);
-  p.v_cache = reinterpret_cast<__half*>(a.v_cache);
   p.out = reinterpret_cast<__half*>(a.out);
-  const uint32_t n_pairs = (a.tokens + ptc::QT * ptc::TOK - 1) / (ptc::QT * ptc::TOK);
-  if (n_pairs > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
   dim3 grid(ptc::KVH, n_pairs);
-  ptc::prefill_tc_kernel<<<grid, ptc::THREADS, ptc::SMEM_BYTES, stream>>>(maps, p);
+  ptc::prefill_attn_kernel<<<grid, ptc::THREADS, ptc::SMEM_BYTES, stream>>>(maps, p);
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 

@@ -214,7 +214,7 @@ int pvlc_attn_decoder_prefill(const pvlc_half* q, const pvlc_half* k, const pvlc
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(rope_cos) ||
       !aligned16(rope_sin) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return PVLC_MISALIGNED_POINTER;
-  PrefillArgs a{q, k, v, rope_cos, rope_sin, rope_rows, tokens, k_cache, v_cache, out};
+  PrefillArgs a{q, k, v, rope_cos, rope_sin, rope_rows, tokens, capacity, k_cache, v_cache, out};
   return prefill_launch(a, static_cast<cudaStream_t>(stream));
 }
 

@@ -62,6 +62,7 @@ struct PrefillArgs {
   const float* rope_sin;
   uint32_t rope_rows;
   uint32_t tokens;
+  uint32_t capacity;
   pvlc_half* k_cache;
   pvlc_half* v_cache;
   pvlc_half* out;
