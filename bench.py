@@ -319,7 +319,7 @@ def run_components(args, dev, tf_peak, peak_src):
                                           "peak": tf_peak, "unit": "TFLOP/s",
                                           "frac": round(tf / tf_peak, 4),
                                           "peak_source": peak_src},
-                             "kernel": "pvlc::vision::vision_mma_kernel"}
+                             "kernel": "pvlc::vtc::vision_tc_kernel"}
 
     # decoder causal prefill, configs[2]
     ids = [7] * 19 + [101305] + [100295] * 1480 + [9] * 64
@@ -349,7 +349,7 @@ def run_components(args, dev, tf_peak, peak_src):
                                            "peak": tf_peak, "unit": "TFLOP/s",
                                            "frac": round(tf / tf_peak, 4),
                                            "peak_source": peak_src},
-                              "kernel": "pvlc::prefill::prefill_mma_kernel"}
+                              "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
     return res
 
 
@@ -432,13 +432,12 @@ def main():
         line = run_reference(args, rank)
     else:
         if world > 1:
-            import datetime
-
             import torch
             import torch.distributed as tdist
+
+            from pvlc_b200 import dist as pdist
             torch.cuda.set_device(local_rank)
-            tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                     device_id=torch.device("cuda", local_rank))
+            pdist.init("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
             dist = tdist
         line = run_gpu(args, rank, world, local_rank, dist)
         if dist is not None:
