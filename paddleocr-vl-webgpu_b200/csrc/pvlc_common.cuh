@@ -210,6 +210,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// Packed half-precision 2^x (one MUFU operation for two values).
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 // Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

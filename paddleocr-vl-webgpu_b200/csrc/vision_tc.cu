@@ -81,6 +81,11 @@ static_assert(SMEM_BYTES <= 227 * 1024, "vision shared memory exceeds the sm_100
 static_assert(STAGE_BYTES % 1024 == 0 && Q_BYTES % 1024 == 0, "swizzle atoms need 1 KB alignment");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;             // log2 units
+// V's dims 72..79 are padding (TMA zero fill).  Dim 72 is set to 1.0 in every
+// staged V tile, so the PV MMA accumulates the softmax row sum of the exact
+// fp16 P into O column 72 -- rescaled together with O -- and the softmax
+// needs no per-element sum.
+constexpr int SUM_COL = 72;
 
 struct Sched {
   uint32_t n_segments;
@@ -349,6 +354,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
       uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
       if (rope && j * BN + r < seglen) rotate_row_regs(st + ST_K0, st + ST_K1, r, tab);
+      // row-sum column: V row r, dims 72..79 (chunk 1 of the second 64-dim block) = {1, 0 x 7}
+      *reinterpret_cast<uint4*>(st + ST_V1 + r * 128 + ((1 ^ (r & 7)) << 4)) =
+          make_uint4(0x3C00u, 0u, 0u, 0u);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&k_rot[s]);
@@ -384,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (active) {
       const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
       const uint64_t scale2 = f2_pack(scale, scale);
-      float m_run = -CUDART_INF_F, l_run = 0.f;
+      float m_run = -CUDART_INF_F;   // running max (the row sum lives in O[:, 72])
       bool good = __all_sync(0xffffffffu, ok);
       for (int j = 0; j < nk && good; ++j) {
         // warp-uniform control flow around the collective tcgen05.ld / .st
@@ -416,7 +424,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (need) {
           alpha = fast_exp2(m_run - mx);   // 0 on the first tile
           m_run = mx;
-          l_run *= alpha;
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1))) { good = false; break; }
@@ -431,8 +438,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_st16(tO + cc, ov);
           }
         }
+        // P = 2^(x - m) as fp16 pairs: scale and shift in f32, round the
+        // exponent to fp16 and evaluate two exponentials per MUFU operation
         const uint64_t negm2 = f2_pack(-m_run, -m_run);
-        uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t pk[16];
@@ -440,15 +448,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < 16; ++c) {
             const int k = 32 * ch + 2 * c;
             const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
-            const float a = fast_exp2(x.x), b = fast_exp2(x.y);
-            sum2 = f2_add(sum2, f2_pack(a, b));
-            pk[c] = pack_half2(a, b);
+            pk[c] = ex2_h2(pack_half2(x.x, x.y));
           }
           tc::tmem_st16(tS + 16 * ch, pk);
         }
         tc::tmem_wait_st();
-        const float2 sum = f2_unpack(sum2);
-        l_run += sum.x + sum.y;
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[t]);
@@ -458,16 +462,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (__all_sync(0xffffffffu, good && mbar_wait(&o_done[t], (nk - 1) & 1))) {
         tc::fence_after_sync();
         const bool store = row < seg_end;
-        const float inv = 1.f / l_run;
         __half* orow = p.out + ((size_t)row * p.heads + head) * HD;
+        // columns 64..79 first: column 72 holds the row sum
+        uint32_t last[16];
+        tc::tmem_ld16(tO + 64, last);
+        tc::tmem_wait_ld();
+        const float inv = 1.f / __uint_as_float(last[SUM_COL - 64]);
 #pragma unroll
         for (int cc = 0; cc < 80; cc += 16) {
           uint32_t ov[16];
-          tc::tmem_ld16(tO + cc, ov);
-          tc::tmem_wait_ld();
+          if (cc < 64) {
+            tc::tmem_ld16(tO + cc, ov);
+            tc::tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) ov[e] = last[e];
+          }
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (cc + 8 * h >= HD) break;   // columns 72..79 are padding
+            if (cc + 8 * h >= HD) break;   // columns 72..79: row sum and padding
             uint4 v;
             v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
             v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
