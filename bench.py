@@ -268,16 +268,13 @@ def run_gpu(args, rank, world, local_rank, dist):
     return line
 
 
-def run_components(args, dev, tf_peak, peak_src):
-    import numpy as np
+def run_components(args, dev, tf_peak, peak_src, which=("vision", "prefill"), iters=20, warm=3):
     import torch
-
-    from pvlc_b200 import ops, positions
 
     res = {}
     stream = torch.cuda.current_stream()
 
-    def timeit(fn, iters, warm=3):
+    def timeit(fn):
         for _ in range(warm):
             fn()
         torch.cuda.synchronize()
@@ -290,7 +287,18 @@ def run_components(args, dev, tf_peak, peak_src):
         torch.cuda.synchronize()
         return statistics.mean(a.elapsed_time(b) for a, b in evs)
 
-    # vision varlen prefill, configs[1]
+    if "vision" in which:
+        res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src)
+    if "prefill" in which:
+        res["decoder_prefill"] = bench_prefill(dev, timeit, tf_peak, peak_src)
+    return res
+
+
+def bench_vision(dev, timeit, tf_peak, peak_src):
+    """Vision varlen prefill, configs[1]."""
+    import torch
+
+    from pvlc_b200 import ops, positions
     grids = [(1, 32, 32), (1, 48, 48), (1, 24, 24), (1, 64, 64)]
     cu = [0, 1024, 3328, 3904, 8000]
     T = 8000
@@ -310,18 +318,25 @@ def run_components(args, dev, tf_peak, peak_src):
         it[0] += 1
         ops.vision_varlen_attention(qs[i], ks[i], vs[i], cu, vcos, vsin, out=vout)
 
-    ms = timeit(vis, 20)
+    ms = timeit(vis)
     flops = 4.0 * 72 * 16 * sum((cu[i + 1] - cu[i]) ** 2 for i in range(4))
     tf = flops / (ms * 1e-3) / 1e12
-    res["vision_prefill"] = {"workload": "configs[1] 8000 tokens, segments 1024/2304/576/4096, H16 D72, 2-D RoPE",
-                             "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
-                             "roofline": {"bound": "tensor", "achieved": round(tf, 2),
-                                          "peak": tf_peak, "unit": "TFLOP/s",
-                                          "frac": round(tf / tf_peak, 4),
-                                          "peak_source": peak_src},
-                             "kernel": "pvlc::vtc::vision_tc_kernel"}
+    return {"workload": "configs[1] 8000 tokens, segments 1024/2304/576/4096, H16 D72, 2-D RoPE",
+            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                         "peak_source": peak_src},
+            "kernel": "pvlc::vtc::vision_tc_kernel"}
 
-    # decoder causal prefill, configs[2]
+
+def bench_prefill(dev, timeit, tf_peak, peak_src):
+    """Decoder causal prefill, configs[2]."""
+    import torch
+
+    from pvlc_b200 import ops, positions
+    nrot = 8
+    it = [0]
+    g = torch.Generator(device=dev)
     ids = [7] * 19 + [101305] + [100295] * 1480 + [9] * 64
     pos, delta = positions.mrope_position_ids(ids, [(1, 80, 74)])
     Tp = len(ids)
@@ -340,17 +355,15 @@ def run_components(args, dev, tf_peak, peak_src):
         it[0] += 1
         ops.decoder_prefill(pq[i], pk[i], pv[i], pcos, psin, kcache, vcache, out=pout)
 
-    ms = timeit(pre, 20)
+    ms = timeit(pre)
     flops = 4.0 * 128 * 16 * Tp * (Tp + 1) / 2
     tf = flops / (ms * 1e-3) / 1e12
-    res["decoder_prefill"] = {"workload": "configs[2] T=1564 (20 text + 40x37 image + 64 text), Q16/KV2/D128, M-RoPE",
-                              "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
-                              "roofline": {"bound": "tensor", "achieved": round(tf, 2),
-                                           "peak": tf_peak, "unit": "TFLOP/s",
-                                           "frac": round(tf / tf_peak, 4),
-                                           "peak_source": peak_src},
-                              "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
-    return res
+    return {"workload": "configs[2] T=1564 (20 text + 40x37 image + 64 text), Q16/KV2/D128, M-RoPE",
+            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                         "peak_source": peak_src},
+            "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
 
 
 # --------------------------------------------------------------- CPU (oracle)
@@ -418,6 +431,8 @@ def main():
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (profiling runs use a smaller case)")
     ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--only", choices=["vision", "prefill"], default=None,
+                    help="time one prefill component alone (profiling runs); prints its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.seqs != SEQS_PER_GPU or args.layers != LAYERS:
@@ -428,6 +443,13 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
+    if args.only is not None and args.impl == "ours":
+        import torch
+        hbm_peak, tf_peak, peak_src = peaks()
+        res = run_components(args, torch.device("cuda", 0), tf_peak, peak_src,
+                             which=(args.only,), iters=args.steps, warm=args.warmup)
+        print(json.dumps(res), flush=True)
+        return
     if args.impl == "reference":
         line = run_reference(args, rank)
     else:

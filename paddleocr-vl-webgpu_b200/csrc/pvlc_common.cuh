@@ -217,6 +217,40 @@ __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
   return y;
 }
 
+// 2^x for a pair of f32 exponents, returned as fp16x2 bits, computed on the
+// FMA and integer pipes only (no MUFU, no f32 -> f16 conversion), so that a
+// kernel can split its exponentials between this and ex2_h2.  The argument is
+// xh = x - 0.5 (callers fold the 0.5 into their shift).
+//   j = round-to-nearest(xh) = floor(x), via the 1.5 * 2^23 rounding constant;
+//   g = xh - j in [-0.5, 0.5];
+//   2^(g + 0.5) by a degree-3 minimax polynomial (relative error 7.5e-5 on
+//   [-0.5, 0.5], Remez exchange), evaluated scaled by 1024 with
+//   2^23 + 15 * 1024 - 1024 added, so the last fused multiply-add rounds the
+//   10-bit fp16 mantissa (plus the exponent bias 15 << 10) into the low bits
+//   of its f32 result; a carry out of the mantissa bumps the exponent, as it
+//   should.  The fp16 exponent j is then added as an integer (j << 10).
+// Results are within one fp16 ulp of 2^x for x >= -14; x <= -15 (and -inf)
+// gives exactly 0 and x in (-15, -14) a value below 2^-14.
+__device__ __forceinline__ uint32_t exp2_h2_poly(uint64_t xh2) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float kA3 = 79.89711f, kA2 = 351.33844f, kA1 = 1003.94916f, kA0 = 8404392.f;
+  float2 xh = f2_unpack(xh2);
+  xh.x = fmaxf(xh.x, -15.5f);
+  xh.y = fmaxf(xh.y, -15.5f);
+  const uint64_t x2 = f2_pack(xh.x, xh.y);
+  const uint64_t t2 = f2_add(x2, f2_pack(kRound, kRound));
+  const uint64_t j2 = f2_add(t2, f2_pack(-kRound, -kRound));
+  const uint64_t g2 = f2_fma(j2, f2_pack(-1.f, -1.f), x2);
+  uint64_t q2 = f2_fma(f2_pack(kA3, kA3), g2, f2_pack(kA2, kA2));
+  q2 = f2_fma(q2, g2, f2_pack(kA1, kA1));
+  q2 = f2_fma(q2, g2, f2_pack(kA0, kA0));
+  uint32_t t0, t1, q0, q1;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t2));
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(q0), "=r"(q1) : "l"(q2));
+  // low 16 bits: (j << 10) + (15 << 10) + mantissa; the high halves are dropped
+  return __byte_perm(t0 * 1024u + q0, t1 * 1024u + q1, 0x5410);
+}
+
 // Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -38,6 +38,19 @@ __device__ __forceinline__ void fence_after_sync() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// True in exactly one lane of the (converged) warp.  A warp that runs an MMA
+// schedule together keeps its descriptors and loop state warp-uniform and
+// lets the elected lane issue each tcgen05 instruction.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
+
 // ------------------------------------------------------------- MMA issue
 // D(tmem) (+)= A(smem desc) * B(smem desc), fp16 inputs, f32 accumulate.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,

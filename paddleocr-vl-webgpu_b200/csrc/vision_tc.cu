@@ -59,7 +59,7 @@ constexpr int QT = 2;            // Q tiles per CTA
 constexpr int BN = 128;          // keys per K/V tile
 constexpr int THREADS = 16 * 32;  // 4 warpgroups: rotation, softmax 0, softmax 1, producer/MMA
 // Register split (setmaxnreg) against the 128 x 512 = 65536 registers of the launch.
-constexpr uint32_t REGS_ROT = 96, REGS_SOFTMAX = 176, REGS_CTRL = 56;
+constexpr uint32_t REGS_ROT = 120, REGS_SOFTMAX = 176, REGS_CTRL = 40;
 static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
 constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
 
@@ -86,6 +86,14 @@ constexpr float RESCALE_THRESHOLD = 8.0f;             // log2 units
 // fp16 P into O column 72 -- rescaled together with O -- and the softmax
 // needs no per-element sum.
 constexpr int SUM_COL = 72;
+// Pairs c (of each 16-pair chunk of a score row) whose exponentials run on the
+// FMA / integer pipes (exp2_h2_poly) instead of MUFU: the MUFU / conversion
+// pipe retires a quarter warp per cycle, so moving part of the work off it
+// shortens the exponential phase.
+#ifndef PVLC_VISION_EXP_POLY_MASK
+#define PVLC_VISION_EXP_POLY_MASK 0x4924u
+#endif
+constexpr uint32_t EXP_POLY_MASK = PVLC_VISION_EXP_POLY_MASK;
 
 struct Sched {
   uint32_t n_segments;
@@ -271,10 +279,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the last loads must land before the CTA may exit
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
-    } else if (warp == 13 && lane == 0) {
+    } else if (warp == 13) {
       // ---------------------------------------------------- MMA issuer
-      // Descriptors are built once; each K step only adds a constant to the
-      // start-address field (address >> 4 in the low bits).
+      // The whole warp walks the schedule, so descriptors and loop state stay
+      // warp-uniform; one elected lane issues each group of tcgen05.mma and
+      // the commit that tracks it.  Descriptors are built once; each K step
+      // only adds a constant to the start-address field (address >> 4 in the
+      // low bits).
       constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(128, 80, 0, 1);
       const int ntile = has1 ? 2 : 1;
@@ -292,36 +303,46 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto qk = [&](int t, int s) {
         const uint32_t tS = tmem + 128u * t;
         const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4), so = (uint64_t)s * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)   // 32 bytes (16 dims) per K step -> +2 in the address field
-          tc::mma_ss(tS, dq_w + qo + 2 * ks, dk_w + so + 2 * ks, idesc_qk, ks > 0);
-        tc::mma_ss(tS, dq_n + qo, dk_n + so, idesc_qk, 1);
-        tc::commit(&s_full[t]);
+          for (int ks = 0; ks < 4; ++ks)   // 32 bytes (16 dims) per K step -> +2 in the address field
+            tc::mma_ss(tS, dq_w + qo + 2 * ks, dk_w + so + 2 * ks, idesc_qk, ks > 0);
+          tc::mma_ss(tS, dq_n + qo, dk_n + so, idesc_qk, 1);
+          tc::commit(&s_full[t]);
+        }
+        __syncwarp();
       };
-      auto pv = [&](int t, int s, bool first) {
+      auto pv = [&](int t, int s, bool first, bool release) {
         const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
         const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)   // 16 keys = two 1 KB groups per K step -> +128
-          tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
-        tc::commit(&o_done[t]);
+          for (int ks = 0; ks < 8; ++ks)   // 16 keys = two 1 KB groups per K step -> +128
+            tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+          tc::commit(&o_done[t]);
+          if (release) tc::commit(&kv_empty[s]);   // the stage is free once every tile's PV is done
+        }
+        __syncwarp();
       };
-      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0);
+      constexpr uint32_t kAll = 0xffffffffu;
+      bool ok = __all_sync(kAll, mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0));
       int done = 0;   // K tiles whose PV was issued for every Q tile
       if (ok) {
         tc::fence_after_sync();
         for (int t = 0; t < ntile; ++t) qk(t, 0);
-        for (int j = 0; j < nk && ok && !misc[1]; ++j) {
+        for (int j = 0; j < nk && ok && !__any_sync(kAll, misc[1] != 0); ++j) {
           const bool more = j + 1 < nk;
           const int s = j % STAGES, s1 = (j + 1) % STAGES;
           for (int t = 0; t < ntile; ++t) {
-            if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
+            if (!__all_sync(kAll, mbar_wait(&p_ready[t], j & 1))) { ok = false; break; }
             tc::fence_after_sync();
-            pv(t, s, j == 0);
-            if (t == ntile - 1) tc::commit(&kv_empty[s]);
+            pv(t, s, j == 0, t == ntile - 1);
             if (more) {
               // only the next QK needs the next rotated K tile
-              if (t == 0 && !mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
+              if (t == 0 && !__all_sync(kAll, mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1))) {
+                ok = false;
+                break;
+              }
               tc::fence_after_sync();
               qk(t, s1);
             }
@@ -329,7 +350,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (ok) done = j + 1;
         }
       }
-      if (!ok) misc[1] = 1;
+      if (!ok && lane == 0) misc[1] = 1;
       // never exit with MMAs in flight or commit arrivals still pending
       if (done > 0) {
         for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
@@ -413,11 +434,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= kv) sv[c] = __float_as_uint(-CUDART_INF_F);
         }
-        float mx = __uint_as_float(sv[0]);
+        // row max over four independent chains
+        float m4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
+                       __uint_as_float(sv[3])};
 #pragma unroll
-        for (int c = 1; c < 127; c += 2)
-          mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
-        mx = fmaxf(mx, __uint_as_float(sv[127])) * scale;
+        for (int c = 4; c < 124; c += 8) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            m4[e] = fmax3(m4[e], __uint_as_float(sv[c + 2 * e]), __uint_as_float(sv[c + 2 * e + 1]));
+        }
+        m4[0] = fmax3(m4[0], __uint_as_float(sv[124]), __uint_as_float(sv[125]));
+        m4[1] = fmax3(m4[1], __uint_as_float(sv[126]), __uint_as_float(sv[127]));
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
         // move the running max only when it grew past the threshold
         const bool need = mx > m_run + RESCALE_THRESHOLD;
         float alpha = 1.f;
@@ -438,17 +466,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc::tmem_st16(tO + cc, ov);
           }
         }
-        // P = 2^(x - m) as fp16 pairs: scale and shift in f32, round the
-        // exponent to fp16 and evaluate two exponentials per MUFU operation
+        // P = 2^(x - m) as fp16 pairs, split between two pipes: the pairs of
+        // EXP_POLY_MASK by the polynomial on the FMA / integer pipes, the
+        // others by scaling in f32, rounding the exponent to fp16 and one
+        // MUFU operation per two values
         const uint64_t negm2 = f2_pack(-m_run, -m_run);
+        const uint64_t negmh2 = f2_pack(-m_run - 0.5f, -m_run - 0.5f);
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int k = 32 * ch + 2 * c;
-            const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
-            pk[c] = ex2_h2(pack_half2(x.x, x.y));
+            if ((EXP_POLY_MASK >> c) & 1u) {
+              pk[c] = exp2_h2_poly(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negmh2));
+            } else {
+              const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
+              pk[c] = ex2_h2(pack_half2(x.x, x.y));
+            }
           }
           tc::tmem_st16(tS + 16 * ch, pk);
         }
