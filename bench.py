@@ -23,7 +23,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -49,57 +48,72 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Reads NVML (the library behind nvidia-smi) from a thread every 2 ms, so
+    that a timed region of a few tens of milliseconds still gets samples;
+    read-only queries, no setting of the GPU is touched.  The NVML device is
+    found by the UUID of the CUDA device."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.rows = []
-        self.proc = None
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.sm, self.bits = [], 0
+        self.max_mhz = None
+        self.error = None
         self.thread = None
+        self.stop_flag = threading.Event()
+        self.nvml = None
+        self.handle = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = str(torch.cuda.get_device_properties(self.cuda_index).uuid)
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                    uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle,
+                                                                  pynvml.NVML_CLOCK_SM))
+        except Exception as e:   # noqa: BLE001 - reported in the JSON line
+            self.error = f"nvml unavailable: {type(e).__name__}"
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
+    def _run(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)))
+                self.bits |= int(get_reasons(self.handle))
+            except Exception as e:   # noqa: BLE001
+                self.error = f"nvml query failed: {type(e).__name__}"
+                return
+            time.sleep(self.period)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        self.stop_flag.set()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = sorted(n for b, n in self.REASONS.items() if self.bits & b)
+        res = {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+               "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.sm),
+               "source": "nvml"}
+        if self.error:
+            res["error"] = self.error
+        return res
 
 
 def algorithmic_decode_bytes(lengths_after_append):
@@ -275,17 +289,18 @@ def run_components(args, dev, tf_peak, peak_src, which=("vision", "prefill"), it
     stream = torch.cuda.current_stream()
 
     def timeit(fn):
+        # launches queued back to back: the device time per call, without the
+        # host's per-call launch preparation showing up as device idle time
         for _ in range(warm):
             fn()
         torch.cuda.synchronize()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(iters)]
-        for a, b in evs:
-            a.record(stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(iters):
             fn()
-            b.record(stream)
+        b.record(stream)
         torch.cuda.synchronize()
-        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return a.elapsed_time(b) / iters
 
     if "vision" in which:
         res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src)
@@ -311,12 +326,13 @@ def bench_vision(dev, timeit, tf_peak, peak_src):
     c_np, s_np = positions.vision_rope_tables(grids)
     vcos, vsin = torch.from_numpy(c_np).to(dev), torch.from_numpy(s_np).to(dev)
     vout = torch.empty_like(qs[0])
+    vws = torch.empty(ops.vision_workspace_bytes(T, 16), dtype=torch.uint8, device=dev)
     it = [0]
 
     def vis():
         i = it[0] % nrot
         it[0] += 1
-        ops.vision_varlen_attention(qs[i], ks[i], vs[i], cu, vcos, vsin, out=vout)
+        ops.vision_varlen_attention(qs[i], ks[i], vs[i], cu, vcos, vsin, out=vout, workspace=vws)
 
     ms = timeit(vis)
     flops = 4.0 * 72 * 16 * sum((cu[i + 1] - cu[i]) ** 2 for i in range(4))
@@ -326,7 +342,7 @@ def bench_vision(dev, timeit, tf_peak, peak_src):
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
                          "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
                          "peak_source": peak_src},
-            "kernel": "pvlc::vtc::vision_tc_kernel"}
+            "kernel": "pvlc::vtc::vision_rope_kernel + pvlc::vtc::vision_tc_kernel"}
 
 
 def bench_prefill(dev, timeit, tf_peak, peak_src):

@@ -91,12 +91,24 @@ int pvlc_attn_device_check(void);
  *   for no rotation.  Pair p of a head rotates dims (p, p + head_dim/2).
  * Attention never crosses a segment boundary; scale is 1/sqrt(head_dim).
  * head_dim must be 72 (the pinned vision head); heads <= 64.
+ * Like the reference's two passes, the rotated q and k go through a device
+ * scratch of pvlc_attn_vision_workspace_bytes: pvlc_attn_vision_varlen takes
+ * it from the stream-ordered allocator (cudaMallocAsync / cudaFreeAsync on
+ * `stream`), pvlc_attn_vision_varlen_ws from the caller (any 16-byte aligned
+ * buffer of at least that size; ignored, and may be NULL, without tables).
  */
 int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
                             const uint32_t* cu_seqlens_host, uint32_t segments,
                             uint32_t tokens, uint32_t heads, uint32_t head_dim,
                             const float* rope_cos, const float* rope_sin, pvlc_half* out,
                             void* stream);
+/* Scratch bytes of a vision call (0 when head_dim is not 72). */
+size_t pvlc_attn_vision_workspace_bytes(uint32_t tokens, uint32_t heads, uint32_t head_dim);
+int pvlc_attn_vision_varlen_ws(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                               const uint32_t* cu_seqlens_host, uint32_t segments,
+                               uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                               const float* rope_cos, const float* rope_sin, void* workspace,
+                               size_t workspace_bytes, pvlc_half* out, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Path 2: decoder causal GQA prefill with fused 3-section M-RoPE and in-place

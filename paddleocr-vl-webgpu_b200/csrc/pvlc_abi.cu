@@ -44,6 +44,32 @@ int sms_or_default() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The library's own stream-ordered memory pool of the current device, for the
+// scratch of the entry points that take none from the caller.  Memory freed
+// into it stays reserved (release threshold: unlimited), so back-to-back
+// calls reuse it instead of returning it to the driver at every synchronize;
+// the process's default pool is left untouched.
+cudaMemPool_t scratch_pool() {
+  static cudaMemPool_t pools[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) return nullptr;
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    pools[dev] = pool;
+  }
+  return pools[dev];
+}
+
 // crates/pvlc-runtime-core/src/lib.rs:443-478 (+ validate_sequence_boundaries
 // crates/pvlc-cpu-ref/src/lib.rs:3393-3405)
 int check_vision(const uint32_t* cu, uint32_t segments, uint32_t tokens, uint32_t heads,
@@ -156,20 +182,26 @@ int pvlc_plan_vision_varlen(const uint32_t* cu, uint32_t segments, uint32_t toke
   plan->grid[0] = heads;
   plan->grid[1] = items;
   plan->grid[2] = 1;
-  plan->block[0] = 512;
+  plan->block[0] = 384;
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = items * heads;
   plan->output_elements = (uint64_t)tokens * heads * head_dim;
   plan->output_bytes = plan->output_elements * 2;
+  plan->workspace_bytes = vision_workspace_bytes(tokens, heads);   // rotated q, k (with tables)
   plan->flops = 4.0 * head_dim * heads * sumsq;
   plan->hbm_bytes = 4.0 * plan->output_bytes + (double)tokens * head_dim * 4.0;  // q,k,v,o + tables
   return PVLC_OK;
 }
 
-int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
-                            const uint32_t* cu, uint32_t segments, uint32_t tokens, uint32_t heads,
-                            uint32_t head_dim, const float* rope_cos, const float* rope_sin,
-                            pvlc_half* out, void* stream) {
+size_t pvlc_attn_vision_workspace_bytes(uint32_t tokens, uint32_t heads, uint32_t head_dim) {
+  if (head_dim != 72) return 0;
+  return vision_workspace_bytes(tokens, heads);
+}
+
+static int vision_checks(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                         const uint32_t* cu, uint32_t segments, uint32_t tokens, uint32_t heads,
+                         uint32_t head_dim, const float* rope_cos, const float* rope_sin,
+                         const pvlc_half* out) {
   const int st = check_vision(cu, segments, tokens, heads, head_dim);
   if (st) return st;
   if (!q || !k || !v || !out) return PVLC_NULL_POINTER;
@@ -177,8 +209,48 @@ int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_h
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) ||
       (rope_cos && (!aligned16(rope_cos) || !aligned16(rope_sin))))
     return PVLC_MISALIGNED_POINTER;
+  return PVLC_OK;
+}
+
+int pvlc_attn_vision_varlen_ws(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                               const uint32_t* cu, uint32_t segments, uint32_t tokens,
+                               uint32_t heads, uint32_t head_dim, const float* rope_cos,
+                               const float* rope_sin, void* workspace, size_t workspace_bytes,
+                               pvlc_half* out, void* stream) {
+  const int st = vision_checks(q, k, v, cu, segments, tokens, heads, head_dim, rope_cos, rope_sin,
+                               out);
+  if (st) return st;
+  if (rope_cos) {
+    if (!workspace) return PVLC_NULL_POINTER;
+    if (!aligned16(workspace)) return PVLC_MISALIGNED_POINTER;
+    if (workspace_bytes < vision_workspace_bytes(tokens, heads)) return PVLC_WORKSPACE_TOO_SMALL;
+  }
   VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out};
-  return vision_launch(a, cu, segments, static_cast<cudaStream_t>(stream));
+  return vision_launch(a, cu, segments, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                            const uint32_t* cu, uint32_t segments, uint32_t tokens, uint32_t heads,
+                            uint32_t head_dim, const float* rope_cos, const float* rope_sin,
+                            pvlc_half* out, void* stream) {
+  const int st = vision_checks(q, k, v, cu, segments, tokens, heads, head_dim, rope_cos, rope_sin,
+                               out);
+  if (st) return st;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* ws = nullptr;
+  if (rope_cos) {
+    // stream-ordered scratch for the rotated q and k, released after the launch
+    cudaMemPool_t pool = scratch_pool();
+    if (!pool ||
+        cudaMallocFromPoolAsync(&ws, vision_workspace_bytes(tokens, heads), pool, s) != cudaSuccess) {
+      cudaGetLastError();
+      return PVLC_CUDA_ERROR;
+    }
+  }
+  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out};
+  const int rc = vision_launch(a, cu, segments, ws, s);
+  if (ws && cudaFreeAsync(ws, s) != cudaSuccess && rc == PVLC_OK) return PVLC_CUDA_ERROR;
+  return rc;
 }
 
 // ------------------------------------------------------------------ prefill

@@ -31,15 +31,6 @@ struct DecodeArgs {
 size_t decode_workspace_bytes(uint32_t batch, int num_sms);
 int decode_launch(const DecodeArgs& a, cudaStream_t stream);
 
-// Varlen vision schedule: work items (segment, 128-row query tile) sorted by
-// decreasing segment length so the longest tiles start first.
-constexpr int kVisionMaxItems = 1024;
-struct VisionSchedule {
-  uint32_t n_items;
-  uint32_t item_seg_start[kVisionMaxItems];  // first token of the item's segment
-  uint32_t item_seg_len[kVisionMaxItems];
-  uint32_t item_q0[kVisionMaxItems];         // first query token of the item
-};
 struct VisionArgs {
   const pvlc_half* q;
   const pvlc_half* k;
@@ -51,8 +42,12 @@ struct VisionArgs {
   pvlc_half* out;
 };
 int vision_query_tile();
+// Scratch for the rotated q and k (2 x tokens x heads x 72 fp16).
+size_t vision_workspace_bytes(uint32_t tokens, uint32_t heads);
+// workspace: vision_workspace_bytes of device memory when rope tables are
+// given (unused otherwise).
 int vision_launch(const VisionArgs& a, const uint32_t* cu_seqlens, uint32_t segments,
-                  cudaStream_t stream);
+                  void* workspace, cudaStream_t stream);
 
 struct PrefillArgs {
   const pvlc_half* q;

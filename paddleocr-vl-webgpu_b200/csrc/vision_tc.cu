@@ -1,6 +1,6 @@
 // vision_tc.cu -- vision-encoder bidirectional varlen attention on the
 // Blackwell tensor cores (tcgen05 + TMEM + TMA), head_dim 72, with the 2-D
-// RoPE fused into the Q/K tiles.  sm_100a.
+// RoPE.  sm_100a.
 //
 // Reference path replaced: VisionRope2dF16 followed by VisionAttentionF16
 // (crates/pvlc-wgsl/src/lib.rs:2309-2454,2553-2596; call site
@@ -8,32 +8,38 @@
 // crates/pvlc-cpu-ref/src/lib.rs:472-542 (rotation) and :2752-2878
 // (segmented attention).  A CTA only visits keys of its own segment.
 //
-// One CTA = one (segment, 256-query pair of tiles, head) work item, one CTA
-// per SM.  head_dim 72 never gets padded in HBM: TMA zero-fills the columns
-// past dim 72 as out-of-bounds.
+// Two launches, like the reference's two passes:
+//   vision_rope_kernel   rotates Q and K once into a scratch buffer
+//                        (HBM-bound elementwise pass).  Rotating inside the
+//                        attention kernel would repeat the rotation of every
+//                        K tile once per query tile pair of its segment.
+//   vision_tc_kernel     attention over the rotated Q and K.
+//
+// Attention: one CTA = one (segment, 256-query pair of tiles, head) work
+// item, one CTA per SM.  head_dim 72 never gets padded in HBM: TMA zero-fills
+// the columns past dim 72 as out-of-bounds.
 //   Q, K (MMA K dimension): a 64-dim block (128-byte rows, 128B swizzle) and
 //     a 16-dim block (32-byte rows, 32B swizzle) -> 4 + 1 MMAs of K = 16.
 //   V (MMA N dimension): two 64-dim blocks of 128-byte rows (the second one
 //     holds dims 64..71 and zeros) -> one N = 80 MMA per K step.
 //
-//   warp 12      TMA producer: both Q tiles once, then K/V tiles of 128 keys
+//   warp 8       TMA producer: both Q tiles once, then K/V tiles of 128 keys
 //                through a 3-stage ring
-//   warps 0-3    rotation: thread r rotates key row r of a staged K tile in
-//                place (2-D RoPE from the [T,36] tables); one rotation serves
-//                both Q tiles
-//   warps 4-7,   softmax for Q tile 0 / Q tile 1: thread i owns query row i =
-//   warps 8-11   TMEM lane i; rotates its Q row once; per K tile reads S from
-//                TMEM, online softmax in f32 (exp2 domain, packed f32x2 math),
-//                writes P (fp16) over S; the running max only moves (and O
-//                is rescaled in TMEM) when a row max grows by more than 8 in
-//                log2 units, so P stays <= 256 and the rescale is rare
-//   warp 13      MMA issuer (one thread), ping-pong over the two tiles:
+//   warp 9       MMA issuer (the whole warp walks the schedule, one elected
+//                lane issues), ping-pong over the two tiles:
 //                PV(t0, j), QK(t0, j+1), PV(t1, j), QK(t1, j+1), ... so the
 //                tensor pipe works on one tile while the other's softmax runs
+//   warps 10-11  write the row-sum column of every staged V tile
+//   warps 0-3,   softmax for Q tile 0 / Q tile 1: thread i owns query row i =
+//   warps 4-7    TMEM lane i; per K tile reads S from TMEM, online softmax in
+//                f32 (exp2 domain, packed f32x2 math), writes P (fp16) over
+//                S; the running max only moves (and O is rescaled in TMEM)
+//                when a row max grows by more than 8 in log2 units, so P
+//                stays <= 256 and the rescale is rare
 // TMEM (512 columns): S/P of tile t at [128t, 128t+128), O of tile t at
 // [256+128t, 256+128t+80).
-// setmaxnreg moves registers from the rotation and control warpgroups to the
-// two softmax warpgroups.
+// setmaxnreg moves registers from the control warpgroup to the two softmax
+// warpgroups.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -54,13 +60,18 @@ namespace vtc {
 
 constexpr int HD = 72;
 constexpr int PAIRS = 36;
-constexpr int BM = 128;          // rows per Q tile
-constexpr int QT = 2;            // Q tiles per CTA
-constexpr int BN = 128;          // keys per K/V tile
-constexpr int THREADS = 16 * 32;  // 4 warpgroups: rotation, softmax 0, softmax 1, producer/MMA
-// Register split (setmaxnreg) against the 128 x 512 = 65536 registers of the launch.
-constexpr uint32_t REGS_ROT = 120, REGS_SOFTMAX = 176, REGS_CTRL = 40;
-static_assert(128 * REGS_ROT + 256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 65536, "register split");
+constexpr int QUADS = PAIRS / 4;  // rotation pairs in groups of four (16 bytes of table)
+constexpr int BM = 128;           // rows per Q tile
+constexpr int QT = 2;             // Q tiles per CTA
+constexpr int BN = 128;           // keys per K/V tile
+constexpr int THREADS = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producer/MMA/row-sum
+constexpr int CTRL_WARP = 8;      // first warp of the control warpgroup
+// Register split (setmaxnreg) against the registers of the launch: 384
+// threads start with 168 each (65536 / 384 rounded down to the allocation
+// unit of 8).
+constexpr uint32_t REGS_LAUNCH = 168;
+constexpr uint32_t REGS_SOFTMAX = 208, REGS_CTRL = 88;
+static_assert(128 * (2 * REGS_SOFTMAX + REGS_CTRL) <= THREADS * REGS_LAUNCH, "register split");
 constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
 
 // shared memory map (offsets from a 1024-aligned base)
@@ -73,8 +84,8 @@ constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_W, ST_V0 = SZ_W + SZ_N, ST_V1 = 2 * SZ_
 constexpr uint32_t STAGE_BYTES = 3 * SZ_W + SZ_N;
 constexpr int STAGES = 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
-// q_full, q_ready, kv_full[3], k_rot[3], kv_empty[3], s_full[2], p_ready[2], o_done[2]
-constexpr int NBARS = 17;
+// q_full, kv_full[3], v_ready[3], kv_empty[3], s_full[2], p_ready[2], o_done[2]
+constexpr int NBARS = 16;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "vision shared memory exceeds the sm_100 limit");
@@ -107,86 +118,9 @@ struct Maps {
 };
 
 struct Params {
-  const float* rope_cos;  // [T, 36] or null
-  const float* rope_sin;
   __half* out;
   uint32_t heads;
-  uint32_t tokens;
 };
-
-// The 36 (cos, sin) table entries of one token, held in registers.
-struct RopeRow {
-  float4 c[PAIRS / 4], s[PAIRS / 4];
-};
-
-__device__ __forceinline__ void load_rope_row(RopeRow& t, const float* cs, const float* sn) {
-#pragma unroll
-  for (int j = 0; j < PAIRS / 4; ++j) {
-    t.c[j] = __ldg(reinterpret_cast<const float4*>(cs) + j);
-    t.s[j] = __ldg(reinterpret_cast<const float4*>(sn) + j);
-  }
-}
-
-// Element (row r, 16-byte chunk c) of a 72-dim row split into a 64-dim
-// 128B-swizzled block and a 16-dim 32B-swizzled block.
-__device__ __forceinline__ uint8_t* row_chunk(uint8_t* b0, uint8_t* b1, int r, int c) {
-  return c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4) : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
-}
-
-// Rotate one row in place with tables already in registers.  Quad j holds
-// pairs 4j..4j+3: dims 4j..4j+3 (8 bytes) and their partners 36+4j..39+4j.
-__device__ __forceinline__ void rotate_row_regs(uint8_t* b0, uint8_t* b1, int r, const RopeRow& t) {
-#pragma unroll
-  for (int j = 0; j < PAIRS / 4; ++j) {
-    uint2* lo = reinterpret_cast<uint2*>(row_chunk(b0, b1, r, j >> 1) + 8 * (j & 1));
-    uint2* hi = reinterpret_cast<uint2*>(row_chunk(b0, b1, r, (j + 9) >> 1) + 8 * ((j + 9) & 1));
-    const uint2 a = *lo, b = *hi;
-    const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
-    const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
-    const float2 b0v = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
-    const float2 b1v = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
-    const float4 c = t.c[j], s = t.s[j];
-    *lo = make_uint2(pack_half2(a0.x * c.x - b0v.x * s.x, a0.y * c.y - b0v.y * s.y),
-                     pack_half2(a1.x * c.z - b1v.x * s.z, a1.y * c.w - b1v.y * s.w));
-    *hi = make_uint2(pack_half2(b0v.x * c.x + a0.x * s.x, b0v.y * c.y + a0.y * s.y),
-                     pack_half2(b1v.x * c.z + a1.x * s.z, b1v.y * c.w + a1.y * s.w));
-  }
-}
-
-// Rotate one 72-dim row held in a (64-dim SW128, 16-dim SW32) pair of tiles,
-// in place.  Pair p rotates dims (p, p + 36) by table entry p.
-__device__ __forceinline__ void rotate_row(uint8_t* b0, uint8_t* b1, int r, const float* cs,
-                                           const float* sn) {
-  // w[k] holds dims (2k, 2k+1) as a half2; dims 72..79 of the row are padding
-  uint32_t w[36];
-#pragma unroll
-  for (int c = 0; c < 9; ++c) {
-    const uint8_t* src = c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4)
-                               : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
-    const uint4 v = *reinterpret_cast<const uint4*>(src);
-    w[4 * c] = v.x; w[4 * c + 1] = v.y; w[4 * c + 2] = v.z; w[4 * c + 3] = v.w;
-  }
-#pragma unroll
-  for (int j = 0; j < PAIRS / 4; ++j) {   // pairs 4j..4j+3: words 2j,2j+1 and 18+2j,18+2j+1
-    const float4 c = __ldg(reinterpret_cast<const float4*>(cs) + j);
-    const float4 s = __ldg(reinterpret_cast<const float4*>(sn) + j);
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float c0 = e ? c.z : c.x, c1 = e ? c.w : c.y;
-      const float s0 = e ? s.z : s.x, s1 = e ? s.w : s.y;
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * j + e]));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[18 + 2 * j + e]));
-      w[2 * j + e] = pack_half2(a.x * c0 - b.x * s0, a.y * c1 - b.y * s1);
-      w[18 + 2 * j + e] = pack_half2(b.x * c0 + a.x * s0, b.y * c1 + a.y * s1);
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < 9; ++c) {
-    uint8_t* dst = c < 8 ? b0 + r * 128 + ((c ^ (r & 7)) << 4)
-                         : b1 + r * 32 + ((0 ^ ((r >> 2) & 1)) << 4);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-  }
-}
 
 __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
   uint64_t r;
@@ -194,6 +128,47 @@ __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
   return r;
 }
 
+// ------------------------------------------------------------ 2-D RoPE pass
+// One thread per (token, head, quad of 4 rotation pairs): pair p rotates
+// dims (p, p + 36) of the head by table entry p of the token
+// (crates/pvlc-cpu-ref/src/lib.rs:472-542): x' = x cos - y sin,
+// y' = y cos + x sin in f32, rounded to fp16.  q and k share the table loads.
+// Consecutive threads touch consecutive 8-byte pieces of a row and
+// consecutive 16-byte table quads, so every access is coalesced (measured
+// faster than one thread per 144-byte row, whose 16-byte accesses stride by
+// a row).
+__global__ void __launch_bounds__(256)
+    vision_rope_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+                       const float* __restrict__ cs, const float* __restrict__ sn,
+                       __half* __restrict__ q_rot, __half* __restrict__ k_rot, uint32_t heads,
+                       uint64_t quads) {
+  const uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= quads) return;
+  const uint64_t row = g / QUADS;               // token * heads + head
+  const uint32_t quad = (uint32_t)(g - row * QUADS);
+  const uint64_t token = row / heads;
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cs + token * PAIRS) + quad);
+  const float4 s = __ldg(reinterpret_cast<const float4*>(sn + token * PAIRS) + quad);
+  const size_t lo = row * HD + 4 * quad, hi = lo + PAIRS;
+  auto rot = [&](const __half* src, __half* dst) {
+    const uint2 a = __ldg(reinterpret_cast<const uint2*>(src + lo));
+    const uint2 b = __ldg(reinterpret_cast<const uint2*>(src + hi));
+    const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
+    const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
+    const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
+    const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&b.y));
+    *reinterpret_cast<uint2*>(dst + lo) =
+        make_uint2(pack_half2(a0.x * c.x - b0.x * s.x, a0.y * c.y - b0.y * s.y),
+                   pack_half2(a1.x * c.z - b1.x * s.z, a1.y * c.w - b1.y * s.w));
+    *reinterpret_cast<uint2*>(dst + hi) =
+        make_uint2(pack_half2(b0.x * c.x + a0.x * s.x, b0.y * c.y + a0.y * s.y),
+                   pack_half2(b1.x * c.z + a1.x * s.z, b1.y * c.w + a1.y * s.w));
+  };
+  rot(q, q_rot);
+  rot(k, k_rot);
+}
+
+// --------------------------------------------------------------- attention
 __global__ void __launch_bounds__(THREADS, 1)
     vision_tc_kernel(const __grid_constant__ Maps maps, const Params p, const Sched sc) {
   extern __shared__ uint8_t smem_raw[];
@@ -201,13 +176,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
   uint64_t* q_full = bars + 0;
-  uint64_t* q_ready = bars + 1;
-  uint64_t* kv_full = bars + 2;    // [3]
-  uint64_t* k_rot = bars + 5;      // [3]
-  uint64_t* kv_empty = bars + 8;   // [3]
-  uint64_t* s_full = bars + 11;    // [2]
-  uint64_t* p_ready = bars + 13;   // [2]
-  uint64_t* o_done = bars + 15;    // [2]
+  uint64_t* kv_full = bars + 1;    // [3]
+  uint64_t* v_ready = bars + 4;    // [3] K/V landed and the row-sum column written
+  uint64_t* kv_empty = bars + 7;   // [3]
+  uint64_t* s_full = bars + 10;    // [2]
+  uint64_t* p_ready = bars + 12;   // [2]
+  uint64_t* o_done = bars + 14;    // [2]
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
   // misc[0]: TMEM base, misc[1]: abort
 
@@ -224,10 +198,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_ready, 8);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&k_rot[s], 4);
+      mbar_init(&v_ready[s], 2);     // the two row-sum warps
       mbar_init(&kv_empty[s], 1);
     }
     for (int t = 0; t < QT; ++t) {
@@ -238,7 +211,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     misc[1] = 0;
     fence_mbar_init();
   }
-  if (warp == 12) {
+  if (warp == CTRL_WARP) {
     tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
     tc::tmem_relinquish();
   }
@@ -250,9 +223,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   // Registers follow the work (softmax rows hold 128 scores each); each
   // warpgroup changes its budget at the head of its own branch.
   const int wg = warp >> 2;
-  if (wg == 3) {
+  if (wg == CTRL_WARP / 4) {
     tc::regs_dec<REGS_CTRL>();
-    if (warp == 12 && lane == 0) {
+    if (warp == CTRL_WARP && lane == 0) {
       // ---------------------------------------------------- TMA producer
       tc::tma_prefetch_desc(&maps.q0);
       tc::tma_prefetch_desc(&maps.k0);
@@ -279,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the last loads must land before the CTA may exit
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
-    } else if (warp == 13) {
+    } else if (warp == CTRL_WARP + 1) {
       // ---------------------------------------------------- MMA issuer
       // The whole warp walks the schedule, so descriptors and loop state stay
       // warp-uniform; one elected lane issues each group of tcgen05.mma and
@@ -325,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
       };
       constexpr uint32_t kAll = 0xffffffffu;
-      bool ok = __all_sync(kAll, mbar_wait(q_ready, 0) && mbar_wait(&k_rot[0], 0));
+      bool ok = __all_sync(kAll, mbar_wait(q_full, 0) && mbar_wait(&v_ready[0], 0));
       int done = 0;   // K tiles whose PV was issued for every Q tile
       if (ok) {
         tc::fence_after_sync();
@@ -335,17 +308,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int s = j % STAGES, s1 = (j + 1) % STAGES;
           for (int t = 0; t < ntile; ++t) {
             if (!__all_sync(kAll, mbar_wait(&p_ready[t], j & 1))) { ok = false; break; }
+            // the next QK needs the next K/V tile; checked before the PV
+            // issue so that PV and QK reach the tensor pipe back to back
+            if (more && t == 0 &&
+                !__all_sync(kAll, mbar_wait(&v_ready[s1], ((j + 1) / STAGES) & 1))) {
+              ok = false;
+              break;
+            }
             tc::fence_after_sync();
             pv(t, s, j == 0, t == ntile - 1);
-            if (more) {
-              // only the next QK needs the next rotated K tile
-              if (t == 0 && !__all_sync(kAll, mbar_wait(&k_rot[s1], ((j + 1) / STAGES) & 1))) {
-                ok = false;
-                break;
-              }
-              tc::fence_after_sync();
-              qk(t, s1);
-            }
+            if (more) qk(t, s1);
           }
           if (ok) done = j + 1;
         }
@@ -357,64 +329,39 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
           mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
       }
-    }
-  } else if (wg == 0) {
-    tc::regs_dec<REGS_ROT>();
-    // ------------------------------------------------------ K rotation
-    // Software-pipelined: the table row of the next tile is fetched right
-    // after the current tile is rotated, so its L2 latency overlaps the wait
-    // for the next K tile.
-    const int r = tid;  // key row of the tile
-    const bool rope = p.rope_cos != nullptr;
-    RopeRow tab;
-    if (rope && (uint32_t)r < seglen)
-      load_rope_row(tab, p.rope_cos + (size_t)(seg0 + r) * PAIRS,
-                    p.rope_sin + (size_t)(seg0 + r) * PAIRS);
-    for (int j = 0; j < nk; ++j) {
-      const int s = j % STAGES;
-      if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
-      uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
-      if (rope && j * BN + r < seglen) rotate_row_regs(st + ST_K0, st + ST_K1, r, tab);
-      // row-sum column: V row r, dims 72..79 (chunk 1 of the second 64-dim block) = {1, 0 x 7}
-      *reinterpret_cast<uint4*>(st + ST_V1 + r * 128 + ((1 ^ (r & 7)) << 4)) =
-          make_uint4(0x3C00u, 0u, 0u, 0u);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&k_rot[s]);
-      const uint32_t next = (j + 1) * BN + r;
-      if (rope && next < seglen)
-        load_rope_row(tab, p.rope_cos + (size_t)(seg0 + next) * PAIRS,
-                      p.rope_sin + (size_t)(seg0 + next) * PAIRS);
+    } else if (warp >= CTRL_WARP + 2) {
+      // ---------------------------------------------------- row-sum column
+      // V row r, dims 72..79 (chunk 1 of the second 64-dim block) = {1, 0 x 7}
+      const int u = tid - 32 * (CTRL_WARP + 2);   // 0..63: rows u and u + 64
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % STAGES;
+        if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
+        uint8_t* v1 = smem + OFF_STAGE + s * STAGE_BYTES + ST_V1;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = u + 64 * h;
+          *reinterpret_cast<uint4*>(v1 + r * 128 + ((1 ^ (r & 7)) << 4)) =
+              make_uint4(0x3C00u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&v_ready[s]);
+      }
     }
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
     // ------------------------------------------------------ softmax
-    const int t = wg - 1;                          // Q tile of this warpgroup
-    const int i = tid - 128 - 128 * t;             // query row == TMEM lane
+    const int t = wg;                              // Q tile of this warpgroup
+    const int i = tid - 128 * t;                   // query row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128u * t;
     const uint32_t tO = tmem + lane_base + 256u + 128u * t;
     const uint32_t row = q0 + t * BM + i;          // token of this query row
-    const bool active = t == 0 || has1;
-    bool ok = true;
-    if (active) {
-      ok = mbar_wait(q_full, 0);
-      if (ok && p.rope_cos && row < p.tokens) {
-        uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
-        rotate_row(qb, qb + SZ_W, i, p.rope_cos + (size_t)row * PAIRS,
-                   p.rope_sin + (size_t)row * PAIRS);
-      }
-      fence_proxy_async_smem();
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(q_ready);
-    if (!ok) misc[1] = 1;
-
-    if (active) {
+    if (t == 0 || has1) {
       const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
       const uint64_t scale2 = f2_pack(scale, scale);
       float m_run = -CUDART_INF_F;   // running max (the row sum lives in O[:, 72])
-      bool good = __all_sync(0xffffffffu, ok);
+      bool good = true;
       for (int j = 0; j < nk && good; ++j) {
         // warp-uniform control flow around the collective tcgen05.ld / .st
         if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], j & 1))) {
@@ -532,7 +479,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == CTRL_WARP) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -577,7 +524,11 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
 
 int vision_query_tile() { return vtc::QT * vtc::BM; }
 
-int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
+size_t vision_workspace_bytes(uint32_t tokens, uint32_t heads) {
+  return 2ull * tokens * heads * vtc::HD * sizeof(__half);
+}
+
+int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, void* workspace,
                   cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
@@ -588,11 +539,27 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
       return PVLC_CUDA_ERROR;
     attr_set[dev] = true;
   }
+  // rotated q and k (the scratch) or the inputs themselves when there is no RoPE
+  const void* qa = a.q;
+  const void* ka = a.k;
+  if (a.rope_cos != nullptr) {
+    __half* q_rot = static_cast<__half*>(workspace);
+    __half* k_rot = q_rot + (size_t)a.tokens * a.heads * vtc::HD;
+    const uint64_t quads = (uint64_t)a.tokens * a.heads * vtc::QUADS;
+    const uint64_t blocks = (quads + 255) / 256;
+    if (blocks > 0x7fffffffull) return PVLC_ARITHMETIC_OVERFLOW;
+    vtc::vision_rope_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
+        reinterpret_cast<const __half*>(a.q), reinterpret_cast<const __half*>(a.k), a.rope_cos,
+        a.rope_sin, q_rot, k_rot, a.heads, quads);
+    if (cudaPeekAtLastError() != cudaSuccess) return PVLC_CUDA_ERROR;
+    qa = q_rot;
+    ka = k_rot;
+  }
   vtc::Maps maps;
-  const bool ok = vtc::make_map(&maps.q0, a.q, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  vtc::make_map(&maps.q1, a.q, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
-                  vtc::make_map(&maps.k0, a.k, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  vtc::make_map(&maps.k1, a.k, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
+  const bool ok = vtc::make_map(&maps.q0, qa, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  vtc::make_map(&maps.q1, qa, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
+                  vtc::make_map(&maps.k0, ka, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+                  vtc::make_map(&maps.k1, ka, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
                   vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return PVLC_CUDA_ERROR;
   vtc::Sched sc;
@@ -613,11 +580,8 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments,
   sc.item_prefix[segments] = items;
   if (items > 65535u) return PVLC_INVALID_VISION_GEOMETRY;
   vtc::Params p;
-  p.rope_cos = a.rope_cos;
-  p.rope_sin = a.rope_sin;
   p.out = reinterpret_cast<__half*>(a.out);
   p.heads = a.heads;
-  p.tokens = a.tokens;
   dim3 grid(a.heads, items);
   vtc::vision_tc_kernel<<<grid, vtc::THREADS, vtc::SMEM_BYTES, stream>>>(maps, p, sc);
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;

@@ -66,6 +66,9 @@ _SIGNATURES = {
     "pvlc_attn_device_check": (ctypes.c_int, []),
     "pvlc_attn_vision_varlen": (ctypes.c_int, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _P, _P,
                                                _P, _P]),
+    "pvlc_attn_vision_workspace_bytes": (ctypes.c_size_t, [_U32, _U32, _U32]),
+    "pvlc_attn_vision_varlen_ws": (ctypes.c_int, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _P, _P,
+                                                  _P, ctypes.c_size_t, _P, _P]),
     "pvlc_attn_decoder_prefill": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _P,
                                                  _P, _P]),
     "pvlc_attn_decode_workspace_bytes": (ctypes.c_size_t, [_U32]),

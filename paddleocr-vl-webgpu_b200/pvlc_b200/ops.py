@@ -36,11 +36,19 @@ def _need(t, dtype, shape=None, name="tensor"):
         raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
 
 
-def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, out=None):
-    """Bidirectional block-diagonal attention over packed images with fused 2-D RoPE.
+def vision_workspace_bytes(tokens: int, heads: int, head_dim: int = VISION_HD) -> int:
+    """Device scratch of a vision call with rope tables (the rotated q and k)."""
+    return int(abi.lib().pvlc_attn_vision_workspace_bytes(tokens, heads, head_dim))
+
+
+def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, out=None,
+                            workspace=None):
+    """Bidirectional block-diagonal attention over packed images with the 2-D RoPE.
 
     q, k, v: [T, H, 72] fp16 CUDA; cu_seqlens: host sequence of segment boundaries;
-    rope_cos/rope_sin: [T, 36] f32 CUDA tables or None.  Returns [T, H, 72] fp16.
+    rope_cos/rope_sin: [T, 36] f32 CUDA tables or None; workspace: optional uint8
+    CUDA tensor of at least vision_workspace_bytes (taken from torch's allocator
+    when omitted).  Returns [T, H, 72] fp16.
     """
     T, H, D = q.shape
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -51,10 +59,18 @@ def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, o
     cu = np.ascontiguousarray(np.asarray(cu_seqlens, dtype=np.uint32))
     if out is None:
         out = torch.empty_like(q)
-    st = abi.lib().pvlc_attn_vision_varlen(
+    ws_bytes = 0
+    if rope_cos is not None:
+        ws_bytes = vision_workspace_bytes(T, H, D)
+        if workspace is None:
+            workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        _need(workspace, torch.uint8, None, "workspace")
+        ws_bytes = workspace.numel()
+    st = abi.lib().pvlc_attn_vision_varlen_ws(
         _ptr(q), _ptr(k), _ptr(v), cu.ctypes.data_as(ctypes.c_void_p), max(len(cu) - 1, 0), T, H,
-        D, _ptr(rope_cos), _ptr(rope_sin), _ptr(out), _stream())
-    abi.check(st, "pvlc_attn_vision_varlen")
+        D, _ptr(rope_cos), _ptr(rope_sin), _ptr(workspace if rope_cos is not None else None),
+        ws_bytes, _ptr(out), _stream())
+    abi.check(st, "pvlc_attn_vision_varlen_ws")
     return out
 
 

@@ -50,6 +50,10 @@ def test_vision_plan_config2():
     assert plan.flops == pytest.approx(1.0813e11, rel=1e-4)      # 4*72*16*sum n_i^2
     assert plan.output_elements == 8000 * 16 * 72
     assert plan.work_items == plan.grid[0] * plan.grid[1]
+    # scratch for the rotated q and k of the two-pass rotation + attention
+    assert plan.workspace_bytes == 2 * 8000 * 16 * 72 * 2
+    assert abi.lib().pvlc_attn_vision_workspace_bytes(8000, 16, 72) == plan.workspace_bytes
+    assert abi.lib().pvlc_attn_vision_workspace_bytes(8000, 16, 80) == 0
 
 
 @pytest.mark.parametrize("args,code", [

@@ -122,3 +122,42 @@ def test_vision_validation_errors(cuda_lib):
         with pytest.raises(abi.PvlcError) as e:
             ops.vision_varlen_attention(z, z, z, cu)
         assert e.value.status == code
+
+
+def test_workspace_entry_points_agree(cuda_lib):
+    """pvlc_attn_vision_varlen (stream-ordered scratch) and pvlc_attn_vision_varlen_ws
+    (caller scratch) run the same kernels: bitwise equal outputs; the _ws checks."""
+    import ctypes
+    from pvlc_b200 import abi, ops, positions
+    grids = [(1, 8, 8), (1, 6, 10)]
+    cu = np.array([0, 64, 124], np.uint32)
+    T = 124
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    q, k, v = (torch.randn((T, H, D), generator=g, device="cuda").half() for _ in range(3))
+    c, s = (torch.from_numpy(x).cuda() for x in positions.vision_rope_tables(grids))
+    a = ops.vision_varlen_attention(q, k, v, cu, c, s)
+    b = torch.empty_like(a)
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    st = abi.lib().pvlc_attn_vision_varlen(P(q), P(k), P(v), cu.ctypes.data_as(ctypes.c_void_p),
+                                           2, T, H, D, P(c), P(s), P(b), stream)
+    assert st == abi.OK
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    need = ops.vision_workspace_bytes(T, H)
+    assert need == 2 * T * H * D * 2
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    f = abi.lib().pvlc_attn_vision_varlen_ws
+    args = (P(q), P(k), P(v), cu.ctypes.data_as(ctypes.c_void_p), 2, T, H, D, P(c), P(s))
+    assert f(*args, P(ws), need - 1, P(b), stream) == abi.WORKSPACE_TOO_SMALL
+    assert f(*args, P(None), need, P(b), stream) == abi.NULL_POINTER
+    assert f(*args, P(ws[1:]), need - 1, P(b), stream) in (abi.MISALIGNED_POINTER,
+                                                         abi.WORKSPACE_TOO_SMALL)
+    # without tables no scratch is needed: NULL workspace is fine
+    ref = ops.vision_varlen_attention(q, k, v, cu)
+    nul = P(None)
+    assert f(P(q), P(k), P(v), cu.ctypes.data_as(ctypes.c_void_p), 2, T, H, D, nul, nul, nul, 0,
+             P(b), stream) == abi.OK
+    torch.cuda.synchronize()
+    assert torch.equal(ref, b)
