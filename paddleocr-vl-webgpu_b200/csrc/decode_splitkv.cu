@@ -12,19 +12,25 @@
 //     end to end and split evenly over one CTA per SM, so every SM streams the
 //     same number of bytes whatever the per-sequence lengths are.  A CTA's
 //     range may cover the tail of one sequence and the head of the next.
-//   * Two producer warps stream 512-byte cache rows (both KV heads) into a
-//     4-stage shared-memory ring with 16-byte cp.async copies (one coalesced
-//     row per warp instruction) whose completion arrives on per-stage
-//     mbarriers; rows land at a 528-byte pitch so ldmatrix is conflict free.
-//     (Per-row 1-D bulk copies were issue-bound at ~2 TB/s: 64 small TMA
-//     operations per 32 KB tile.)
+//   * A copy warp streams 512-byte cache rows (both KV heads) into a 4-stage
+//     shared-memory ring with 16-byte cp.async copies (one coalesced row per
+//     warp instruction) whose completion arrives on per-stage mbarriers; rows
+//     land at a 528-byte pitch so ldmatrix is conflict free.  (Per-row 1-D
+//     bulk copies were issue-bound at ~2 TB/s: 64 small TMA operations per
+//     32 KB tile.)
 //   * Eight consumer warps (2 tile-parity groups x 2 KV heads x 2 row halves)
 //     run the 8 query heads of a KV group as the N=8 side of mma.m16n8k16:
 //     S^T = K Q^T (keys on M), online softmax over keys in f32 (exp2 domain),
 //     P^T transposed in registers with movmatrix, O^T += V^T P^T.
-//   * Decode M-RoPE of q is applied while building the Q fragments; the new
-//     key is rotated, patched into the staged tile and written to the cache
-//     row cache_tokens[b] by the one warp that owns that row.
+//   * A sequence warp does the per-sequence work ahead of the stream: for
+//     each sequence of the CTA's range it writes the decode-M-RoPE-rotated q
+//     into a double-buffered shared-memory slot and performs the KV append
+//     (the rotated new key and the new value into cache row
+//     cache_tokens[b]) before the copy warp reaches that row.  A sequence
+//     change costs the consumers one shared-memory read of their Q fragments
+//     and the copy warp nothing.
+//   * The ring is never zeroed: rows past a sequence end are masked to
+//     P = 0 and the consumer zeroes their V bytes before the PV product.
 //   * Per-sequence partials (unnormalised O, running max, running sum) are
 //     merged across warps in shared memory; a sequence split over several
 //     CTAs is combined by the last CTA to finish it (atomic ticket, no
@@ -65,8 +71,12 @@ constexpr int SM_MERGE_ACC = SM_V + STAGES * STAGE_BYTES;          // [8 warps][
 constexpr int SM_MERGE_M = SM_MERGE_ACC + CONSUMER_WARPS * GROUP * HD * 4;
 constexpr int SM_MERGE_L = SM_MERGE_M + CONSUMER_WARPS * GROUP * 4;
 constexpr int SM_TILE_OFF = SM_MERGE_L + CONSUMER_WARPS * GROUP * 4;  // [MAX_BATCH+1]
-constexpr int SM_BARS = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
-constexpr int SM_MISC = SM_BARS + 2 * STAGES * 8;
+// rotated q of the current / next sequence: [2 slots][16 heads][Q_PITCH halves]
+constexpr int Q_PITCH = HD + 8;          // 272-byte rows: conflict-free fragment reads
+constexpr int SM_Q = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
+constexpr int SM_BARS = SM_Q + 2 * QH * Q_PITCH * 2;
+// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2]
+constexpr int SM_MISC = SM_BARS + (2 * STAGES + 6) * 8;
 constexpr int SMEM_BYTES = SM_MISC + 64;
 
 static_assert(SMEM_BYTES <= 227 * 1024, "decode shared memory exceeds the sm_100 limit");
@@ -114,11 +124,41 @@ __device__ __forceinline__ uint32_t owner_cta(uint64_t x, uint64_t G, uint64_t N
   return static_cast<uint32_t>(((x + 1) * G + NT - 1) / NT - 1);
 }
 
+// M-RoPE of 8 consecutive dims d0..d0+7 of a 128-wide head (d0 a multiple of
+// 8, so they share one table plane: the section edges 16 and 40 are multiples
+// of 8).  x holds the dims, y their partners (d + 64 below 64, d - 64 above):
+// d < 64 becomes x cos - y sin, d >= 64 becomes x cos + y sin
+// (crates/pvlc-cpu-ref/src/lib.rs:645-668).
+__device__ __forceinline__ uint4 mrope8(uint4 x, uint4 y, uint32_t d0, const Params& p,
+                                        uint32_t rrow) {
+  const size_t tb = ((size_t)mrope_axis(d0) * p.rope_rows + rrow) * HD + d0;
+  const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + tb);
+  const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + tb);
+  const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
+  const bool lower = d0 < 64;
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+    float2 bp = __half22float2(*reinterpret_cast<const __half2*>(&yw[e]));
+    if (lower) bp = make_float2(-bp.x, -bp.y);
+    o[e] = pack_half2(a.x * cs[2 * e] + bp.x * sn[2 * e], a.y * cs[2 * e + 1] + bp.y * sn[2 * e + 1]);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* tile_off = reinterpret_cast<uint32_t*>(smem + SM_TILE_OFF);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM_BARS);
   uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* q_full = empty_bar + STAGES;   // [2] rotated q (and the append) of a sequence are done
+  uint64_t* q_empty = q_full + 2;          // [2] every consumer warp has read the slot
+  uint64_t* app_free = q_empty + 2;        // [2] the copy warp has left the slot's sequence
+  __half* qs = reinterpret_cast<__half*>(smem + SM_Q);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   // misc[0]: abort flag, misc[1]: "this CTA combines" flag
 
@@ -127,12 +167,30 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   const int lane = tid & 31;
   const uint32_t B = p.batch;
 
-  // ---- schedule: exclusive prefix sum of per-sequence tile counts (warp 0)
+  // ---- schedule: per-sequence tile counts (every thread), then an in-place
+  // exclusive prefix sum over them (warp 0)
+  for (uint32_t bb = tid; bb < B; bb += THREADS) tile_off[bb + 1] = seq_tiles(p, bb, blockIdx.x == 0);
+  if (tid == 0) {
+    tile_off[0] = 0;
+    misc[0] = 0;
+    misc[1] = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 32);   // the copy warp's lanes
+      mbar_init(&empty_bar[s], 4);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 32);     // the sequence warp's lanes
+      mbar_init(&q_empty[s], CONSUMER_WARPS);
+      mbar_init(&app_free[s], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
   if (warp == 0) {
     const uint32_t per = (B + 31) / 32;
     const uint32_t b0 = min(B, lane * per), b1 = min(B, b0 + per);
     uint32_t s = 0;
-    for (uint32_t b = b0; b < b1; ++b) s += seq_tiles(p, b, false);
+    for (uint32_t bb = b0; bb < b1; ++bb) s += tile_off[bb + 1];
     uint32_t incl = s;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -140,29 +198,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       if (lane >= o) incl += y;
     }
     uint32_t run = incl - s;
-    for (uint32_t b = b0; b < b1; ++b) {
-      tile_off[b] = run;
-      run += seq_tiles(p, b, blockIdx.x == 0);
+    for (uint32_t bb = b0; bb < b1; ++bb) {
+      run += tile_off[bb + 1];
+      tile_off[bb + 1] = run;
     }
-    if (lane == 31) tile_off[B] = incl;
   }
-  if (tid == 0) {
-    misc[0] = 0;
-    misc[1] = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], PRODUCER_WARPS * 32);
-      mbar_init(&empty_bar[s], 4);
-    }
-    fence_mbar_init();
-  }
-  // zero the staging ring once: rows past a sequence end are never copied and
-  // must hold finite values (P = 0 there, and 0 * NaN would poison O)
-  {
-    uint4* z = reinterpret_cast<uint4*>(smem + SM_K);
-    const int n16 = 2 * STAGES * STAGE_BYTES / 16;
-    for (int i = tid; i < n16; i += THREADS) z[i] = make_uint4(0, 0, 0, 0);
-  }
-  fence_proxy_async_smem();
   __syncthreads();
 
   const uint64_t NT = tile_off[B];
@@ -193,40 +233,107 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
 
   if (warp >= CONSUMER_WARPS) {
     // ======================= producer warps =======================
-    // Each warp instruction moves one whole 512-byte cache row (16 bytes per
-    // lane, fully coalesced) into the padded staging row; producer warp pw
-    // takes rows pw, pw + PRODUCER_WARPS, ...  Every producer lane arrives on
-    // the stage's full barrier once its own copies have landed.
-    const int pw = warp - CONSUMER_WARPS;
-    uint32_t b = seq_of(t0);
-    const uint8_t* kc = reinterpret_cast<const uint8_t*>(p.k_cache[b]);
-    const uint8_t* vc = reinterpret_cast<const uint8_t*>(p.v_cache[b]);
-    uint32_t L = __ldg(p.cache_tokens + b) + 1;
+    // Warp 8, the copy warp, streams the tiles: each warp instruction moves
+    // one whole 512-byte cache row (16 bytes per lane, fully coalesced) into
+    // the padded staging row, and every lane arrives on the stage's full
+    // barrier once its own copies have landed.  It never stalls on anything
+    // but free ring stages, so the ring stays full across sequence changes.
+    // Warp 9, the sequence warp, does the per-sequence work ahead of the
+    // stream: for each sequence of the CTA's range, in order, it writes the
+    // decode-M-RoPE-rotated q into a double-buffered shared-memory slot and,
+    // when the range holds the sequence's appended row, first stores the
+    // rotated new key and the new value in cache row cache_tokens[b] (the KV
+    // append); then it announces the slot (q_full).  The copy warp waits for
+    // that announcement before copying the tile that holds the appended row,
+    // and releases the slot's append (app_free) when it leaves the sequence,
+    // which keeps the slot's barrier phases in step.
     bool aborted = false;
-    for (uint64_t it = 0; it < t1 - t0; ++it) {
-      const uint64_t gt = t0 + it;
-      if (gt >= tile_off[b + 1]) {
-        while (gt >= tile_off[b + 1]) ++b;
-        kc = reinterpret_cast<const uint8_t*>(p.k_cache[b]);
-        vc = reinterpret_cast<const uint8_t*>(p.v_cache[b]);
-        L = __ldg(p.cache_tokens + b) + 1;
+    uint32_t b = seq_of(t0);
+    if (warp == CONSUMER_WARPS) {
+      uint32_t nseq = 0;
+      uint8_t* kc = reinterpret_cast<uint8_t*>(p.k_cache[b]);
+      uint8_t* vc = reinterpret_cast<uint8_t*>(p.v_cache[b]);
+      uint32_t L = __ldg(p.cache_tokens + b) + 1;
+      for (uint64_t it = 0; it < t1 - t0; ++it) {
+        const uint64_t gt = t0 + it;
+        if (gt >= tile_off[b + 1]) {
+          if (lane == 0) mbar_arrive(&app_free[nseq & 1u]);
+          ++nseq;
+          while (gt >= tile_off[b + 1]) ++b;
+          kc = reinterpret_cast<uint8_t*>(p.k_cache[b]);
+          vc = reinterpret_cast<uint8_t*>(p.v_cache[b]);
+          L = __ldg(p.cache_tokens + b) + 1;
+        }
+        const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
+        const uint32_t n = umin32(TILE, L - row0);
+        const int stage = static_cast<int>(it % STAGES);
+        const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+        if (misc[0] || !mbar_wait(&empty_bar[stage], ph ^ 1u)) {
+          aborted = true;
+          break;
+        }
+        if (row0 + n == L &&   // the tile that holds the appended row L - 1
+            (misc[0] || !mbar_wait(&q_full[nseq & 1u], (nseq >> 1) & 1u))) {
+          aborted = true;
+          break;
+        }
+        const uint32_t ks = smem_u32(smem + SM_K + stage * STAGE_BYTES) + lane * 16;
+        const uint32_t vs = smem_u32(smem + SM_V + stage * STAGE_BYTES) + lane * 16;
+        for (uint32_t r = 0; r < n; ++r) {
+          const size_t src = (size_t)(row0 + r) * ROW_BYTES + lane * 16;
+          cp_async_16(ks + r * ROW_PITCH, kc + src);
+          cp_async_16(vs + r * ROW_PITCH, vc + src);
+        }
+        cp_async_arrive_noinc(&full_bar[stage]);
       }
-      const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
-      const uint32_t n = umin32(TILE, L - row0);
-      const int stage = static_cast<int>(it % STAGES);
-      const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
-      if (misc[0] || !mbar_wait(&empty_bar[stage], ph ^ 1u)) {
-        aborted = true;
-        break;
+    } else {
+      // sequence warp: lane l rotates query head l/2, dims 32(l%2)..+31 and
+      // their partners 64 above
+      uint32_t nseq = 0;
+      while (true) {
+        const uint32_t slot = nseq & 1u, round = nseq >> 1;
+        if (misc[0] || !mbar_wait(&q_empty[slot], (round & 1u) ^ 1u) ||
+            !mbar_wait(&app_free[slot], (round & 1u) ^ 1u)) {
+          aborted = true;
+          break;
+        }
+        const uint32_t ct = __ldg(p.cache_tokens + b);
+        const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + b) : ct;
+        const int h = lane >> 1;
+        const __half* qrow = p.q + ((size_t)b * QH + h) * HD;
+        __half* qdst = qs + (slot * QH + h) * Q_PITCH;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t d = 32 * (lane & 1) + 8 * u;
+          const uint4 lo = __ldg(reinterpret_cast<const uint4*>(qrow + d));
+          const uint4 hi = __ldg(reinterpret_cast<const uint4*>(qrow + d + 64));
+          *reinterpret_cast<uint4*>(qdst + d) = mrope8(lo, hi, d, p, rrow);
+          *reinterpret_cast<uint4*>(qdst + d + 64) = mrope8(hi, lo, d + 64, p, rrow);
+        }
+        const uint64_t append_tile = tile_off[b] + ct / TILE;
+        if (append_tile >= t0 && append_tile < t1) {
+          // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
+          // 8(l%16)..+7; the M-RoPE partners (d +- 64) sit in lane l ^ 8
+          const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
+          const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)b * KVH * HD) + lane);
+          const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)b * KVH * HD) + lane);
+          uint4 ky;
+          ky.x = __shfl_xor_sync(0xffffffffu, kx.x, 8);
+          ky.y = __shfl_xor_sync(0xffffffffu, kx.y, 8);
+          ky.z = __shfl_xor_sync(0xffffffffu, kx.z, 8);
+          ky.w = __shfl_xor_sync(0xffffffffu, kx.w, 8);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.k_cache[b]) + off) =
+              mrope8(kx, ky, (lane & 15) * 8, p, rrow);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.v_cache[b]) + off) = vx;
+          __threadfence();   // visible before the copy warp reads the row back
+        }
+        mbar_arrive(&q_full[slot]);
+        ++nseq;
+        const uint64_t s1 = umin64(t1, tile_off[b + 1]);
+        if (s1 >= t1) break;
+        ++b;
+        while (tile_off[b + 1] <= s1) ++b;   // skip sequences with no tiles
       }
-      const uint32_t ks = smem_u32(smem + SM_K + stage * STAGE_BYTES) + lane * 16;
-      const uint32_t vs = smem_u32(smem + SM_V + stage * STAGE_BYTES) + lane * 16;
-      for (uint32_t r = pw; r < n; r += PRODUCER_WARPS) {
-        const size_t src = (size_t)(row0 + r) * ROW_BYTES + lane * 16;
-        cp_async_16(ks + r * ROW_PITCH, kc + src);
-        cp_async_16(vs + r * ROW_PITCH, vc + src);
-      }
-      cp_async_arrive_noinc(&full_bar[stage]);
     }
     if (aborted) {
       if (lane == 0) atomicOr(p.flags, kFlagTimeout);
@@ -250,33 +357,35 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   float* merge_l = reinterpret_cast<float*>(smem + SM_MERGE_L);
 
   uint32_t b = seq_of(t0);
+  uint32_t nseq = 0;   // sequences of this CTA so far (q slot parity, in producer order)
   while (true) {
     const uint64_t s0 = umax64(t0, tile_off[b]);
     const uint64_t s1 = umin64(t1, tile_off[b + 1]);
-    const uint32_t ct = __ldg(p.cache_tokens + b);
-    const uint32_t L = ct + 1;
-    const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + b) : ct;
+    const uint32_t L = __ldg(p.cache_tokens + b) + 1;
 
-    // ---- rotated Q^T fragments (B operand: k = dim, n = head) for this KV group
+    // ---- rotated Q^T fragments (B operand: k = dim, n = head) for this KV
+    // group, from the shared-memory slot the producers filled for sequence b
     uint32_t qf[8][2];
     {
-      const __half* qrow = p.q + ((size_t)b * QH + kvh * GROUP + g) * HD;
+      const int slot = static_cast<int>(nseq & 1u);
+      // On an abort (or a timed-out wait) every consumer warp still walks the
+      // same merges and named barriers below: the tile loop does nothing once
+      // misc[0] is set, so no warp can leave another waiting at a barrier.
+      const bool go = __all_sync(0xffffffffu, misc[0] == 0);
+      if (go && !__all_sync(0xffffffffu, mbar_wait(&q_full[slot], (nseq >> 1) & 1u))) {
+        if (lane == 0) atomicOr(p.flags, kFlagTimeout);
+        misc[0] = 1;
+      }
+      const __half* qrow = qs + (slot * QH + kvh * GROUP + g) * Q_PITCH;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          float r[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int d = ks * 16 + hh * 8 + 2 * c + e;
-            const float x = __half2float(qrow[d]);
-            const float partner = d < 64 ? -__half2float(qrow[d + 64]) : __half2float(qrow[d - 64]);
-            const size_t ti = ((size_t)mrope_axis(d) * p.rope_rows + rrow) * HD + d;
-            r[e] = x * __ldg(p.rope_cos + ti) + partner * __ldg(p.rope_sin + ti);
-          }
-          qf[ks][hh] = pack_half2(r[0], r[1]);
-        }
+        for (int hh = 0; hh < 2; ++hh)
+          qf[ks][hh] = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + hh * 8 + 2 * c);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[slot]);
+      ++nseq;
     }
 
     float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F};
@@ -289,8 +398,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       const uint64_t it = gt - t0;
       const int stage = static_cast<int>(it % STAGES);
       const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
-      if (misc[0]) break;
-      if (!mbar_wait(&full_bar[stage], ph)) {
+      // warp-uniform exits: the tile body below is warp-collective
+      if (!__all_sync(0xffffffffu, misc[0] == 0)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full_bar[stage], ph))) {
         if (lane == 0) atomicOr(p.flags, kFlagTimeout);
         misc[0] = 1;
         break;
@@ -300,27 +410,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       uint8_t* kst = smem + SM_K + stage * STAGE_BYTES;
       uint8_t* vst = smem + SM_V + stage * STAGE_BYTES;
       if (n_valid > 0) {
-        // ---- the appended token lives in this warp's rows: rotate + patch
-        const int newrow = static_cast<int>(ct - row0);
-        if (newrow >= half * 16 && newrow < half * 16 + 16) {
-          const __half* kn = p.k_new + ((size_t)b * KVH + kvh) * HD;
-          const __half* vn = p.v_new + ((size_t)b * KVH + kvh) * HD;
-          __half kr[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int d = lane * 4 + e;
-            const float x = __half2float(kn[d]);
-            const float partner = d < 64 ? -__half2float(kn[d + 64]) : __half2float(kn[d - 64]);
-            const size_t ti = ((size_t)mrope_axis(d) * p.rope_rows + rrow) * HD + d;
-            kr[e] = __float2half_rn(x * __ldg(p.rope_cos + ti) + partner * __ldg(p.rope_sin + ti));
-          }
-          const uint2 kv = *reinterpret_cast<uint2*>(kr);
-          const uint2 vv = *reinterpret_cast<const uint2*>(vn + lane * 4);
-          *reinterpret_cast<uint2*>(kst + newrow * ROW_PITCH + kvh * HD * 2 + lane * 8) = kv;
-          *reinterpret_cast<uint2*>(vst + newrow * ROW_PITCH + kvh * HD * 2 + lane * 8) = vv;
-          *reinterpret_cast<uint2*>(p.k_cache[b] + (size_t)ct * KVH * HD + kvh * HD + lane * 4) = kv;
-          *reinterpret_cast<uint2*>(p.v_cache[b] + (size_t)ct * KVH * HD + kvh * HD + lane * 4) = vv;
-          fence_proxy_async_smem();
+        if (n_valid < 16) {
+          // past the sequence end the staged rows hold whatever the ring last
+          // carried (or nothing yet): zero this warp's V rows there, since
+          // P = 0 meets them in the PV product and 0 * NaN would poison O
+          for (int r = n_valid; r < 16; ++r)
+            *reinterpret_cast<uint2*>(vst + (half * 16 + r) * ROW_PITCH + kvh * HD * 2 + lane * 8) =
+                make_uint2(0u, 0u);
           __syncwarp();
         }
 
