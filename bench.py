@@ -37,6 +37,15 @@ L_MIN, L_MAX = 512, 8192
 METRIC = "decode-attn HBM GB/s (64 seqs x 18 layers, L~U[512,8192])"
 UNIT = "GB/s"
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of single launches
+# captured with ncu on this workload's shapes (profiles/decode_kernel_64seq.txt,
+# profiles/vision_tc_kernel_config1.txt, profiles/prefill_attn_kernel_config2.txt).
+# The decode capture is one 64-sequence launch: its traffic / algorithmic-bytes
+# ratio scales the figure to the bench's average launch.
+DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 282.96e6 / 278.20e6
+VISION_TC_TRAFFIC_BYTES = 59.09e6
+PREFILL_ATTN_TRAFFIC_BYTES = 11.34e6
+
 
 def peaks():
     try:
@@ -273,7 +282,10 @@ def run_gpu(args, rank, world, local_rank, dist):
                      "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": peak_src, "kernel": "pvlc::decode::decode_kernel",
                      "avg_launch_ms": round(avg_kernel_ms, 5),
-                     "traffic": args.traffic_bytes},
+                     "traffic": round(args.traffic_bytes if args.traffic_bytes is not None else
+                                      DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE * bytes_rank / launches),
+                     "traffic_source": "--traffic-bytes" if args.traffic_bytes is not None else
+                                       "ncu capture of one 64-sequence launch, scaled by algorithmic bytes"},
         "clocks": clocks,
         "components": components,
     }
@@ -341,7 +353,8 @@ def bench_vision(dev, timeit, tf_peak, peak_src):
             "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
                          "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
-                         "peak_source": peak_src},
+                         "peak_source": peak_src, "traffic": VISION_TC_TRAFFIC_BYTES,
+                         "traffic_kernel": "pvlc::vtc::vision_tc_kernel (ncu, one launch)"},
             "kernel": "pvlc::vtc::vision_rope_kernel + pvlc::vtc::vision_tc_kernel"}
 
 
@@ -378,7 +391,8 @@ def bench_prefill(dev, timeit, tf_peak, peak_src):
             "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
                          "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
-                         "peak_source": peak_src},
+                         "peak_source": peak_src, "traffic": PREFILL_ATTN_TRAFFIC_BYTES,
+                         "traffic_kernel": "pvlc::ptc::prefill_attn_kernel (ncu, one launch)"},
             "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
 
 
