@@ -12,7 +12,7 @@
 //     end to end and split evenly over one CTA per SM, so every SM streams the
 //     same number of bytes whatever the per-sequence lengths are.  A CTA's
 //     range may cover the tail of one sequence and the head of the next.
-//   * A copy warp streams 512-byte cache rows (both KV heads) into a 4-stage
+//   * A copy warp streams 512-byte cache rows (both KV heads) into a 5-stage
 //     shared-memory ring with 16-byte cp.async copies (one coalesced row per
 //     warp instruction) whose completion arrives on per-stage mbarriers; rows
 //     land at a 528-byte pitch so ldmatrix is conflict free.  (Per-row 1-D
@@ -31,10 +31,15 @@
 //     and the copy warp nothing.
 //   * The ring is never zeroed: rows past a sequence end are masked to
 //     P = 0 and the consumer zeroes their V bytes before the PV product.
-//   * Per-sequence partials (unnormalised O, running max, running sum) are
-//     merged across warps in shared memory; a sequence split over several
-//     CTAs is combined by the last CTA to finish it (atomic ticket, no
-//     spinning), which also resets the ticket for the next launch.
+//   * Per-sequence partials (unnormalised O, running max, running sum): each
+//     consumer warp hands its (O, m, l) to a merge warp through shared memory
+//     and moves on to the next sequence, so a sequence end inside the range
+//     does not stall the stream; the merge warp combines the 8 warps and
+//     writes the output or, for a sequence split over several CTAs, this
+//     CTA's partial record.  The range's last sequence, with nothing left to
+//     overlap, is merged by all 256 consumer threads.  The last CTA to finish
+//     a split sequence (atomic ticket, no spinning) combines every CTA's
+//     record in CTA (= token) order and resets the ticket for the next launch.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math_constants.h>
@@ -53,13 +58,14 @@ constexpr int KVH = 2;
 constexpr int QH = 16;
 constexpr int GROUP = 8;
 constexpr int TILE = 32;          // cache rows per pipeline stage
-constexpr int STAGES = 4;
+constexpr int STAGES = 5;
 constexpr int ROW_BYTES = KVH * HD * 2;   // 512
 constexpr int ROW_PITCH = ROW_BYTES + 16; // 528: conflict-free ldmatrix rows
 constexpr int STAGE_BYTES = TILE * ROW_PITCH;
 constexpr int CONSUMER_WARPS = 8;
-constexpr int PRODUCER_WARPS = 2;
-constexpr int THREADS = (CONSUMER_WARPS + PRODUCER_WARPS) * 32;
+constexpr int PRODUCER_WARPS = 2;             // copy warp, sequence warp
+constexpr int MERGE_WARP = CONSUMER_WARPS + PRODUCER_WARPS;
+constexpr int THREADS = (CONSUMER_WARPS + PRODUCER_WARPS + 1) * 32;
 constexpr int CONSUMER_THREADS = CONSUMER_WARPS * 32;
 constexpr int MAX_BATCH = 2048;
 constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]
@@ -67,6 +73,7 @@ constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]
 // shared memory map (bytes)
 constexpr int SM_K = 0;
 constexpr int SM_V = SM_K + STAGES * STAGE_BYTES;
+// per-sequence (O, m, l) of the consumer warps, handed to the merge warp
 constexpr int SM_MERGE_ACC = SM_V + STAGES * STAGE_BYTES;          // [8 warps][8 heads][128]
 constexpr int SM_MERGE_M = SM_MERGE_ACC + CONSUMER_WARPS * GROUP * HD * 4;
 constexpr int SM_MERGE_L = SM_MERGE_M + CONSUMER_WARPS * GROUP * 4;
@@ -75,8 +82,8 @@ constexpr int SM_TILE_OFF = SM_MERGE_L + CONSUMER_WARPS * GROUP * 4;  // [MAX_BA
 constexpr int Q_PITCH = HD + 8;          // 272-byte rows: conflict-free fragment reads
 constexpr int SM_Q = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
 constexpr int SM_BARS = SM_Q + 2 * QH * Q_PITCH * 2;
-// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2]
-constexpr int SM_MISC = SM_BARS + (2 * STAGES + 6) * 8;
+// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2], merge_full, merge_empty
+constexpr int SM_MISC = SM_BARS + (2 * STAGES + 8) * 8;
 constexpr int SMEM_BYTES = SM_MISC + 64;
 
 static_assert(SMEM_BYTES <= 227 * 1024, "decode shared memory exceeds the sm_100 limit");
@@ -158,6 +165,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   uint64_t* q_full = empty_bar + STAGES;   // [2] rotated q (and the append) of a sequence are done
   uint64_t* q_empty = q_full + 2;          // [2] every consumer warp has read the slot
   uint64_t* app_free = q_empty + 2;        // [2] the copy warp has left the slot's sequence
+  uint64_t* merge_full = app_free + 2;     // every consumer warp wrote its (O, m, l)
+  uint64_t* merge_empty = merge_full + 1;  // the merge warp has read the merge buffer
   __half* qs = reinterpret_cast<__half*>(smem + SM_Q);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   // misc[0]: abort flag, misc[1]: "this CTA combines" flag
@@ -183,6 +192,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       mbar_init(&q_empty[s], CONSUMER_WARPS);
       mbar_init(&app_free[s], 1);
     }
+    mbar_init(merge_full, CONSUMER_WARPS);
+    mbar_init(merge_empty, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         }
         cp_async_arrive_noinc(&full_bar[stage]);
       }
-    } else {
+    } else if (warp == CONSUMER_WARPS + 1) {
       // sequence warp: lane l rotates query head l/2, dims 32(l%2)..+31 and
       // their partners 64 above
       uint32_t nseq = 0;
@@ -331,6 +342,131 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         ++nseq;
         const uint64_t s1 = umin64(t1, tile_off[b + 1]);
         if (s1 >= t1) break;
+        ++b;
+        while (tile_off[b + 1] <= s1) ++b;   // skip sequences with no tiles
+      }
+    } else {
+      // merge warp: per sequence of the range except the last, in order,
+      // combines the eight consumer warps' (O, m, l) from the buffer they
+      // filled and writes the output (whole sequence) or this CTA's partial
+      // record; for a split sequence the last CTA to finish (atomic ticket, no
+      // spinning) combines every CTA's record in CTA (= token) order and
+      // resets the ticket.  The consumers hand over and move on, so a sequence
+      // end inside the range does not stall the stream; the range's last
+      // sequence, after which nothing is left to overlap, is merged by all
+      // consumer threads.  Lane l owns query head l/2, dims 64(l%2)..+63.
+      const int hq = lane >> 1, dbase = (lane & 1) * 64;
+      const int kg = hq >> 3, hig = hq & 7;
+      float* merge_acc = reinterpret_cast<float*>(smem + SM_MERGE_ACC);
+      float* merge_m = reinterpret_cast<float*>(smem + SM_MERGE_M);
+      float* merge_l = reinterpret_cast<float*>(smem + SM_MERGE_L);
+      uint32_t j = 0;
+      while (true) {
+        const uint64_t s0 = umax64(t0, tile_off[b]);
+        const uint64_t s1 = umin64(t1, tile_off[b + 1]);
+        if (s1 >= t1) break;   // the range's last sequence: merged by the consumers
+        if (misc[0] || !mbar_wait(merge_full, j & 1u)) {
+          aborted = true;
+          break;
+        }
+        const float* mm = merge_m;
+        const float* ml = merge_l;
+        const float* ma = merge_acc;
+        // the four warps of KV group kg: (grp, half) in {0,1}^2 -> warp 4*grp + 2*kg + half
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) M = fmaxf(M, mm[(2 * kg + (i & 1) + 4 * (i >> 1)) * GROUP + hig]);
+        float f[4], Lsum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
+          const float mi = mm[w * GROUP + hig];
+          f[i] = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - M);
+          Lsum += ml[w * GROUP + hig] * f[i];
+        }
+        const bool whole = (s0 == tile_off[b]) && (s1 == tile_off[b + 1]);
+        const uint32_t slot = blockIdx.x + b;
+        float* rec = p.partials + (size_t)slot * PART_FLOATS;
+        const float inv = 1.f / Lsum;
+#pragma unroll 2
+        for (int ch = 0; ch < 8; ++ch) {
+          const int d0 = dbase + 8 * ch;
+          float A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
+            const float4 u = *reinterpret_cast<const float4*>(ma + (w * GROUP + hig) * HD + d0);
+            const float4 x = *reinterpret_cast<const float4*>(ma + (w * GROUP + hig) * HD + d0 + 4);
+            A[0] += u.x * f[i]; A[1] += u.y * f[i]; A[2] += u.z * f[i]; A[3] += u.w * f[i];
+            A[4] += x.x * f[i]; A[5] += x.y * f[i]; A[6] += x.z * f[i]; A[7] += x.w * f[i];
+          }
+          if (whole) {
+            __align__(16) __half o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[e] * inv);
+            *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+                *reinterpret_cast<uint4*>(o);
+          } else {
+            *reinterpret_cast<float4*>(rec + hq * HD + d0) = make_float4(A[0], A[1], A[2], A[3]);
+            *reinterpret_cast<float4*>(rec + hq * HD + d0 + 4) = make_float4(A[4], A[5], A[6], A[7]);
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(merge_empty);   // the buffer has been read
+        if (!whole) {
+          if ((lane & 1) == 0) {
+            rec[QH * HD + hq] = M;
+            rec[QH * HD + QH + hq] = Lsum;
+          }
+          __threadfence();
+          __syncwarp();
+          uint32_t first = 0, last = 0, mine = 0;
+          if (lane == 0) {
+            first = owner_cta(tile_off[b], G, NT);
+            last = owner_cta(tile_off[b + 1] - 1, G, NT);
+            const uint32_t prev = atomicAdd(p.tickets + b, 1u);
+            mine = prev == last - first;
+            if (mine) {
+              __threadfence();
+              p.tickets[b] = 0;  // ready for the next launch
+            }
+          }
+          mine = __shfl_sync(0xffffffffu, mine, 0);
+          first = __shfl_sync(0xffffffffu, first, 0);
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (mine) {
+            float Mc = -CUDART_INF_F;
+            for (uint32_t i = first; i <= last; ++i)
+              Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
+            float Lc = 0.f;
+            for (uint32_t i = first; i <= last; ++i) {
+              const float* ri = p.partials + (size_t)(i + b) * PART_FLOATS;
+              const float mi = __ldcg(ri + QH * HD + hq);
+              Lc += __ldcg(ri + QH * HD + QH + hq) * (mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc));
+            }
+            const float invc = 1.f / Lc;
+#pragma unroll 2
+            for (int ch = 0; ch < 8; ++ch) {
+              const int d0 = dbase + 8 * ch;
+              float Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+              for (uint32_t i = first; i <= last; ++i) {
+                const float* ri = p.partials + (size_t)(i + b) * PART_FLOATS;
+                const float mi = __ldcg(ri + QH * HD + hq);
+                const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
+                const float4 u = __ldcg(reinterpret_cast<const float4*>(ri + hq * HD + d0));
+                const float4 w = __ldcg(reinterpret_cast<const float4*>(ri + hq * HD + d0 + 4));
+                Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
+                Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
+              }
+              __align__(16) __half o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * invc);
+              *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+                  *reinterpret_cast<uint4*>(o);
+            }
+          }
+        }
+        ++j;
         ++b;
         while (tile_off[b + 1] <= s1) ++b;   // skip sequences with no tiles
       }
@@ -482,8 +618,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       if (lane == 0) mbar_arrive(&empty_bar[stage]);
     }
 
-    // ---- merge the four warps of each KV group for this sequence
+    // ---- hand this warp's (O, m, l) for the sequence over: to the merge warp,
+    // or, for the range's last sequence, to the merge below by all consumers
     {
+      const uint32_t e = nseq - 1;   // this sequence's index in the CTA's range
+      if (!__all_sync(0xffffffffu, mbar_wait(merge_empty, (e & 1u) ^ 1u))) {
+        if (lane == 0) atomicOr(p.flags, kFlagTimeout);
+        misc[0] = 1;
+      }
       float l0 = l_run[0], l1 = l_run[1];
 #pragma unroll
       for (int o = 4; o < 32; o <<= 1) {
@@ -504,99 +646,101 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         ma[(2 * c) * HD + mt * 16 + g + 8] = acc[mt][2];
         ma[(2 * c + 1) * HD + mt * 16 + g + 8] = acc[mt][3];
       }
+      __syncwarp();
+      if (s1 < t1 && lane == 0) mbar_arrive(merge_full);
     }
-    named_bar_sync(1, CONSUMER_THREADS);
-
-    const bool whole = (s0 == tile_off[b]) && (s1 == tile_off[b + 1]);
-    const uint32_t slot = blockIdx.x + b;
-    // thread -> (query head, 8 dims)
-    const int hq = tid >> 4;               // 0..15
-    const int d0 = (tid & 15) * 8;
-    const int kg = hq >> 3, hig = hq & 7;
-    // the four warps of KV group kg: (grp, half) in {0,1}^2 -> warp 4*grp + 2*kg + half
-    float M = -CUDART_INF_F;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) M = fmaxf(M, merge_m[(2 * kg + (i & 1) + 4 * (i >> 1)) * GROUP + hig]);
-    float f[4], Lsum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
-      const float mi = merge_m[w * GROUP + hig];
-      f[i] = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - M);
-      Lsum += merge_l[w * GROUP + hig] * f[i];
-    }
-    float A[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) A[e] = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
-      const float4 u = *reinterpret_cast<const float4*>(merge_acc + (w * GROUP + hig) * HD + d0);
-      const float4 x = *reinterpret_cast<const float4*>(merge_acc + (w * GROUP + hig) * HD + d0 + 4);
-      A[0] += u.x * f[i]; A[1] += u.y * f[i]; A[2] += u.z * f[i]; A[3] += u.w * f[i];
-      A[4] += x.x * f[i]; A[5] += x.y * f[i]; A[6] += x.z * f[i]; A[7] += x.w * f[i];
-    }
-    if (whole) {
-      const float inv = 1.f / Lsum;
-      __align__(16) __half o[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[e] * inv);
-      *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
-          *reinterpret_cast<uint4*>(o);
-    } else {
-      float* rec = p.partials + (size_t)slot * PART_FLOATS;
-      *reinterpret_cast<float4*>(rec + hq * HD + d0) = make_float4(A[0], A[1], A[2], A[3]);
-      *reinterpret_cast<float4*>(rec + hq * HD + d0 + 4) = make_float4(A[4], A[5], A[6], A[7]);
-      if ((tid & 15) == 0) {
-        rec[QH * HD + hq] = M;
-        rec[QH * HD + QH + hq] = Lsum;
-      }
-      __threadfence();
-    }
-    named_bar_sync(1, CONSUMER_THREADS);
-    if (!whole) {
-      if (tid == 0) {
-        const uint32_t first = owner_cta(tile_off[b], G, NT);
-        const uint32_t last = owner_cta(tile_off[b + 1] - 1, G, NT);
-        const uint32_t prev = atomicAdd(p.tickets + b, 1u);
-        const bool mine = prev == last - first;
-        if (mine) {
-          __threadfence();
-          p.tickets[b] = 0;  // ready for the next launch
-        }
-        misc[1] = mine ? 1u : 0u;
-        misc[2] = first;
-        misc[3] = last;
-      }
+    if (s1 >= t1) {
       named_bar_sync(1, CONSUMER_THREADS);
-      if (misc[1]) {
-        // combine every CTA's record of sequence b in CTA (= token) order
-        const uint32_t first = misc[2], last = misc[3];
-        float Mc = -CUDART_INF_F;
-        for (uint32_t i = first; i <= last; ++i)
-          Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
-        float Lc = 0.f, Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (uint32_t i = first; i <= last; ++i) {
-          const float* rec = p.partials + (size_t)(i + b) * PART_FLOATS;
-          const float mi = __ldcg(rec + QH * HD + hq);
-          const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
-          Lc += __ldcg(rec + QH * HD + QH + hq) * fi;
-          const float4 u = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0));
-          const float4 w = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0 + 4));
-          Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
-          Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
-        }
-        const float inv = 1.f / Lc;
+      const bool whole = (s0 == tile_off[b]) && (s1 == tile_off[b + 1]);
+      const uint32_t slot = blockIdx.x + b;
+      // thread -> (query head, 8 dims)
+      const int hq = tid >> 4;               // 0..15
+      const int d0 = (tid & 15) * 8;
+      const int kg = hq >> 3, hig = hq & 7;
+      // the four warps of KV group kg: (grp, half) in {0,1}^2 -> warp 4*grp + 2*kg + half
+      float M = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) M = fmaxf(M, merge_m[(2 * kg + (i & 1) + 4 * (i >> 1)) * GROUP + hig]);
+      float f[4], Lsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
+        const float mi = merge_m[w * GROUP + hig];
+        f[i] = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - M);
+        Lsum += merge_l[w * GROUP + hig] * f[i];
+      }
+      float A[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) A[e] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int w = 2 * kg + (i & 1) + 4 * (i >> 1);
+        const float4 u = *reinterpret_cast<const float4*>(merge_acc + (w * GROUP + hig) * HD + d0);
+        const float4 x = *reinterpret_cast<const float4*>(merge_acc + (w * GROUP + hig) * HD + d0 + 4);
+        A[0] += u.x * f[i]; A[1] += u.y * f[i]; A[2] += u.z * f[i]; A[3] += u.w * f[i];
+        A[4] += x.x * f[i]; A[5] += x.y * f[i]; A[6] += x.z * f[i]; A[7] += x.w * f[i];
+      }
+      if (whole) {
+        const float inv = 1.f / Lsum;
         __align__(16) __half o[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * inv);
+        for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[e] * inv);
         *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
             *reinterpret_cast<uint4*>(o);
+      } else {
+        float* rec = p.partials + (size_t)slot * PART_FLOATS;
+        *reinterpret_cast<float4*>(rec + hq * HD + d0) = make_float4(A[0], A[1], A[2], A[3]);
+        *reinterpret_cast<float4*>(rec + hq * HD + d0 + 4) = make_float4(A[4], A[5], A[6], A[7]);
+        if ((tid & 15) == 0) {
+          rec[QH * HD + hq] = M;
+          rec[QH * HD + QH + hq] = Lsum;
+        }
+        __threadfence();
       }
       named_bar_sync(1, CONSUMER_THREADS);
+      if (!whole) {
+        if (tid == 0) {
+          const uint32_t first = owner_cta(tile_off[b], G, NT);
+          const uint32_t last = owner_cta(tile_off[b + 1] - 1, G, NT);
+          const uint32_t prev = atomicAdd(p.tickets + b, 1u);
+          const bool mine = prev == last - first;
+          if (mine) {
+            __threadfence();
+            p.tickets[b] = 0;  // ready for the next launch
+          }
+          misc[1] = mine ? 1u : 0u;
+          misc[2] = first;
+          misc[3] = last;
+        }
+        named_bar_sync(1, CONSUMER_THREADS);
+        if (misc[1]) {
+          // combine every CTA's record of sequence b in CTA (= token) order
+          const uint32_t first = misc[2], last = misc[3];
+          float Mc = -CUDART_INF_F;
+          for (uint32_t i = first; i <= last; ++i)
+            Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
+          float Lc = 0.f, Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (uint32_t i = first; i <= last; ++i) {
+            const float* rec = p.partials + (size_t)(i + b) * PART_FLOATS;
+            const float mi = __ldcg(rec + QH * HD + hq);
+            const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
+            Lc += __ldcg(rec + QH * HD + QH + hq) * fi;
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0));
+            const float4 w = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0 + 4));
+            Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
+            Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
+          }
+          const float inv = 1.f / Lc;
+          __align__(16) __half o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * inv);
+          *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+              *reinterpret_cast<uint4*>(o);
+        }
+        named_bar_sync(1, CONSUMER_THREADS);
+      }
+      break;
     }
-
-    if (s1 >= t1) break;
     ++b;
     while (tile_off[b + 1] <= s1) ++b;  // skip sequences with no tiles
   }
@@ -605,6 +749,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
 }  // namespace decode
 
 // ----------------------------------------------------------------- launcher
+int decode_block_threads() { return decode::THREADS; }
+
 size_t decode_workspace_bytes(uint32_t batch, int num_sms) {
   const size_t header = 256;
   const size_t tickets = ((size_t)batch * 4 + 255) / 256 * 256;

@@ -481,6 +481,7 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t rows, uint32_t heads,
 }  // namespace ptc
 
 int prefill_query_tile() { return ptc::QT * ptc::TOK; }
+int prefill_block_threads() { return ptc::THREADS; }
 
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   static bool attr_set[64] = {};

@@ -182,7 +182,7 @@ int pvlc_plan_vision_varlen(const uint32_t* cu, uint32_t segments, uint32_t toke
   plan->grid[0] = heads;
   plan->grid[1] = items;
   plan->grid[2] = 1;
-  plan->block[0] = 384;
+  plan->block[0] = (uint32_t)vision_block_threads();
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = items * heads;
   plan->output_elements = (uint64_t)tokens * heads * head_dim;
@@ -264,7 +264,7 @@ int pvlc_plan_decoder_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_
   plan->grid[0] = PVLC_DECODER_KV_HEADS;   // one CTA per (KV group, 32-token block)
   plan->grid[1] = (tokens + bm - 1) / bm;
   plan->grid[2] = 1;
-  plan->block[0] = 512;
+  plan->block[0] = (uint32_t)prefill_block_threads();
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = plan->grid[0] * plan->grid[1];
   plan->output_elements = (uint64_t)tokens * 16 * 128;
@@ -318,7 +318,7 @@ int pvlc_plan_decode(const uint32_t* cache_tokens, uint32_t batch, uint32_t capa
   }
   plan->grid[0] = (uint32_t)(tiles < (uint64_t)sms ? tiles : (uint64_t)sms);
   plan->grid[1] = plan->grid[2] = 1;
-  plan->block[0] = 288;
+  plan->block[0] = (uint32_t)decode_block_threads();
   plan->block[1] = plan->block[2] = 1;
   plan->work_items = (uint32_t)tiles;
   plan->output_elements = (uint64_t)batch * 16 * 128;

@@ -29,6 +29,7 @@ struct DecodeArgs {
   int num_ctas;
 };
 size_t decode_workspace_bytes(uint32_t batch, int num_sms);
+int decode_block_threads();
 int decode_launch(const DecodeArgs& a, cudaStream_t stream);
 
 struct VisionArgs {
@@ -42,6 +43,7 @@ struct VisionArgs {
   pvlc_half* out;
 };
 int vision_query_tile();
+int vision_block_threads();
 // Scratch for the rotated q and k (2 x tokens x heads x 72 fp16).
 size_t vision_workspace_bytes(uint32_t tokens, uint32_t heads);
 // workspace: vision_workspace_bytes of device memory when rope tables are
@@ -63,6 +65,7 @@ struct PrefillArgs {
   pvlc_half* out;
 };
 int prefill_query_tile();
+int prefill_block_threads();
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream);
 
 int device_sm_count();

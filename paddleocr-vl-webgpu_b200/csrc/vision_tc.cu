@@ -523,6 +523,7 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
 }  // namespace vtc
 
 int vision_query_tile() { return vtc::QT * vtc::BM; }
+int vision_block_threads() { return vtc::THREADS; }
 
 size_t vision_workspace_bytes(uint32_t tokens, uint32_t heads) {
   return 2ull * tokens * heads * vtc::HD * sizeof(__half);
