@@ -20,19 +20,28 @@
 //
 // GQA packing: a Q tile is 16 tokens x the 8 query heads of one KV group =
 // 128 MMA rows (row r = token r/8, head r%8), loaded by one 3-D TMA box, so a
-// K/V tile of 128 keys serves all 8 heads.  One CTA = (KV head, two
-// consecutive 16-token blocks); its two Q tiles ping-pong on the MMA warp.
-// Causal: K tiles 0 .. diagonal only, masking inside tiles that cross it.
+// K/V tile of 128 keys serves all 8 heads.  One CTA = (KV head, one Q tile);
+// its causal key range (K tiles 0 .. the diagonal) is split between two
+// streams, even and odd K tiles, with their own S and O in TMEM, which
+// ping-pong on the MMA warp.  The chain of dependent K tiles per CTA is
+// therefore at most ceil(13 / 2) = 7 at T = 1564 (a CTA holding all of a
+// 32-token block's keys had 13), over 2 x ceil(T / 16) CTAs; the two
+// streams' (O, m, l) are merged inside the CTA at the end.
+// Causal masking inside tiles that cross the diagonal.
 // head_dim 128 = two 64-dim blocks of 128-byte rows (128B swizzle); QK = 8 x
 // K16 steps (M128 N128), PV = 8 x K16 steps (M128 N128, V MN-major across
 // both blocks), P from TMEM.
 //
-//   warps 0-3, 4-7  softmax for Q tile 0 / 1: thread i owns row i = TMEM lane
-//                   i; rotates its Q row once (M-RoPE), then per K tile the
-//                   online softmax (f32, exp2 domain) and P (fp16) over S
-//   warp 8          TMA producer: both Q tiles, then K/V tiles (2 stages)
-//   warp 9          MMA issuer (one thread)
-// TMEM (512 columns): S/P of tile t at [128t, 128t+128), O at [256+128t, +128).
+//   warps 0-3, 4-7  softmax for stream 0 / 1: thread i owns row i = TMEM lane
+//                   i; both rotate their half of the Q tile's dims once
+//                   (M-RoPE), then per K tile of the stream the online
+//                   softmax (f32, exp2 domain) and P (fp16) over S; at the
+//                   end each writes output columns 64t..64t+63 from both
+//                   streams' O
+//   warp 8          TMA producer: the Q tile, then K/V tiles (3 stages)
+//   warp 9          MMA issuer (the whole warp walks the schedule, one
+//                   elected lane issues)
+// TMEM (512 columns): S/P of stream t at [128t, 128t+128), O at [256+128t, +128).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -53,7 +62,8 @@ constexpr int QH = 16;
 constexpr int KVH = 2;
 constexpr int GROUP = 8;
 constexpr int TOK = 16;          // tokens per Q tile (x 8 heads = 128 rows)
-constexpr int QT = 2;            // Q tiles per CTA
+constexpr int QT = 1;            // Q tiles per CTA
+constexpr int STREAMS = 2;       // K-tile streams per CTA (even / odd K tiles)
 constexpr int BN = 128;          // keys per K/V tile
 constexpr int THREADS = 12 * 32;
 // launch: 384 threads x 168 registers; softmax warpgroups take 200, control 56
@@ -66,15 +76,21 @@ constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_STAGE = QT * Q_BYTES;
 constexpr uint32_t ST_K = 0, ST_V = 2 * SZ_W;
 constexpr uint32_t STAGE_BYTES = 4 * SZ_W;
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
-// q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2]
-constexpr int NBARS = 12;
+// q_full, q_ready, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_done[2], ml_ready
+constexpr int NBARS = 15;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "prefill shared memory exceeds the sm_100 limit");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;
+// Pairs c (of each 16-pair chunk of a score row) whose exponentials run on the
+// FMA / integer pipes (exp2_h2_poly) instead of MUFU.
+#ifndef PVLC_PREFILL_EXP_POLY_MASK
+#define PVLC_PREFILL_EXP_POLY_MASK 0x4924u
+#endif
+constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
 
 struct Maps {
   CUtensorMap q, k, v;   // k maps the KV cache (rotated keys), v the raw values
@@ -101,6 +117,9 @@ __global__ void __launch_bounds__(256) kv_rope_kernel(const __half* __restrict__
                                                       uint32_t rope_rows, uint32_t tokens,
                                                       __half* __restrict__ k_cache,
                                                       __half* __restrict__ v_cache) {
+  // the attention launch may start its prologue (barriers, TMEM, Q load and
+  // rotation) now; it waits for this kernel before reading the cache
+  pdl_launch_dependents();
   const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t c = gid & 7, head = (gid >> 3) & 1, token = gid >> 4;
   if (token >= tokens) return;
@@ -139,11 +158,12 @@ __device__ __forceinline__ uint8_t* chunk_addr(uint8_t* blk, int r, int c) {
   return blk + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in place.
+// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in
+// place: chunks c0..c0+3 of 8 dims (dims 8c..8c+7 and their partners 64 above).
 __device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const Params& p,
-                                          uint32_t token) {
+                                          uint32_t token, int c0) {
 #pragma unroll 2
-  for (int c = 0; c < 8; ++c) {
+  for (int c = c0; c < c0 + 4; ++c) {
     const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
     const size_t tb = ((size_t)axis * p.rope_rows + token) * HD + 8 * c;
     const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + tb);
@@ -185,21 +205,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
   uint64_t* q_full = bars + 0;
   uint64_t* q_ready = bars + 1;
-  uint64_t* kv_full = bars + 2;    // [2]
-  uint64_t* kv_empty = bars + 4;   // [2]
-  uint64_t* s_full = bars + 6;     // [2]
-  uint64_t* p_ready = bars + 8;    // [2]
-  uint64_t* o_done = bars + 10;    // [2]
+  uint64_t* kv_full = bars + 2;    // [3]
+  uint64_t* kv_empty = bars + 5;   // [3]
+  uint64_t* s_full = bars + 8;     // [2] per stream
+  uint64_t* p_ready = bars + 10;   // [2]
+  uint64_t* o_done = bars + 12;    // [2]
+  uint64_t* ml_ready = bars + 14;  // both streams' (m, l) are in the exchange area
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t g = blockIdx.x;                      // KV head
-  const uint32_t n_pairs = (p.tokens + QT * TOK - 1) / (QT * TOK);
-  const uint32_t pair = n_pairs - 1 - blockIdx.y;     // heaviest (latest) first
-  const uint32_t tok0 = pair * QT * TOK;              // first token of Q tile 0
-  const bool has1 = tok0 + TOK < p.tokens;
-  const uint32_t last_tok = umin32(tok0 + QT * TOK, p.tokens) - 1;
+  const uint32_t n_qt = (p.tokens + TOK - 1) / TOK;
+  const uint32_t qt = n_qt - 1 - blockIdx.y;          // heaviest (latest) first
+  const uint32_t tok0 = qt * TOK;                     // first token of the Q tile
+  const uint32_t last_tok = umin32(tok0 + TOK, p.tokens) - 1;
   const int nk = static_cast<int>(last_tok / BN) + 1;  // K tiles 0 .. the diagonal
+  // stream t takes K tiles t, t + 2, ...
+  const int nks[STREAMS] = {(nk + 1) / 2, nk / 2};
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -208,11 +230,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int t = 0; t < QT; ++t) {
+    for (int t = 0; t < STREAMS; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_ready[t], 4);
       mbar_init(&o_done[t], 1);
     }
+    mbar_init(ml_ready, 8);
     misc[1] = 0;
     fence_mbar_init();
   }
@@ -233,11 +256,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tma_prefetch_desc(&maps.q);
       tc::tma_prefetch_desc(&maps.k);
       tc::tma_prefetch_desc(&maps.v);
-      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
-      for (int t = 0; t < (has1 ? 2 : 1); ++t)
-        for (int b = 0; b < 2; ++b)
-          tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + b * SZ_W, &maps.q, 64 * b, GROUP * g,
-                          tok0 + t * TOK, q_full);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      for (int b = 0; b < 2; ++b)
+        tc::tma_load_3d(smem + OFF_Q + b * SZ_W, &maps.q, 64 * b, GROUP * g, tok0, q_full);
+      // keys are read from the cache that kv_rope_kernel (the preceding launch) writes
+      pdl_wait();
       int issued = 0;
       for (int j = 0; j < nk; ++j) {
         const int s = j % STAGES;
@@ -252,11 +275,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
         mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
-    } else if (warp == 9 && lane == 0) {
+    } else if (warp == 9) {
       // ---------------------------------------------------- MMA issuer
+      // Tile j lives in stage j % 3; stream t = j % 2.  Per step: PV of the
+      // stream's current tile, then QK of its next tile (two ahead), so PV
+      // and QK reach the tensor pipe back to back and the other stream's
+      // softmax overlaps them.
       constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
-      const int ntile = has1 ? 2 : 1;
       const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + OFF_STAGE);
       const uint64_t dq = tc::smem_desc(sq, 16, 1024, tc::kSw128);
       const uint64_t dk = tc::smem_desc(st0 + ST_K, 16, 1024, tc::kSw128);
@@ -264,175 +290,236 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t dv = tc::smem_desc(st0 + ST_V, SZ_W, 1024, tc::kSw128);
       auto qk = [&](int t, int s) {
         const uint32_t tS = tmem + 128u * t;
-        const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4), so = (uint64_t)s * (STAGE_BYTES >> 4);
+        const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {   // block ks/4, 32 bytes per K step within a block
-          const uint64_t off = (uint64_t)(ks >> 2) * (SZ_W >> 4) + 2 * (ks & 3);
-          tc::mma_ss(tS, dq + qo + off, dk + so + off, idesc_qk, ks > 0);
+          for (int ks = 0; ks < 8; ++ks) {   // block ks/4, 32 bytes per K step within a block
+            const uint64_t off = (uint64_t)(ks >> 2) * (SZ_W >> 4) + 2 * (ks & 3);
+            tc::mma_ss(tS, dq + off, dk + so + off, idesc_qk, ks > 0);
+          }
+          tc::commit(&s_full[t]);
         }
-        tc::commit(&s_full[t]);
+        __syncwarp();
       };
       auto pv = [&](int t, int s, bool first) {
         const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
         const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)     // 16 keys = two 1 KB groups per K step
-          tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
-        tc::commit(&o_done[t]);
+          for (int ks = 0; ks < 8; ++ks)     // 16 keys = two 1 KB groups per K step
+            tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+          tc::commit(&o_done[t]);
+          tc::commit(&kv_empty[s]);          // the stage's only tile is consumed
+        }
+        __syncwarp();
       };
-      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&kv_full[0], 0);
-      int done = 0;
+      constexpr uint32_t kAll = 0xffffffffu;
+      auto kv_ready = [&](int j) { return mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1); };
+      bool ok = __all_sync(kAll, mbar_wait(q_ready, 0) && kv_ready(0));
+      int done = 0;   // K tiles whose PV was issued
       if (ok) {
         tc::fence_after_sync();
-        for (int t = 0; t < ntile; ++t) qk(t, 0);
-        for (int j = 0; j < nk && ok && !misc[1]; ++j) {
-          const bool more = j + 1 < nk;
-          const int s = j % STAGES, s1 = (j + 1) % STAGES;
-          for (int t = 0; t < ntile; ++t) {
-            if (!mbar_wait(&p_ready[t], j & 1)) { ok = false; break; }
+        qk(0, 0);
+        if (nk > 1) {
+          ok = __all_sync(kAll, kv_ready(1));
+          if (ok) {
             tc::fence_after_sync();
-            pv(t, s, j == 0);
-            if (t == ntile - 1) tc::commit(&kv_empty[s]);
-            if (more) {
-              if (t == 0 && !mbar_wait(&kv_full[s1], ((j + 1) / STAGES) & 1)) { ok = false; break; }
-              tc::fence_after_sync();
-              qk(t, s1);
-            }
+            qk(1, 1);
           }
-          if (ok) done = j + 1;
+        }
+        for (int j = 0; j < nk && ok && !__any_sync(kAll, misc[1] != 0); ++j) {
+          const int t = j & 1, i = j >> 1;   // stream, its step
+          if (!__all_sync(kAll, mbar_wait(&p_ready[t], i & 1))) { ok = false; break; }
+          const bool more = j + 2 < nk;
+          if (more && !__all_sync(kAll, kv_ready(j + 2))) { ok = false; break; }
+          tc::fence_after_sync();
+          pv(t, j % STAGES, i == 0);
+          if (more) qk(t, (j + 2) % STAGES);
+          done = j + 1;
         }
       }
-      if (!ok) misc[1] = 1;
-      if (done > 0) {
-        for (int t = 0; t < ntile; ++t) mbar_wait(&o_done[t], (done - 1) & 1);
-        for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
-          mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+      if (!ok && lane == 0) misc[1] = 1;
+      // never exit with MMAs in flight or commit arrivals still pending
+      for (int t = 0; t < STREAMS; ++t) {
+        const int issued_t = (done + 1 - t) / 2;   // PVs issued on stream t
+        if (issued_t > 0) mbar_wait(&o_done[t], (issued_t - 1) & 1);
       }
+      for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
+        mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
     }
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
     // ------------------------------------------------------ softmax
-    const int t = wg;
-    const int i = tid - 128 * t;                     // row == TMEM lane
+    const int t = wg;                                // stream of this warpgroup
+    const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128u * t;
-    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
-    const uint32_t token = tok0 + t * TOK + (i >> 3);
+    const uint32_t token = tok0 + (i >> 3);
     const uint32_t head = GROUP * g + (i & 7);
-    const bool active = t == 0 || has1;
-    bool ok = true;
-    if (active) {
-      ok = mbar_wait(q_full, 0);
-      if (ok && token < p.tokens) {
-        uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
-        mrope_row(qb, qb + SZ_W, i, p, token);
-      }
-      fence_proxy_async_smem();
+    bool ok = mbar_wait(q_full, 0);
+    if (ok && token < p.tokens) {
+      // the two warpgroups rotate disjoint halves of the row's dims
+      mrope_row(smem + OFF_Q, smem + OFF_Q + SZ_W, i, p, token, 4 * t);
     }
+    fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(q_ready);
     if (!ok) misc[1] = 1;
 
-    if (active) {
-      const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
-      const uint64_t scale2 = f2_pack(scale, scale);
-      float m_run = -CUDART_INF_F, l_run = 0.f;
-      bool good = __all_sync(0xffffffffu, ok);
-      // rows 32w'..32w'+31 of this warp hold tokens +4w' .. +4w'+3
-      const uint32_t warp_tok_lo = tok0 + t * TOK + ((warp & 3) * 32 >> 3);
-      for (int j = 0; j < nk && good; ++j) {
-        if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], j & 1))) {
-          good = false;
-          break;
-        }
-        tc::fence_after_sync();
-        uint32_t sv[128];
-        tc::tmem_ld32(tS + 0, sv);
-        tc::tmem_ld32(tS + 32, sv + 32);
-        tc::tmem_ld32(tS + 64, sv + 64);
-        tc::tmem_ld32(tS + 96, sv + 96);
-        tc::tmem_wait_ld();
-        // causal mask where this tile reaches past the warp's first token;
-        // it also removes cache rows past the prompt (unwritten, any bits)
-        if (j * BN + BN - 1 > warp_tok_lo) {
-#pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (j * BN + c > token) sv[c] = __float_as_uint(-CUDART_INF_F);
-        }
-        float mx = __uint_as_float(sv[0]);
-#pragma unroll
-        for (int c = 1; c < 127; c += 2)
-          mx = fmax3(mx, __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
-        mx = fmaxf(mx, __uint_as_float(sv[127])) * scale;
-        const bool need = mx > m_run + RESCALE_THRESHOLD;
-        float alpha = 1.f;
-        if (need) {
-          alpha = fast_exp2(m_run - mx);
-          m_run = mx;
-          l_run *= alpha;
-        }
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1))) { good = false; break; }
-          tc::fence_after_sync();
-#pragma unroll
-          for (int cc = 0; cc < 128; cc += 16) {
-            uint32_t ov[16];
-            tc::tmem_ld16(tO + cc, ov);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tc::tmem_st16(tO + cc, ov);
-          }
-        }
-        // a row can only be fully masked before its first key (never here:
-        // key 0 <= every token); guard the subtraction anyway
-        const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
-        const uint64_t negm2 = f2_pack(-mm, -mm);
-        uint64_t sum2 = f2_pack(0.f, 0.f);
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int k = 32 * ch + 2 * c;
-            const float2 x = f2_unpack(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negm2));
-            const float a = fast_exp2(x.x), b = fast_exp2(x.y);
-            sum2 = f2_add(sum2, f2_pack(a, b));
-            pk[c] = pack_half2(a, b);
-          }
-          tc::tmem_st16(tS + 16 * ch, pk);
-        }
-        tc::tmem_wait_st();
-        const float2 sum = f2_unpack(sum2);
-        l_run += sum.x + sum.y;
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[t]);
+    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+    const uint64_t scale2 = f2_pack(scale, scale);
+    float m_run = -CUDART_INF_F, l_run = 0.f;
+    bool good = __all_sync(0xffffffffu, ok);
+    // rows 32w'..32w'+31 of this warp hold tokens +4w' .. +4w'+3
+    const uint32_t warp_tok_lo = tok0 + ((warp & 3) * 32 >> 3);
+    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+    for (int step = 0; step < nks[t] && good; ++step) {
+      const int j = 2 * step + t;                    // K tile
+      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], step & 1))) {
+        good = false;
+        break;
       }
-      if (!good) misc[1] = 1;
-      if (__all_sync(0xffffffffu, good && mbar_wait(&o_done[t], (nk - 1) & 1))) {
+      tc::fence_after_sync();
+      uint32_t sv[128];
+      tc::tmem_ld32(tS + 0, sv);
+      tc::tmem_ld32(tS + 32, sv + 32);
+      tc::tmem_ld32(tS + 64, sv + 64);
+      tc::tmem_ld32(tS + 96, sv + 96);
+      tc::tmem_wait_ld();
+      // causal mask where this tile reaches past the warp's first token;
+      // it also removes cache rows past the prompt (unwritten, any bits)
+      if (j * BN + BN - 1 > warp_tok_lo) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (j * BN + c > token) sv[c] = __float_as_uint(-CUDART_INF_F);
+      }
+      // row max over four independent chains
+      float m4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
+                     __uint_as_float(sv[3])};
+#pragma unroll
+      for (int c = 4; c < 124; c += 8) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          m4[e] = fmax3(m4[e], __uint_as_float(sv[c + 2 * e]), __uint_as_float(sv[c + 2 * e + 1]));
+      }
+      m4[0] = fmax3(m4[0], __uint_as_float(sv[124]), __uint_as_float(sv[125]));
+      m4[1] = fmax3(m4[1], __uint_as_float(sv[126]), __uint_as_float(sv[127]));
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
+      const bool need = mx > m_run + RESCALE_THRESHOLD;
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2(m_run - mx);
+        m_run = mx;
+        l_run *= alpha;
+      }
+      if (step > 0 && __any_sync(0xffffffffu, need)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (step - 1) & 1))) { good = false; break; }
         tc::fence_after_sync();
-        const bool store = token < p.tokens;
-        const float inv = 1.f / l_run;
-        __half* orow = p.out + ((size_t)token * QH + head) * HD;
 #pragma unroll
         for (int cc = 0; cc < 128; cc += 16) {
           uint32_t ov[16];
           tc::tmem_ld16(tO + cc, ov);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
-            v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
-            v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
-            v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
-            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
-          }
+          for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tc::tmem_st16(tO + cc, ov);
         }
-      } else {
-        misc[1] = 1;
       }
+      // a row whose keys in this stream are all masked keeps m = -inf: its
+      // P is 0 (guard the subtraction)
+      const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
+      // P = 2^(x - m) as fp16 pairs, split between two pipes as in the
+      // vision kernel: the pairs of EXP_POLY_MASK by the polynomial on the
+      // FMA / integer pipes, the others by one f32 -> f16x2 rounding and one
+      // MUFU operation per two values.  The row sum adds the fp16 P the PV
+      // product consumes, in f32, over two accumulator chains.
+      const uint64_t negm2 = f2_pack(-mm, -mm);
+      const uint64_t negmh2 = f2_pack(-mm - 0.5f, -mm - 0.5f);
+      uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int k = 32 * ch + 2 * c;
+          const uint64_t s2 = f2_pack(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
+          if ((EXP_POLY_MASK >> c) & 1u) {
+            pk[c] = exp2_h2_poly(f2_fma(s2, scale2, negmh2));
+          } else {
+            const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
+            pk[c] = ex2_h2(pack_half2(x.x, x.y));
+          }
+          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
+          sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
+        }
+        tc::tmem_st16(tS + 16 * ch, pk);
+      }
+      tc::tmem_wait_st();
+      const float2 sum = f2_unpack(f2_add(sum2[0], sum2[1]));
+      l_run += sum.x + sum.y;
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready[t]);
+    }
+    if (!good) misc[1] = 1;
+    // epilogue: each warpgroup waits for its own stream's last PV (its own
+    // o_done phases, which it tracks exactly) and posts (m, l) in its
+    // stream's S columns, which no MMA touches after that PV; ml_ready
+    // completing means both streams are done.  Then this warpgroup writes
+    // output columns 64t..64t+63 =
+    //   (O0 2^(m0-M) + O1 2^(m1-M)) / (l0 2^(m0-M) + l1 2^(m1-M))
+    const bool fin = __all_sync(0xffffffffu,
+                                good && (nks[t] == 0 || mbar_wait(&o_done[t], (nks[t] - 1) & 1)));
+    if (fin) {
+      tc::fence_after_sync();
+      uint32_t ml[16] = {};
+      ml[0] = __float_as_uint(m_run);
+      ml[1] = __float_as_uint(l_run);
+      tc::tmem_st16(tS, ml);
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ml_ready);
+    if (__all_sync(0xffffffffu, fin && mbar_wait(ml_ready, 0))) {
+      tc::fence_after_sync();
+      uint32_t x0[16], x1[16];
+      tc::tmem_ld16(tmem + lane_base, x0);           // stream 0's (m, l)
+      tc::tmem_ld16(tmem + lane_base + 128u, x1);    // stream 1's (m, l)
+      tc::tmem_wait_ld();
+      const float m0 = __uint_as_float(x0[0]), l0 = __uint_as_float(x0[1]);
+      const float m1 = nks[1] > 0 ? __uint_as_float(x1[0]) : -CUDART_INF_F;
+      const float l1 = nks[1] > 0 ? __uint_as_float(x1[1]) : 0.f;
+      const float M = fmaxf(m0, m1);
+      const float f0 = m0 == -CUDART_INF_F ? 0.f : fast_exp2(m0 - M);
+      const float f1 = m1 == -CUDART_INF_F ? 0.f : fast_exp2(m1 - M);
+      const float inv = 1.f / (l0 * f0 + l1 * f1);
+      const float a0 = f0 * inv, a1 = f1 * inv;
+      const bool store = token < p.tokens;
+      __half* orow = p.out + ((size_t)token * QH + head) * HD;
+      const uint32_t tO0 = tmem + lane_base + 256u, tO1 = tmem + lane_base + 384u;
+#pragma unroll
+      for (int cc = 64 * t; cc < 64 * t + 64; cc += 16) {
+        uint32_t o0[16], o1[16];
+        tc::tmem_ld16(tO0 + cc, o0);
+        if (nks[1] > 0) tc::tmem_ld16(tO1 + cc, o1);
+        tc::tmem_wait_ld();
+        float v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          v[e] = __uint_as_float(o0[e]) * a0 + (nks[1] > 0 ? __uint_as_float(o1[e]) * a1 : 0.f);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint4 w;
+          w.x = pack_half2(v[8 * h + 0], v[8 * h + 1]);
+          w.y = pack_half2(v[8 * h + 2], v[8 * h + 3]);
+          w.z = pack_half2(v[8 * h + 4], v[8 * h + 5]);
+          w.w = pack_half2(v[8 * h + 6], v[8 * h + 7]);
+          if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
+        }
+      }
+    } else {
+      misc[1] = 1;
     }
   }
 
@@ -500,8 +587,8 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
       !ptc::make_map(&maps.k, a.k_cache, a.capacity, ptc::KVH, 1, ptc::BN) ||
       !ptc::make_map(&maps.v, a.v, a.tokens, ptc::KVH, 1, ptc::BN))
     return PVLC_CUDA_ERROR;
-  const uint32_t n_pairs = (a.tokens + ptc::QT * ptc::TOK - 1) / (ptc::QT * ptc::TOK);
-  if (n_pairs > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
+  const uint32_t n_qt = (a.tokens + ptc::TOK - 1) / ptc::TOK;
+  if (n_qt > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
   const uint32_t rope_threads = a.tokens * ptc::KVH * 8;
   ptc::kv_rope_kernel<<<(rope_threads + 255) / 256, 256, 0, stream>>>(
       reinterpret_cast<const __half*>(a.k), reinterpret_cast<const __half*>(a.v), a.rope_cos,
@@ -514,8 +601,19 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   p.rope_rows = a.rope_rows;
   p.tokens = a.tokens;
   p.out = reinterpret_cast<__half*>(a.out);
-  dim3 grid(ptc::KVH, n_pairs);
-  ptc::prefill_attn_kernel<<<grid, ptc::THREADS, ptc::SMEM_BYTES, stream>>>(maps, p);
+  // programmatic dependent launch: the attention CTAs' prologue overlaps
+  // kv_rope_kernel; only their cache reads wait for it (pdl_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ptc::KVH, n_qt);
+  cfg.blockDim = dim3(ptc::THREADS);
+  cfg.dynamicSmemBytes = ptc::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, ptc::prefill_attn_kernel, maps, p) != cudaSuccess) return PVLC_CUDA_ERROR;
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 

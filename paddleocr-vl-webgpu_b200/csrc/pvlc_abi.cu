@@ -92,7 +92,7 @@ int check_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_rows) {
   if (tokens == 0 || capacity == 0 || rope_rows == 0) return PVLC_ZERO_DIMENSION;
   if (tokens > capacity) return PVLC_CAPACITY_EXHAUSTED;
   if (tokens > rope_rows) return PVLC_INVALID_DECODER_GEOMETRY;
-  const uint64_t n_tiles = (tokens + 31) / 32;
+  const uint64_t n_tiles = (tokens + 15) / 16;   // one CTA per 16-token Q tile and KV head
   if (n_tiles > 65535) return PVLC_INVALID_DECODER_GEOMETRY;
   return PVLC_OK;
 }
@@ -261,7 +261,7 @@ int pvlc_plan_decoder_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_
   if (!plan) return PVLC_NULL_POINTER;
   memset(plan, 0, sizeof(*plan));
   const uint32_t bm = (uint32_t)prefill_query_tile();
-  plan->grid[0] = PVLC_DECODER_KV_HEADS;   // one CTA per (KV group, 32-token block)
+  plan->grid[0] = PVLC_DECODER_KV_HEADS;   // one CTA per (KV group, 16-token Q tile)
   plan->grid[1] = (tokens + bm - 1) / bm;
   plan->grid[2] = 1;
   plan->block[0] = (uint32_t)prefill_block_threads();

@@ -251,6 +251,17 @@ __device__ __forceinline__ uint32_t exp2_h2_poly(uint64_t xh2) {
   return __byte_perm(t0 * 1024u + q0, t1 * 1024u + q1, 0x5410);
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the preceding kernel of its
+// stream still runs, once every CTA of that kernel has called
+// pdl_launch_dependents (or exited); it must call pdl_wait before it reads
+// anything the preceding kernel writes, which returns once that kernel has
+// completed and its memory is visible.  Both are no-ops without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier over `threads` threads (a multiple of 32) with id `id` (1..15).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
