@@ -142,6 +142,9 @@ __global__ void __launch_bounds__(256)
                        const float* __restrict__ cs, const float* __restrict__ sn,
                        __half* __restrict__ q_rot, __half* __restrict__ k_rot, uint32_t heads,
                        uint64_t quads) {
+  // the attention launch may start its prologue (barriers, TMEM) now; it
+  // waits for this kernel before loading the rotated q and k
+  pdl_launch_dependents();
   const uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= quads) return;
   const uint64_t row = g / QUADS;               // token * heads + head
@@ -230,6 +233,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tma_prefetch_desc(&maps.q0);
       tc::tma_prefetch_desc(&maps.k0);
       tc::tma_prefetch_desc(&maps.v0);
+      // q and k come from the rotation pass (the preceding launch, when rotated)
+      pdl_wait();
       mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
       for (int t = 0; t < (has1 ? 2 : 1); ++t) {
         tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES, &maps.q0, 0, head, q0 + t * BM, q_full);
@@ -583,8 +588,20 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, vo
   vtc::Params p;
   p.out = reinterpret_cast<__half*>(a.out);
   p.heads = a.heads;
-  dim3 grid(a.heads, items);
-  vtc::vision_tc_kernel<<<grid, vtc::THREADS, vtc::SMEM_BYTES, stream>>>(maps, p, sc);
+  // programmatic dependent launch: the attention CTAs' prologue overlaps the
+  // tail of the rotation pass; their q/k loads wait for it (pdl_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.heads, items);
+  cfg.blockDim = dim3(vtc::THREADS);
+  cfg.dynamicSmemBytes = vtc::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.rope_cos != nullptr ? 1 : 0;
+  if (cudaLaunchKernelEx(&cfg, vtc::vision_tc_kernel, maps, p, sc) != cudaSuccess)
+    return PVLC_CUDA_ERROR;
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 
