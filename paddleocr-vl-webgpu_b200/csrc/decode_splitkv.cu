@@ -175,6 +175,12 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const uint32_t B = p.batch;
+  // Programmatic dependent launch: this grid may have been launched before
+  // the preceding kernel of the stream finished; nothing is read before it
+  // has (pdl_wait).  The next launch may then be scheduled early: its CTAs
+  // take an SM as soon as one of this grid's CTAs leaves it.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // ---- schedule: per-sequence tile counts (every thread), then an in-place
   // exclusive prefix sum over them (warp 0)
@@ -787,7 +793,17 @@ int decode_launch(const DecodeArgs& a, cudaStream_t stream) {
   p.tickets = reinterpret_cast<uint32_t*>(ws + 256);
   p.partials = reinterpret_cast<float*>(ws + 256 + ((size_t)a.batch * 4 + 255) / 256 * 256);
   p.out = reinterpret_cast<__half*>(a.out);
-  decode::decode_kernel<<<a.num_ctas, decode::THREADS, decode::SMEM_BYTES, stream>>>(p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.num_ctas);
+  cfg.blockDim = dim3(decode::THREADS);
+  cfg.dynamicSmemBytes = decode::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, decode::decode_kernel, p) != cudaSuccess) return PVLC_CUDA_ERROR;
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 
