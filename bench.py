@@ -504,6 +504,10 @@ def main():
             import torch.distributed as tdist
 
             from pvlc_b200 import dist as pdist
+            # NCCL prints its version banner on stdout under NCCL_DEBUG=VERSION;
+            # stdout carries only the JSON line
+            if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+                os.environ["NCCL_DEBUG"] = "WARN"
             torch.cuda.set_device(local_rank)
             pdist.init("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
             dist = tdist
