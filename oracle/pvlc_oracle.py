@@ -38,8 +38,9 @@ class OracleError(RuntimeError):
 
 def build() -> str:
     """Compile the oracle with its Makefile (only when the library is missing or stale)."""
-    src = os.path.join(_HERE, "pvlc_oracle.cpp")
-    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, f) for f in ("pvlc_oracle.cpp", "pvlc_model_oracle.cpp")]
+    if not os.path.exists(_LIB_PATH) or \
+            os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
 
@@ -229,3 +230,129 @@ def decode_mrope_position(cache_position, rope_delta):
     _check(lib().pvlc_oracle_decode_mrope_position(ctypes.c_uint32(cache_position),
                                                    ctypes.c_int64(rope_delta), ctypes.byref(out)))
     return int(out.value)
+
+
+# ----------------------------------------------------------------- model level
+def linear(x, weight, bias=None):
+    """x [rows, in] @ weight[out, in]^T (+ bias): the reference's linear_f32 order."""
+    x, w = _f32(x), _f32(weight)
+    rows, iw = x.reshape(-1, x.shape[-1]).shape
+    ow = w.shape[0]
+    b = None if bias is None else _f32(bias)
+    out = np.empty((rows, ow), np.float32)
+    _check(lib().pvlc_oracle_linear(_p(x), ctypes.c_uint32(rows), ctypes.c_uint32(iw), _p(w),
+                                    _p(b) if b is not None else None, ctypes.c_uint32(ow),
+                                    _p(out)))
+    return out
+
+
+def rms_norm(x, weight, eps):
+    x, w = _f32(x), _f32(weight)
+    out = np.empty_like(x)
+    rows, width = x.reshape(-1, x.shape[-1]).shape
+    _check(lib().pvlc_oracle_rms_norm(_p(x), ctypes.c_uint32(rows), ctypes.c_uint32(width), _p(w),
+                                      ctypes.c_float(eps), _p(out)))
+    return out
+
+
+def layer_norm(x, weight, bias, eps):
+    x, w, b = _f32(x), _f32(weight), _f32(bias)
+    out = np.empty_like(x)
+    rows, width = x.reshape(-1, x.shape[-1]).shape
+    _check(lib().pvlc_oracle_layer_norm(_p(x), ctypes.c_uint32(rows), ctypes.c_uint32(width),
+                                        _p(w), _p(b), ctypes.c_float(eps), _p(out)))
+    return out
+
+
+def prefill_last_logits(final_norm, lm_head):
+    fn, w = _f32(final_norm), _f32(lm_head)
+    tokens, hidden = fn.reshape(-1, w.shape[1]).shape
+    out = np.empty(w.shape[0], np.float32)
+    _check(lib().pvlc_oracle_prefill_last_logits(_p(fn), ctypes.c_uint32(tokens),
+                                                 ctypes.c_uint32(hidden), _p(w),
+                                                 ctypes.c_uint32(w.shape[0]), _p(out)))
+    return out
+
+
+DECODER_TRACE_FIELDS = ("norm1", "query", "key", "value", "mrope_query", "mrope_key",
+                        "attention_context", "attention_output", "attention_residual", "norm2",
+                        "mlp_gate", "mlp_up", "mlp_activation", "mlp_down", "output")
+
+
+def decoder_layer_prefill(x, tokens, hidden, intermediate, query_heads, kv_heads, head_dim, eps,
+                          sections, raw_cos, raw_sin, weights):
+    """One f32 decoder prefill layer; weights = (input_norm, q, k, v, o, post_norm, gate, up,
+    down).  Returns the trace as a dict of the reference's field names."""
+    x, c, s = _f32(x), _f32(raw_cos), _f32(raw_sin)
+    ws = [_f32(w) for w in weights]
+    qw, kw = query_heads * head_dim, kv_heads * head_dim
+    widths = {"norm1": hidden, "query": qw, "key": kw, "value": kw, "mrope_query": qw,
+              "mrope_key": kw, "attention_context": qw, "attention_output": hidden,
+              "attention_residual": hidden, "norm2": hidden, "mlp_gate": intermediate,
+              "mlp_up": intermediate, "mlp_activation": intermediate, "mlp_down": hidden,
+              "output": hidden}
+    trace = {k: np.empty(tokens * widths[k], np.float32) for k in DECODER_TRACE_FIELDS}
+    wp = (ctypes.c_void_p * 9)(*[w.ctypes.data for w in ws])
+    tp = (ctypes.c_void_p * 15)(*[trace[k].ctypes.data for k in DECODER_TRACE_FIELDS])
+    sec = _u32(sections)
+    _check(lib().pvlc_oracle_decoder_layer_prefill(
+        _p(x), ctypes.c_uint32(tokens), ctypes.c_uint32(hidden), ctypes.c_uint32(intermediate),
+        ctypes.c_uint32(query_heads), ctypes.c_uint32(kv_heads), ctypes.c_uint32(head_dim),
+        ctypes.c_float(eps), _p(sec), _p(c), _p(s), wp, tp))
+    return trace
+
+
+class ModelDims(ctypes.Structure):
+    """Mirror of pvlc_oracle_model_dims (oracle/pvlc_model_oracle.cpp)."""
+    _fields_ = [("vision_theta", ctypes.c_double), ("decoder_theta", ctypes.c_double),
+                ("vision_eps", ctypes.c_float), ("projector_eps", ctypes.c_float),
+                ("decoder_eps", ctypes.c_float), ("reserved", ctypes.c_float)] + \
+               [(n, ctypes.c_uint32) for n in (
+                   "vision_layers", "vision_hidden", "vision_heads", "vision_head_dim",
+                   "vision_intermediate", "patch_input", "pos_side", "merge", "decoder_layers",
+                   "decoder_hidden", "query_heads", "kv_heads", "head_dim",
+                   "decoder_intermediate", "vocab", "eos_token_id", "image_token_id",
+                   "vision_start_token_id")] + \
+               [("sections", ctypes.c_uint32 * 3), ("reserved2", ctypes.c_uint32)]
+
+
+def generate(dims: dict, vision_w, projector_w, decoder_w, patches, grids, input_ids,
+             max_new_tokens, fp16_storage=True, want_logits=False, want_features=False):
+    """One request end to end (pvlc_oracle_generate).  Weight lists hold fp16 numpy arrays in
+    the documented order.  Returns dict(tokens, logits?, vision?, projector?)."""
+    d = ModelDims()
+    for k, v in dims.items():
+        if k == "sections":
+            d.sections[:] = list(v)
+        else:
+            setattr(d, k, v)
+    keep = []
+
+    def table(ws):
+        arrs = [np.ascontiguousarray(w).view(np.uint16) for w in ws]
+        keep.extend(arrs)
+        return (ctypes.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+
+    vt, pt, dt = table(vision_w), table(projector_w), table(decoder_w)
+    p = _f32(patches)
+    g = _u32(grids).reshape(-1)
+    ids = _u32(input_ids)
+    toks = np.zeros(max_new_tokens, np.uint32)
+    n = ctypes.c_uint32(0)
+    logits = np.empty((max_new_tokens, d.vocab), np.float32) if want_logits else None
+    n_patches = int(sum(int(g[i]) * int(g[i + 1]) * int(g[i + 2]) for i in range(0, len(g), 3)))
+    vis = np.empty((n_patches, d.vision_hidden), np.float32) if want_features else None
+    proj = (np.empty((n_patches // (d.merge * d.merge), d.decoder_hidden), np.float32)
+            if want_features else None)
+    _check(lib().pvlc_oracle_generate(
+        ctypes.byref(d), vt, pt, dt, _p(p), _p(g), ctypes.c_uint32(len(g) // 3), _p(ids),
+        ctypes.c_uint32(len(ids)), ctypes.c_uint32(max_new_tokens),
+        ctypes.c_int(1 if fp16_storage else 0), _p(toks), ctypes.byref(n),
+        _p(logits) if logits is not None else None, _p(vis) if vis is not None else None,
+        _p(proj) if proj is not None else None))
+    out = {"tokens": toks[: n.value].astype(np.int64).tolist()}
+    if want_logits:
+        out["logits"] = logits[: n.value]
+    if want_features:
+        out["vision"], out["projector"] = vis, proj
+    return out
