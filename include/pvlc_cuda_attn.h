@@ -203,6 +203,24 @@ int pvlc_attn_decode_noalloc(const pvlc_half* q, const pvlc_half* k_new, const p
                              pvlc_half* out, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Vision preprocessing on the device (engine glue beside the attention path).
+ *
+ * Replaces the reference's host-side canonical_rgb8_to_patches
+ * (crates/pvlc-cpu-ref/src/lib.rs:2515-2563) after smart_resize has chosen
+ * the output size (:2442-2513): Pillow bicubic resample of an [H, W, 3] RGB8
+ * image to [out_height, out_width, 3] (22-bit fixed-point coefficients, int64
+ * accumulation, :3092-3273) and the normalised patch-major f32 values
+ * [(out_height/p)*(out_width/p), 3*p*p], bit-identical to the host path.
+ * The coefficient tables are computed on the host and copied to `workspace`
+ * on `stream` (pageable copies, so the call may block briefly).
+ */
+size_t pvlc_image_patches_workspace_bytes(uint32_t height, uint32_t width, uint32_t out_height,
+                                          uint32_t out_width);
+int pvlc_image_patches(const uint8_t* rgb, uint32_t height, uint32_t width, uint32_t out_height,
+                       uint32_t out_width, uint32_t patch_size, void* workspace,
+                       size_t workspace_bytes, float* patches, void* stream);
+
+/* ----------------------------------------------------------------------------
  * Plans: the host-side half of the contract, callable without a GPU.
  * They run the same validation as the launch entry points and report the
  * launch geometry the library will use.

@@ -78,6 +78,9 @@ _SIGNATURES = {
     "pvlc_attn_decode_errors": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "pvlc_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32,
                                                 _U32, _U32, _P, _P]),
+    "pvlc_image_patches_workspace_bytes": (ctypes.c_size_t, [_U32, _U32, _U32, _U32]),
+    "pvlc_image_patches": (ctypes.c_int, [_P, _U32, _U32, _U32, _U32, _U32, _P, ctypes.c_size_t,
+                                          _P, _P]),
     "pvlc_plan_vision_varlen": (ctypes.c_int, [_P, _U32, _U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_prefill": (ctypes.c_int, [_U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_kv_session": (ctypes.c_int, [_U32, _U32, _U32, _U32, _U32,

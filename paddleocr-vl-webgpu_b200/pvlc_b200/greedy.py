@@ -276,6 +276,63 @@ def greedy_generate_chunked(prefill_top_k, initial_kv_caches, config: GreedyGene
             return GreedyChunkedGenerationTrace(state.into_trace(terminal), chunks)
 
 
+class BatchedGreedyState:
+    """The rules of GreedyGenerationState applied to B requests at once.
+
+    The batched engine decodes every request of a batch in lockstep and
+    reads back [steps, B] top-1 tokens per chunk; per request this applies
+    exactly GreedyGenerationState's rules (first token from the prefill, EOS
+    kept and terminal, stop at max_new_tokens, steps after a stop ignored)
+    without a Python object per request, layer and step.  Top-1 ties are
+    resolved on the device by argmax's first (smallest) index, the same rule
+    as compare_top_k_entries for finite logits.
+    """
+
+    def __init__(self, first_tokens, max_new_tokens: int, eos_token_id: int):
+        import numpy as np
+        first = np.asarray(first_tokens, dtype=np.int64).reshape(-1)
+        if max_new_tokens <= 0 or first.size == 0:
+            raise GreedyError(DIMENSION_MISMATCH, "generation config")
+        self.max_new_tokens = int(max_new_tokens)
+        self.eos = int(eos_token_id)
+        self.tokens = np.zeros((first.size, self.max_new_tokens), np.int64)
+        self.tokens[:, 0] = first
+        self.count = np.ones(first.size, np.int64)
+        self.eos_stop = first == self.eos
+        self.done = self.eos_stop | (self.count == self.max_new_tokens)
+        self.decode_steps = np.zeros(first.size, np.int64)
+
+    def remaining_decode_steps(self) -> int:
+        import numpy as np
+        active = ~self.done
+        return int((self.max_new_tokens - self.count[active]).max()) if active.any() else 0
+
+    def apply_steps(self, steps) -> None:
+        """steps: [S, B] top-1 tokens of S consecutive decode steps."""
+        import numpy as np
+        steps = np.asarray(steps, dtype=np.int64)
+        for row in steps:
+            active = ~self.done
+            if not active.any():
+                break
+            idx = np.nonzero(active)[0]
+            self.tokens[idx, self.count[idx]] = row[idx]
+            self.count[idx] += 1
+            self.decode_steps[idx] += 1
+            eos = row[idx] == self.eos
+            self.eos_stop[idx] |= eos
+            self.done[idx] = eos | (self.count[idx] == self.max_new_tokens)
+
+    def all_done(self) -> bool:
+        return bool(self.done.all())
+
+    def generated(self, b: int) -> List[int]:
+        return self.tokens[b, : self.count[b]].tolist()
+
+    def stop_reason(self, b: int) -> str:
+        return EOS_TOKEN if self.eos_stop[b] else MAX_NEW_TOKENS
+
+
 def pinned_greedy_generate(prefill_top_k, initial_kv_caches, max_new_tokens: int,
                            decode_step: DecodeStepFn) -> GreedyGenerationTrace:
     """crates/pvlc-cpu-ref/src/lib.rs:2381-2397."""

@@ -1,0 +1,441 @@
+"""End-to-end PaddleOCR-VL greedy OCR on B200: the engine around the attention path.
+
+Architecture (the reference's pinned PaddleOCR-VL-1.6 shapes; random-init fp16 weights):
+  * vision encoder: patch projection 3*14*14 -> 1152 (+bias), the learned 27x27
+    position table bilinearly interpolated to each image grid
+    (crates/pvlc-cpu-ref/src/lib.rs:156-217), 27 pre-LayerNorm layers (eps 1e-6;
+    q/k/v/o 1152 with bias; 2-D RoPE; bidirectional attention per image; GELU-tanh
+    MLP 4304), post LayerNorm (lib.rs:2880-3064);
+  * projector: LayerNorm (eps 1e-5), 2x2 merge to 4608, linear 4608 -> 4608,
+    GELU(erf), linear 4608 -> 1024 (lib.rs:2598-2678);
+  * decoder: embeddings 103,424 x 1024 with image rows replaced by projector
+    outputs (multimodal.rs:115-163), 18 pre-RMSNorm layers (eps 1e-5; q 2048,
+    k/v 256, o 2048 -> 1024, no bias; M-RoPE; causal GQA 16/2; SwiGLU 3072),
+    final RMSNorm, LM head (lib.rs:1305-1418, 1469-1568), greedy top-1 with EOS 2
+    (lib.rs:2201-2305).
+
+Precision: weights and every intermediate activation in fp16; residual streams,
+normalisation statistics and logits in f32.  Attention runs on this library's
+kernels through the C ABI (vision varlen, decoder causal prefill with the KV
+cache written in place, batched split-KV decode with the KV append fused);
+the dense layers are cuBLAS GEMMs and torch elementwise kernels on the same
+stream.  The batched decode step is captured once in a CUDA graph and
+replayed; tokens are read back once per chunk of steps, as the reference's
+chunked greedy driver does (lib.rs:2309-2366).
+
+Weight lists are in the canonical order shared with the CPU oracle
+(oracle/pvlc_model_oracle.cpp, pvlc_oracle_generate).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, asdict
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import abi, greedy, ops, positions
+
+PROMPT_PREFIX_IDS = (100273, 2969, 93963, 93919, 101305)          # browser_ocr_runtime.mjs:38-40
+OCR_PROMPT_SUFFIX_IDS = (101306, 93972, 2497, 93963, 23, 92267, 93963, 23)  # paddleocr_vl_tasks.mjs:4-6
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    vision_layers: int = 27
+    vision_hidden: int = 1152
+    vision_heads: int = 16
+    vision_head_dim: int = 72
+    vision_intermediate: int = 4304
+    patch_size: int = 14
+    channels: int = 3
+    pos_side: int = 27
+    vision_eps: float = 1e-6
+    merge: int = 2
+    projector_eps: float = 1e-5
+    decoder_layers: int = 18
+    hidden: int = 1024
+    query_heads: int = 16
+    kv_heads: int = 2
+    head_dim: int = 128
+    intermediate: int = 3072
+    vocab: int = 103_424
+    rms_eps: float = 1e-5
+    eos_token_id: int = 2
+    image_token_id: int = positions.IMAGE_TOKEN_ID
+    vision_start_token_id: int = positions.VISION_START_TOKEN_ID
+    vision_theta: float = positions.VISION_ROPE_THETA
+    decoder_theta: float = positions.DECODER_ROPE_THETA
+
+    @property
+    def patch_input(self) -> int:
+        return self.channels * self.patch_size * self.patch_size
+
+    def oracle_dims(self) -> dict:
+        """Field values of the CPU oracle's model-dims struct."""
+        return dict(vision_theta=self.vision_theta, decoder_theta=self.decoder_theta,
+                    vision_eps=self.vision_eps, projector_eps=self.projector_eps,
+                    decoder_eps=self.rms_eps, vision_layers=self.vision_layers,
+                    vision_hidden=self.vision_hidden, vision_heads=self.vision_heads,
+                    vision_head_dim=self.vision_head_dim,
+                    vision_intermediate=self.vision_intermediate, patch_input=self.patch_input,
+                    pos_side=self.pos_side, merge=self.merge,
+                    decoder_layers=self.decoder_layers, decoder_hidden=self.hidden,
+                    query_heads=self.query_heads, kv_heads=self.kv_heads,
+                    head_dim=self.head_dim, decoder_intermediate=self.intermediate,
+                    vocab=self.vocab, eos_token_id=self.eos_token_id,
+                    image_token_id=self.image_token_id,
+                    vision_start_token_id=self.vision_start_token_id,
+                    sections=positions.MROPE_SECTIONS)
+
+
+@dataclass
+class Weights:
+    vision: list
+    projector: list
+    decoder: list
+
+
+def init_weights(cfg: ModelConfig, seed: int = 0, device="cuda") -> Weights:
+    """Seeded random fp16 weights: linear weights and biases N(0, 0.02^2), norm scales
+    1 + N(0, 0.1^2); generated on the device."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def w(*shape, std=0.02):
+        return (torch.randn(shape, generator=g, device=device) * std).half()
+
+    def scale(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=g, device=device)).half()
+
+    H, I, P = cfg.vision_hidden, cfg.vision_intermediate, cfg.patch_input
+    vision = [w(H, P), w(H), w(cfg.pos_side * cfg.pos_side, H)]
+    for _ in range(cfg.vision_layers):
+        vision += [scale(H), w(H), w(H, H), w(H), w(H, H), w(H), w(H, H), w(H), w(H, H), w(H),
+                   scale(H), w(H), w(I, H), w(I), w(H, I), w(H)]
+    vision += [scale(H), w(H)]
+    M, D = H * cfg.merge * cfg.merge, cfg.hidden
+    projector = [scale(H), w(H), w(M, M), w(M), w(D, M), w(D)]
+    QW, KW, DI = cfg.query_heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.intermediate
+    decoder = [w(cfg.vocab, D)]
+    for _ in range(cfg.decoder_layers):
+        decoder += [scale(D), w(QW, D), w(KW, D), w(KW, D), w(D, QW), scale(D), w(DI, D),
+                    w(DI, D), w(D, DI)]
+    decoder += [scale(D), w(cfg.vocab, D)]
+    return Weights(vision, projector, decoder)
+
+
+def ocr_prompt_ids(image_tokens: int, cfg: ModelConfig = ModelConfig()):
+    """The engine's OCR prompt: prefix, vision_start, image tokens, task suffix
+    (web/engine/browser_ocr_runtime.mjs:38-40,415-421)."""
+    return list(PROMPT_PREFIX_IDS) + [cfg.image_token_id] * image_tokens + \
+        list(OCR_PROMPT_SUFFIX_IDS)
+
+
+def _rms(x32, w32, eps):
+    return (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps) * w32).half()
+
+
+def _bilinear_axis(source: int, target: int):
+    """crates/pvlc-cpu-ref/src/lib.rs:265-278 in f32 for every target index."""
+    idx = np.arange(target, dtype=np.float32)
+    if target == 1:
+        coord = np.zeros(1, np.float32)
+    else:
+        coord = idx * np.float32(source - 1) / np.float32(target - 1)
+    lo = np.minimum(np.floor(coord).astype(np.int64), source - 1)
+    hi = np.minimum(lo + 1, source - 1)
+    return lo, hi, (coord - lo.astype(np.float32)).astype(np.float32)
+
+
+class OcrEngine:
+    """Batched greedy OCR over images (one image per request)."""
+
+    def __init__(self, cfg: ModelConfig, weights: Weights, device=None,
+                 vision_batch_tokens: int = 80_000):
+        self.cfg = cfg
+        self.device = torch.device(device or "cuda")
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+        self.vision_batch_tokens = vision_batch_tokens
+        c = cfg
+        vw, pw, dw = weights.vision, weights.projector, weights.decoder
+        f32 = lambda t: t.float()   # noqa: E731
+        self.patch_w, self.patch_b, self.pos_table = vw[0], vw[1], f32(vw[2])
+        self.vlayers = []
+        for l in range(c.vision_layers):
+            lw = vw[3 + 16 * l: 3 + 16 * (l + 1)]
+            self.vlayers.append(dict(
+                ln1=(f32(lw[0]), f32(lw[1])), q=(lw[2], lw[3]), k=(lw[4], lw[5]),
+                v=(lw[6], lw[7]), o=(lw[8], lw[9]), ln2=(f32(lw[10]), f32(lw[11])),
+                fc1=(lw[12], lw[13]), fc2=(lw[14], lw[15])))
+        post = vw[3 + 16 * c.vision_layers:]
+        self.post_ln = (f32(post[0]), f32(post[1]))
+        self.proj = dict(ln=(f32(pw[0]), f32(pw[1])), l1=(pw[2], pw[3]), l2=(pw[4], pw[5]))
+        self.embed = dw[0]
+        self.dlayers = []
+        for l in range(c.decoder_layers):
+            lw = dw[1 + 9 * l: 1 + 9 * (l + 1)]
+            self.dlayers.append(dict(
+                n1=f32(lw[0]), q=lw[1], k=lw[2], v=lw[3], o=lw[4], n2=f32(lw[5]),
+                gate_up=torch.cat([lw[6], lw[7]], 0).contiguous(), down=lw[8]))
+        self.final_norm = f32(dw[1 + 9 * c.decoder_layers])
+        self.lm_head = dw[2 + 9 * c.decoder_layers]
+        self._grid_cache = {}
+        self._graph = None
+
+    # ------------------------------------------------------------- vision side
+    def _grid_tables(self, grid):
+        """Per-grid device tables: interpolated position embedding (f32), 2-D RoPE, merge order."""
+        key = tuple(grid)
+        if key in self._grid_cache:
+            return self._grid_cache[key]
+        t, h, w = key
+        S, dev = self.cfg.pos_side, self.device
+        y0, y1, yf = _bilinear_axis(S, h)
+        x0, x1, xf = _bilinear_axis(S, w)
+        tab = self.pos_table
+        Y0, X0 = np.meshgrid(y0, x0, indexing="ij")
+        Y1, X1 = np.meshgrid(y1, x1, indexing="ij")
+        YF, XF = np.meshgrid(yf, xf, indexing="ij")
+        gather = lambda yy, xx: tab[torch.from_numpy((yy * S + xx).reshape(-1)).to(dev)]  # noqa
+        tl, tr, bl, br = gather(Y0, X0), gather(Y0, X1), gather(Y1, X0), gather(Y1, X1)
+        xft = torch.from_numpy(XF.reshape(-1, 1)).to(dev)
+        yft = torch.from_numpy(YF.reshape(-1, 1)).to(dev)
+        top = tl + (tr - tl) * xft
+        bottom = bl + (br - bl) * xft
+        pos = (top + (bottom - top) * yft).repeat(t, 1)
+        cos, sin = positions.vision_rope_tables([key], self.cfg.vision_head_dim,
+                                                self.cfg.vision_theta)
+        m = self.cfg.merge
+        order = []
+        for tt in range(t):
+            for my in range(h // m):
+                for mx in range(w // m):
+                    for py in range(m):
+                        for px in range(m):
+                            order.append(tt * h * w + (my * m + py) * w + (mx * m + px))
+        entry = (pos, torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev),
+                 torch.tensor(order, dtype=torch.int64, device=dev))
+        self._grid_cache[key] = entry
+        return entry
+
+    def vision_features(self, patches, grids):
+        """patches [N, 588] (f32 or fp16, device) for the images `grids` (pre-merge (t,h,w))
+        packed in order -> encoder output [N, 1152] fp16."""
+        c = self.cfg
+        H, heads, hd = c.vision_hidden, c.vision_heads, c.vision_head_dim
+        N = patches.shape[0]
+        tabs = [self._grid_tables(g) for g in grids]
+        pos = torch.cat([tb[0] for tb in tabs], 0)
+        rcos = torch.cat([tb[1] for tb in tabs], 0).contiguous()
+        rsin = torch.cat([tb[2] for tb in tabs], 0).contiguous()
+        cu = [0]
+        for t, h, w in grids:
+            cu.append(cu[-1] + t * h * w)
+        if cu[-1] != N:
+            raise ValueError("patch count does not match the grids")
+        x = F.linear(patches.half(), self.patch_w, self.patch_b)
+        h32 = x.float() + pos
+        ws = torch.empty(ops.vision_workspace_bytes(N, heads, hd), dtype=torch.uint8,
+                         device=self.device)
+        ctx = torch.empty((N, heads, hd), dtype=torch.float16, device=self.device)
+        for L in self.vlayers:
+            n1 = F.layer_norm(h32, (H,), *L["ln1"], eps=c.vision_eps).half()
+            q = F.linear(n1, *L["q"]).view(N, heads, hd)
+            k = F.linear(n1, *L["k"]).view(N, heads, hd)
+            v = F.linear(n1, *L["v"]).view(N, heads, hd)
+            ops.vision_varlen_attention(q, k, v, cu, rcos, rsin, out=ctx, workspace=ws)
+            h32 += F.linear(ctx.view(N, H), *L["o"]).float()
+            n2 = F.layer_norm(h32, (H,), *L["ln2"], eps=c.vision_eps).half()
+            a = F.gelu(F.linear(n2, *L["fc1"]).float(), approximate="tanh").half()
+            h32 += F.linear(a, *L["fc2"]).float()
+        return F.layer_norm(h32, (H,), *self.post_ln, eps=c.vision_eps).half()
+
+    def project(self, feats, grids):
+        """crates/pvlc-cpu-ref/src/lib.rs:2598-2678: [N, 1152] fp16 -> [N/4, 1024] fp16."""
+        c = self.cfg
+        H, M = c.vision_hidden, c.vision_hidden * c.merge * c.merge
+        pre = F.layer_norm(feats.float(), (H,), *self.proj["ln"], eps=c.projector_eps).half()
+        order, base = [], 0
+        for g in grids:
+            order.append(self._grid_tables(g)[3] + base)
+            base += g[0] * g[1] * g[2]
+        merged = pre.index_select(0, torch.cat(order)).view(-1, M)
+        a = F.gelu(F.linear(merged, *self.proj["l1"]).float()).half()
+        return F.linear(a, *self.proj["l2"])
+
+    def encode_images(self, patches_list, grids):
+        """Vision + projector over many images, packed into sub-batches of at most
+        vision_batch_tokens patches.  Returns one [tokens_i, 1024] fp16 tensor per image."""
+        outs, i = [], 0
+        while i < len(grids):
+            j, n = i, 0
+            while j < len(grids) and (j == i or n + patches_list[j].shape[0] <=
+                                      self.vision_batch_tokens):
+                n += patches_list[j].shape[0]
+                j += 1
+            p = torch.cat(patches_list[i:j], 0) if j - i > 1 else patches_list[i]
+            proj = self.project(self.vision_features(p, grids[i:j]), grids[i:j])
+            m2 = self.cfg.merge * self.cfg.merge
+            outs.extend(torch.split(proj, [g[0] * g[1] * g[2] // m2 for g in grids[i:j]]))
+            i = j
+        return outs
+
+    # ------------------------------------------------------------ decoder side
+    def _layer_mlp(self, L, h32):
+        c = self.cfg
+        n2 = _rms(h32, L["n2"], c.rms_eps)
+        gu = F.linear(n2, L["gate_up"])
+        a = (F.silu(gu[:, : c.intermediate].float()) * gu[:, c.intermediate:].float()).half()
+        h32 += F.linear(a, L["down"]).float()
+
+    def _logits(self, last32):
+        fn = _rms(last32, self.final_norm, self.cfg.rms_eps)
+        return torch.mm(fn, self.lm_head.t(), out_dtype=torch.float32)
+
+    def generate(self, images_patches, grids, max_new_tokens: int, chunk: int = 16,
+                 record_logits: bool = False):
+        """Greedy OCR of B requests (one image each, same prompt template).
+
+        images_patches: list of [N_i, 588] device tensors; grids: list of (t, h, w).
+        Returns dict(tokens=list of lists, stop=list of reasons, logits=optional list of
+        [steps_i, vocab] f32 CPU tensors (the logits each token was chosen from))."""
+        c, dev = self.cfg, self.device
+        B = len(grids)
+        m2 = c.merge * c.merge
+        img = self.encode_images(images_patches, grids)
+        ids = [ocr_prompt_ids(g[0] * g[1] * g[2] // m2, c) for g in grids]
+        Ts = [len(x) for x in ids]
+        cap = max(Ts) + max_new_tokens + 1
+        QW, KW = c.query_heads * c.head_dim, c.kv_heads * c.head_dim
+        Lyr = c.decoder_layers
+        kc = torch.empty((Lyr, B, cap, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
+        vc = torch.empty_like(kc)
+        # ---- prefill: GEMMs over all prompts, attention per prompt
+        ids_t = torch.tensor([t for x in ids for t in x], dtype=torch.int64, device=dev)
+        emb = self.embed.index_select(0, ids_t)
+        is_img = ids_t == c.image_token_id
+        emb[is_img] = torch.cat(img, 0)
+        h32 = emb.float()
+        tables, deltas = [], []
+        for x, g in zip(ids, grids):
+            pos, delta = positions.mrope_position_ids(x, [g])
+            pc, ps = positions.mrope_tables(pos, delta, len(x), c.decoder_theta, c.head_dim)
+            tables.append((torch.from_numpy(pc).to(dev), torch.from_numpy(ps).to(dev)))
+            deltas.append(delta)
+        offs = np.concatenate([[0], np.cumsum(Ts)])
+        NT = int(offs[-1])
+        ctx = torch.empty((NT, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
+        for l, L in enumerate(self.dlayers):
+            n1 = _rms(h32, L["n1"], c.rms_eps)
+            q = F.linear(n1, L["q"]).view(NT, c.query_heads, c.head_dim)
+            k = F.linear(n1, L["k"]).view(NT, c.kv_heads, c.head_dim)
+            v = F.linear(n1, L["v"]).view(NT, c.kv_heads, c.head_dim)
+            for b in range(B):
+                s, e = int(offs[b]), int(offs[b + 1])
+                ops.decoder_prefill(q[s:e], k[s:e], v[s:e], tables[b][0], tables[b][1],
+                                    kc[l, b], vc[l, b], out=ctx[s:e])
+            h32 += F.linear(ctx.view(NT, QW), L["o"]).float()
+            self._layer_mlp(L, h32)
+        last = torch.tensor(offs[1:] - 1, dtype=torch.int64, device=dev)
+        logits0 = self._logits(h32.index_select(0, last))
+        first = torch.argmax(logits0, dim=-1)
+        rec = [logits0.cpu()] if record_logits else None
+        state = greedy.BatchedGreedyState(first.cpu().numpy(), max_new_tokens, c.eos_token_id)
+        # ---- batched decode, one CUDA graph per step shape
+        dec = _DecodeGraph(self, kc, vc, cap, first, torch.tensor(Ts, dtype=torch.int32),
+                           torch.tensor(deltas, dtype=torch.int32))
+        while not state.all_done():
+            n = min(chunk, state.remaining_decode_steps())
+            hist, lg = dec.run(n, record_logits)
+            state.apply_steps(hist.cpu().numpy())
+            if record_logits:
+                rec.append(lg.cpu())
+        out = dict(tokens=[state.generated(b) for b in range(B)],
+                   stop=[state.stop_reason(b) for b in range(B)])
+        if record_logits:
+            allg = torch.cat([r.unsqueeze(0) if r.dim() == 2 else r for r in rec], 0)  # [S,B,V]
+            out["logits"] = [allg[: state.count[b], b] for b in range(B)]
+        return out
+
+
+class _DecodeGraph:
+    """One batched decode step (embedding -> 18 layers with the fused decode attention ->
+    LM head -> argmax), captured in a CUDA graph over static buffers."""
+
+    def __init__(self, eng: OcrEngine, kc, vc, cap, first_tokens, prompt_lens, deltas):
+        c, dev = eng.cfg, eng.device
+        self.eng, self.cap = eng, cap
+        B = first_tokens.shape[0]
+        self.B = B
+        self.tok = first_tokens.clone().to(torch.int64)
+        self.ct = prompt_lens.to(dev).clone()                      # rows before the append
+        self.rope_row = (prompt_lens + deltas).to(dev).clone()     # decode position ct + delta
+        if int(self.rope_row.min()) < 0:
+            raise positions.PositionError("decode position is negative")
+        rows = int((prompt_lens + deltas).max()) + cap + 1
+        rc, rs = positions.linear_rope_tables(rows, c.decoder_theta, c.head_dim)
+        self.rcos, self.rsin = torch.from_numpy(rc).to(dev), torch.from_numpy(rs).to(dev)
+        self.kp = [torch.tensor([kc[l, b].data_ptr() for b in range(B)], dtype=torch.int64,
+                                device=dev) for l in range(c.decoder_layers)]
+        self.vp = [torch.tensor([vc[l, b].data_ptr() for b in range(B)], dtype=torch.int64,
+                                device=dev) for l in range(c.decoder_layers)]
+        self.ws = [ops.DecodeWorkspace(B, dev) for _ in range(c.decoder_layers)]
+        self.q = torch.empty((B, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
+        self.k = torch.empty((B, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
+        self.v = torch.empty_like(self.k)
+        self.ctx = torch.empty_like(self.q)
+        self.graph = None
+        self.logits = None
+
+    def _step(self):
+        eng, c = self.eng, self.eng.cfg
+        B = self.B
+        h32 = eng.embed.index_select(0, self.tok).float()
+        for l, L in enumerate(eng.dlayers):
+            n1 = _rms(h32, L["n1"], c.rms_eps)
+            torch.mm(n1, L["q"].t(), out=self.q.view(B, -1))
+            torch.mm(n1, L["k"].t(), out=self.k.view(B, -1))
+            torch.mm(n1, L["v"].t(), out=self.v.view(B, -1))
+            ops.decode(self.q, self.k, self.v, self.rcos, self.rsin, self.kp[l], self.vp[l],
+                       self.ct, self.cap, self.cap - 1, self.ws[l], rope_row=self.rope_row,
+                       out=self.ctx)
+            h32 += F.linear(self.ctx.view(B, -1), L["o"]).float()
+            eng._layer_mlp(L, h32)
+        self.logits = eng._logits(h32)
+        self.tok.copy_(torch.argmax(self.logits, dim=-1))
+        self.ct += 1
+        self.rope_row += 1
+
+    def _capture(self):
+        saved = (self.tok.clone(), self.ct.clone(), self.rope_row.clone())
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._step()           # warm-up: cuBLAS handles and workspaces
+        torch.cuda.current_stream().wait_stream(s)
+        # the warm-up wrote cache rows at ct, which the first real step rewrites
+        self.tok.copy_(saved[0])
+        self.ct.copy_(saved[1])
+        self.rope_row.copy_(saved[2])
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+
+    def run(self, steps: int, record_logits: bool = False):
+        if int(self.ct.max()) + steps >= self.cap:
+            raise abi.PvlcError(abi.CAPACITY_EXHAUSTED, "decode past the cache capacity")
+        if self.graph is None:
+            self._capture()
+        hist = torch.empty((steps, self.B), dtype=torch.int64, device=self.eng.device)
+        lg = [] if record_logits else None
+        for i in range(steps):
+            self.graph.replay()
+            hist[i].copy_(self.tok)
+            if record_logits:
+                lg.append(self.logits.clone())
+        flags = sum(w.errors() for w in self.ws)
+        if flags:
+            raise abi.PvlcError(abi.DEVICE_FAULT_FLAG, f"decode fault flags {flags:#x}")
+        return hist, (torch.stack(lg, 0) if record_logits else None)

@@ -147,3 +147,27 @@ def decode(q, k_new, v_new, rope_cos, rope_sin, k_cache_ptrs, v_cache_ptrs, cach
         int(max_cache_tokens), B, _ptr(workspace.buffer), workspace.nbytes, _ptr(out), _stream())
     abi.check(st, "pvlc_attn_decode")
     return out
+
+
+def image_patches(rgb, out_height: int, out_width: int, patch_size: int = 14, out=None,
+                  workspace=None):
+    """Bicubic resample of an [H, W, 3] uint8 CUDA image to (out_height, out_width) and its
+    normalised patch-major values [(out_height/p)*(out_width/p), 3*p*p] f32 (the
+    reference's canonical_rgb8_to_patches after smart_resize)."""
+    if not isinstance(rgb, torch.Tensor) or not rgb.is_cuda or rgb.dtype != torch.uint8 or \
+            rgb.dim() != 3 or rgb.shape[2] != 3 or not rgb.is_contiguous():
+        raise TypeError("rgb must be a contiguous [H, W, 3] uint8 CUDA tensor")
+    H, W = int(rgb.shape[0]), int(rgb.shape[1])
+    n = (out_height // patch_size) * (out_width // patch_size)
+    if out is None:
+        out = torch.empty((n, 3 * patch_size * patch_size), dtype=torch.float32,
+                          device=rgb.device)
+    _need(out, torch.float32, (n, 3 * patch_size * patch_size), "out")
+    need = int(abi.lib().pvlc_image_patches_workspace_bytes(H, W, out_height, out_width))
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=rgb.device)
+    _need(workspace, torch.uint8, None, "workspace")
+    st = abi.lib().pvlc_image_patches(_ptr(rgb), H, W, out_height, out_width, patch_size,
+                                      _ptr(workspace), workspace.numel(), _ptr(out), _stream())
+    abi.check(st, "pvlc_image_patches")
+    return out

@@ -294,3 +294,30 @@ def test_pinned_config_freezes_topology():
     cfg = G.pinned_greedy_generation_config(512)
     assert (cfg.layers, cfg.vocab_size, cfg.key_value_heads, cfg.head_dim, cfg.eos_token_id) == \
         (18, 103424, 2, 128, 2)
+
+
+def test_batched_state_applies_the_single_request_rules():
+    """BatchedGreedyState == GreedyGenerationState per request on random step streams."""
+    rng = np.random.default_rng(3)
+    eos, max_new, B, S = 2, 9, 6, 12
+    first = rng.integers(0, 6, B)
+    first[0] = eos                       # prefill EOS
+    steps = rng.integers(0, 6, (S, B))
+    batched = G.BatchedGreedyState(first, max_new, eos)
+    batched.apply_steps(steps[:5])
+    batched.apply_steps(steps[5:])
+    for b in range(B):
+        cfg = G.GreedyGenerationConfig(1, 8, 1, 2, max_new, eos)
+        it = iter(range(S))
+
+        def step(i, tok, caches, b=b):
+            s = next(it)
+            return G.GreedyDecodeStep([G.TopKEntry(int(steps[s, b]), 1.0)],
+                                      [Cache(caches[0].tokens + 1, 1, 2, None, None)])
+
+        ref = G.greedy_generate([G.TopKEntry(int(first[b]), 1.0)],
+                                [Cache(3, 1, 2, None, None)], cfg, step)
+        assert batched.generated(b) == ref.generated_tokens
+        assert batched.stop_reason(b) == ref.stop_reason
+        assert int(batched.decode_steps[b]) == ref.decode_steps
+    assert batched.all_done()
