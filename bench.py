@@ -11,7 +11,10 @@ read + q/out + appended row, per launch) and tokens/s/GPU.  The KV caches
 (~10 GB per GPU) are far larger than the 126 MB L2, so no flush is needed.
 
 Components (rank 0): vision varlen prefill (configs[1], TFLOP/s) and decoder
-causal prefill (configs[2], TFLOP/s), each timed with CUDA events.
+causal prefill (configs[2], TFLOP/s), each timed with CUDA events; and on every
+rank, end-to-end greedy OCR (configs[4]: random-init fp16 PaddleOCR-VL, 256
+noise pages of 1024x1024 sharded by request, 512 tokens each) through the
+engine's public API, tokens/s and requests/s (max time over ranks).
 
 --impl reference times the reference's algorithm on the host cores (the C++
 restatement of pvlc-cpu-ref in oracle/, because the Rust reference cannot be
@@ -274,6 +277,13 @@ def run_gpu(args, rank, world, local_rank, dist):
     components = {}
     if rank == 0 and not args.skip_components:
         components = run_components(args, dev, tf_peak, peak_src)
+    del kc, vc, kp, vp, q, kn, vn, out, ws, qh, knh, vnh, outh
+    torch.cuda.empty_cache()
+    if not args.skip_e2e:
+        # every rank runs its request shard (the collectives inside are taken by all)
+        e2e_res = run_e2e(args, dev, rank, world, dist)
+        if rank == 0:
+            components["e2e_greedy"] = e2e_res
     if rank != 0:
         return None
     line = {
@@ -412,7 +422,102 @@ def bench_prefill(dev, timeit, tf_peak, peak_src):
             "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
 
 
+def run_e2e(args, dev, rank, world, dist):
+    """end-to-end greedy OCR through the public engine API.
+
+    Random-init fp16 PaddleOCR-VL weights; seeded uniform-noise 1024x1024 RGB pages
+    (smart_resize -> 980x980 -> 4900 patches -> 1225 image tokens, 1238-token prompts);
+    args.e2e_requests requests sharded by index over the ranks; args.e2e_tokens greedy
+    tokens each (EOS stops a request early).  Timed per rank with CUDA events around
+    OcrEngine.recognize(): host->device page copies from pinned memory, device
+    preprocessing, vision encoder, projector, decoder prefill, CUDA-graph decode and the
+    token readbacks; max over ranks."""
+    import numpy as np
+    import torch
+
+    from pvlc_b200 import dist as pdist
+    from pvlc_b200 import model as M
+
+    cfg = M.ModelConfig()
+    weights = M.init_weights(cfg, seed=0, device=dev)
+    eng = M.OcrEngine(cfg, weights, dev)
+    mine = pdist.shard(args.e2e_requests, rank, world)
+    pages = []
+    for i in mine:
+        rng = np.random.default_rng(10_000 + i)
+        pages.append(torch.from_numpy(
+            rng.integers(0, 256, (1024, 1024, 3), dtype=np.uint8)).pin_memory())
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    eng.recognize(pages[:2], 4)          # warm-up: kernels, cuBLAS heuristics, graph machinery
+    barrier()
+    timings = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    res = eng.recognize(pages, args.e2e_tokens, timings=timings)
+    e1.record()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    tokens = sum(len(t) for t in res["tokens"])
+    eos = sum(1 for r in res["stop"] if r == "eos_token")
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    n = torch.tensor([tokens, len(mine), eos], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    ms_max = float(t.item())
+    tokens_all, reqs_all, eos_all = (int(x) for x in n.tolist())
+    out = {"workload": "configs[4] e2e greedy OCR, random-init fp16 PaddleOCR-VL, 1024x1024 "
+                       "noise pages -> 980x980 (1225 image tokens), OCR prompt",
+           "requests": reqs_all, "max_new_tokens": args.e2e_tokens, "n_gpus": world,
+           "generated_tokens": tokens_all, "eos_stops": eos_all, "ms": round(ms_max, 2),
+           "tokens_per_s": round(tokens_all / (ms_max * 1e-3), 1),
+           "tokens_per_s_per_gpu": round(tokens_all / (ms_max * 1e-3) / world, 1),
+           "requests_per_s": round(reqs_all / (ms_max * 1e-3), 3),
+           "rank0_breakdown_ms": {k: (round(v, 2) if isinstance(v, float) else v)
+                                  for k, v in timings.items()},
+           "h2d_bytes_per_request": 1024 * 1024 * 3,
+           "path": "pvlc_b200.model.OcrEngine.recognize (host pages in, token ids out)"}
+    if rank == 0 and not args.skip_cpu:
+        out["cpu_baseline"] = cpu_e2e_baseline(cfg, weights)
+    del eng, weights
+    torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------- CPU (oracle)
+def cpu_e2e_baseline(cfg, weights):
+    """The reference's f32 composition (the oracle) on one reduced request: a 112x112 page
+    (8x8 patches, 16 image tokens) and 4 greedy tokens, on the host cores."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    from pvlc_b200 import model as M
+    from pvlc_b200 import preprocess as P
+
+    host = [[t.cpu().numpy() for t in part]
+            for part in (weights.vision, weights.projector, weights.decoder)]
+    rgb = np.random.default_rng(10_000).integers(0, 256, (112, 112, 3), dtype=np.uint8)
+    pre = P.canonical_rgb8_to_patches(rgb, P.VisionPreprocessConfig(min_pixels=112 * 112,
+                                                                     max_pixels=112 * 112))
+    g = pre.image_grid_thw
+    ids = M.ocr_prompt_ids(g[0] * g[1] * g[2] // 4, cfg)
+    t0 = time.perf_counter()
+    r = O.generate(cfg.oracle_dims(), *host, pre.values, [g], ids, 4, fp16_storage=False)
+    el = time.perf_counter() - t0
+    return {"value": round(len(r["tokens"]) / el, 4), "unit": "tokens/s", "cores": O.threads(),
+            "kind": "port",
+            "sample": f"1 request, 112x112 page (16 image tokens, {len(ids)}-token prompt), "
+                      f"{len(r['tokens'])} greedy tokens, {el:.1f} s end to end "
+                      "(reduced: a 980x980 page is ~4e12 FLOP of vision encoder on the CPU)"}
+
+
+
 def cpu_decode_baseline(seconds: float):
     """The C++ restatement of pvlc-cpu-ref's decode step on the host cores, over a
     bounded sample of the decode-sweep workload (same length distribution)."""
@@ -477,7 +582,10 @@ def main():
     ap.add_argument("--seqs", type=int, default=SEQS_PER_GPU,
                     help="sequences per GPU (profiling runs use a smaller case)")
     ap.add_argument("--layers", type=int, default=LAYERS)
-    ap.add_argument("--only", choices=["vision", "prefill"], default=None,
+    ap.add_argument("--skip-e2e", action="store_true", help="skip configs[4] e2e greedy OCR")
+    ap.add_argument("--e2e-requests", type=int, default=256)
+    ap.add_argument("--e2e-tokens", type=int, default=512)
+    ap.add_argument("--only", choices=["vision", "prefill", "e2e"], default=None,
                     help="time one prefill component alone (profiling runs); prints its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -489,6 +597,11 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
+    if args.only == "e2e" and args.impl == "ours":
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(run_e2e(args, torch.device("cuda", 0), 0, 1, None)), flush=True)
+        return
     if args.only is not None and args.impl == "ours":
         import torch
         hbm_peak, tf_peak, peak_src = peaks()

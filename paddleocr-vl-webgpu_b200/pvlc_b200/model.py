@@ -283,6 +283,20 @@ class OcrEngine:
         return outs
 
     # ------------------------------------------------------------ decoder side
+    def _prompt_tables(self, ids, grid):
+        """M-RoPE tables [3, T, 128] (device) and rope delta of a prompt, cached per
+        (prompt, grid): every page of one size shares them."""
+        key = (tuple(ids), tuple(grid))
+        hit = self._grid_cache.get(key)
+        if hit is None:
+            c = self.cfg
+            pos, delta = positions.mrope_position_ids(ids, [grid])
+            pc, ps = positions.mrope_tables(pos, delta, len(ids), c.decoder_theta, c.head_dim)
+            hit = (torch.from_numpy(pc).to(self.device), torch.from_numpy(ps).to(self.device),
+                   delta)
+            self._grid_cache[key] = hit
+        return hit
+
     def _layer_mlp(self, L, h32):
         c = self.cfg
         n2 = _rms(h32, L["n2"], c.rms_eps)
@@ -294,8 +308,33 @@ class OcrEngine:
         fn = _rms(last32, self.final_norm, self.cfg.rms_eps)
         return torch.mm(fn, self.lm_head.t(), out_dtype=torch.float32)
 
+    def recognize(self, images, max_new_tokens: int = 512, chunk: int = 32,
+                  preprocess_config=None, timings: dict | None = None):
+        """Greedy OCR of host RGB8 pages ([H, W, 3] uint8 numpy arrays or CPU tensors).
+
+        Each page is copied to the device (pinned staging), resized and cut into patches
+        by the library's image kernel (smart_resize chooses the size), then generate()
+        runs the model.  Returns generate()'s dict."""
+        from . import preprocess
+        cfgp = preprocess_config or preprocess.MODEL_CONFIG
+        patches, grids = [], []
+        ws = None
+        for im in images:
+            t = im if isinstance(im, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(im))
+            if not t.is_pinned():
+                t = t.pin_memory()
+            d = t.to(self.device, non_blocking=True)
+            h, w = preprocess.smart_resize(int(t.shape[0]), int(t.shape[1]), cfgp)
+            need = int(abi.lib().pvlc_image_patches_workspace_bytes(int(t.shape[0]),
+                                                                    int(t.shape[1]), h, w))
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            patches.append(ops.image_patches(d, h, w, cfgp.patch_size, workspace=ws))
+            grids.append((1, h // cfgp.patch_size, w // cfgp.patch_size))
+        return self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings)
+
     def generate(self, images_patches, grids, max_new_tokens: int, chunk: int = 16,
-                 record_logits: bool = False):
+                 record_logits: bool = False, timings: dict | None = None):
         """Greedy OCR of B requests (one image each, same prompt template).
 
         images_patches: list of [N_i, 588] device tensors; grids: list of (t, h, w).
@@ -304,7 +343,13 @@ class OcrEngine:
         c, dev = self.cfg, self.device
         B = len(grids)
         m2 = c.merge * c.merge
+        ev = None
+        if timings is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
         img = self.encode_images(images_patches, grids)
+        if ev:
+            ev[1].record()
         ids = [ocr_prompt_ids(g[0] * g[1] * g[2] // m2, c) for g in grids]
         Ts = [len(x) for x in ids]
         cap = max(Ts) + max_new_tokens + 1
@@ -320,9 +365,8 @@ class OcrEngine:
         h32 = emb.float()
         tables, deltas = [], []
         for x, g in zip(ids, grids):
-            pos, delta = positions.mrope_position_ids(x, [g])
-            pc, ps = positions.mrope_tables(pos, delta, len(x), c.decoder_theta, c.head_dim)
-            tables.append((torch.from_numpy(pc).to(dev), torch.from_numpy(ps).to(dev)))
+            tc, ts, delta = self._prompt_tables(x, g)
+            tables.append((tc, ts))
             deltas.append(delta)
         offs = np.concatenate([[0], np.cumsum(Ts)])
         NT = int(offs[-1])
@@ -341,6 +385,8 @@ class OcrEngine:
         last = torch.tensor(offs[1:] - 1, dtype=torch.int64, device=dev)
         logits0 = self._logits(h32.index_select(0, last))
         first = torch.argmax(logits0, dim=-1)
+        if ev:
+            ev[2].record()
         rec = [logits0.cpu()] if record_logits else None
         state = greedy.BatchedGreedyState(first.cpu().numpy(), max_new_tokens, c.eos_token_id)
         # ---- batched decode, one CUDA graph per step shape
@@ -352,6 +398,13 @@ class OcrEngine:
             state.apply_steps(hist.cpu().numpy())
             if record_logits:
                 rec.append(lg.cpu())
+        if ev:
+            ev[3].record()
+            ev[3].synchronize()
+            timings.update(encode_ms=ev[0].elapsed_time(ev[1]),
+                           prefill_ms=ev[1].elapsed_time(ev[2]),
+                           decode_ms=ev[2].elapsed_time(ev[3]),
+                           decode_steps=int(state.decode_steps.max()))
         out = dict(tokens=[state.generated(b) for b in range(B)],
                    stop=[state.stop_reason(b) for b in range(B)])
         if record_logits:
