@@ -161,3 +161,39 @@ def test_workspace_entry_points_agree(cuda_lib):
              P(b), stream) == abi.OK
     torch.cuda.synchronize()
     assert torch.equal(ref, b)
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_many_ragged_segments_persistent_schedule(cuda_lib, rope):
+    """More work items than SMs and ragged segments (single-Q-tile items, partial K
+    tiles), with and without rope tables, against the oracle; a second call on the
+    same scratch gives the same bits."""
+    import pvlc_oracle as O
+    from pvlc_b200 import ops, positions
+    rng = np.random.default_rng(21)
+    lens = rng.integers(1, 700, size=48)
+    lens[:4] = [1, 128, 129, 257]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    T = int(cu[-1])
+    q = rng.standard_normal((T, H, D)).astype(np.float16)
+    k = rng.standard_normal((T, H, D)).astype(np.float16)
+    v = rng.standard_normal((T, H, D)).astype(np.float16)
+    dq, dk, dv = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    if rope:
+        grids = [(1, 1, int(n)) for n in lens]
+        c, s_ = positions.vision_rope_tables(grids)
+        tc, ts = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+        ws = torch.empty(ops.vision_workspace_bytes(T, H), dtype=torch.uint8, device="cuda")
+        out = ops.vision_varlen_attention(dq, dk, dv, cu, tc, ts, workspace=ws)
+        out2 = ops.vision_varlen_attention(dq, dk, dv, cu, tc, ts, workspace=ws)
+        qr, kr = O.vision_rope_apply_tables(q.astype(np.float32), k.astype(np.float32), T, H, D,
+                                            c, s_)
+    else:
+        out = ops.vision_varlen_attention(dq, dk, dv, cu)
+        out2 = ops.vision_varlen_attention(dq, dk, dv, cu)
+        qr, kr = q.astype(np.float32), k.astype(np.float32)
+    torch.cuda.synchronize()
+    ref = O.segmented_attention(qr, kr, v.astype(np.float32), T, H, D, cu)
+    err = float(np.abs(out.float().cpu().numpy().reshape(-1) - ref.reshape(-1)).max())
+    assert err <= 2e-3, err
+    assert torch.equal(out, out2)
