@@ -9,9 +9,11 @@
 //
 // Design (HBM-bound: ~8 FLOP per byte of KV):
 //   * Stream-K split: the batch's KV rows, cut into 32-row tiles, are laid
-//     end to end and split evenly over one CTA per SM, so every SM streams the
-//     same number of bytes whatever the per-sequence lengths are.  A CTA's
-//     range may cover the tail of one sequence and the head of the next.
+//     end to end and split over one CTA per SM in proportion to work: each
+//     tile counts one unit and each sequence end (its merge, partial record
+//     and combine) END_WEIGHT units, so every SM does about the same work
+//     whatever the per-sequence lengths are.  A CTA's range may cover the
+//     tail of one sequence and the head of the next.
 //   * A copy warp streams 512-byte cache rows (both KV heads) into a 5-stage
 //     shared-memory ring with 16-byte cp.async copies (one coalesced row per
 //     warp instruction) whose completion arrives on per-stage mbarriers; rows
@@ -69,6 +71,15 @@ constexpr int THREADS = (CONSUMER_WARPS + PRODUCER_WARPS + 1) * 32;
 constexpr int CONSUMER_THREADS = CONSUMER_WARPS * 32;
 constexpr int MAX_BATCH = 2048;
 constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]
+// Work allowance of a sequence end in the stream-K split, in tiles: the CTA
+// that holds a sequence's last tile also merges its consumer warps, writes a
+// partial record, takes the combine ticket and may combine every CTA's
+// record.  Swept on B200 at 64 sequences x 18 layers (0..16): 4 is best
+// (+4 % over an even tile split; larger values overshoot).
+#ifndef PVLC_DECODE_END_WEIGHT
+#define PVLC_DECODE_END_WEIGHT 4
+#endif
+constexpr uint32_t END_WEIGHT = PVLC_DECODE_END_WEIGHT;
 
 // shared memory map (bytes)
 constexpr int SM_K = 0;
@@ -78,12 +89,14 @@ constexpr int SM_MERGE_ACC = SM_V + STAGES * STAGE_BYTES;          // [8 warps][
 constexpr int SM_MERGE_M = SM_MERGE_ACC + CONSUMER_WARPS * GROUP * HD * 4;
 constexpr int SM_MERGE_L = SM_MERGE_M + CONSUMER_WARPS * GROUP * 4;
 constexpr int SM_TILE_OFF = SM_MERGE_L + CONSUMER_WARPS * GROUP * 4;  // [MAX_BATCH+1]
+constexpr int SM_COST_OFF = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;  // [MAX_BATCH+1]
 // rotated q of the current / next sequence: [2 slots][16 heads][Q_PITCH halves]
 constexpr int Q_PITCH = HD + 8;          // 272-byte rows: conflict-free fragment reads
-constexpr int SM_Q = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
+constexpr int SM_Q = SM_COST_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
 constexpr int SM_BARS = SM_Q + 2 * QH * Q_PITCH * 2;
-// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2], merge_full, merge_empty
-constexpr int SM_MISC = SM_BARS + (2 * STAGES + 8) * 8;
+// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2], merge_full, merge_empty,
+// app_done[2]
+constexpr int SM_MISC = SM_BARS + (2 * STAGES + 10) * 8;
 constexpr int SMEM_BYTES = SM_MISC + 64;
 
 static_assert(SMEM_BYTES <= 227 * 1024, "decode shared memory exceeds the sm_100 limit");
@@ -126,9 +139,10 @@ __device__ __forceinline__ uint32_t seq_tiles(const Params& p, uint32_t b, bool 
   return (ct + 1 + TILE - 1) / TILE;
 }
 
-// max{i : floor(i*NT/G) <= x}: the CTA whose tile range holds global tile x.
-__device__ __forceinline__ uint32_t owner_cta(uint64_t x, uint64_t G, uint64_t NT) {
-  return static_cast<uint32_t>(((x + 1) * G + NT - 1) / NT - 1);
+// max{i : floor(i*C/G) <= y}: the CTA whose cost range holds cost position y
+// (the position of a tile: the CTA that streams that tile).
+__device__ __forceinline__ uint32_t owner_cta(uint64_t y, uint64_t G, uint64_t C) {
+  return static_cast<uint32_t>(((y + 1) * G + C - 1) / C - 1);
 }
 
 // M-RoPE of 8 consecutive dims d0..d0+7 of a 128-wide head (d0 a multiple of
@@ -157,9 +171,73 @@ __device__ __forceinline__ uint4 mrope8(uint4 x, uint4 y, uint32_t d0, const Par
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// Final combine of a sequence split over CTAs first..last (CTA = token order):
+// out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the partial records
+// of query head hq, dims d0 .. d0 + 8 NCH - 1.  The records are read in groups
+// of eight with independent loads, so a combine costs two dependent L2 rounds
+// per group (the maxima, then m, l and O together) instead of a round per
+// record and pass; the sums still run record by record in CTA order.
+template <int NCH>
+__device__ __forceinline__ void combine_split(const Params& p, uint32_t b, uint32_t first,
+                                              uint32_t last, int hq, int d0) {
+  const float* base = p.partials + (size_t)b * PART_FLOATS;
+  float Mc = -CUDART_INF_F;
+  for (uint32_t i0 = first; i0 <= last; i0 += 8) {
+    float mv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      mv[e] = i0 + e <= last ? __ldcg(base + (size_t)(i0 + e) * PART_FLOATS + QH * HD + hq)
+                             : -CUDART_INF_F;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) Mc = fmaxf(Mc, mv[e]);
+  }
+  float Lc = 0.f;
+  float A[NCH][8];
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) A[ch][e] = 0.f;
+  for (uint32_t i0 = first; i0 <= last; i0 += 8) {
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      f[e] = 0.f;
+      if (i0 + e <= last) {
+        const float* r = base + (size_t)(i0 + e) * PART_FLOATS;
+        const float mi = __ldcg(r + QH * HD + hq);
+        f[e] = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
+        Lc += __ldcg(r + QH * HD + QH + hq) * f[e];
+      }
+    }
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (i0 + e <= last) {
+          const float* r = base + (size_t)(i0 + e) * PART_FLOATS + hq * HD + d0 + 8 * ch;
+          const float4 u = __ldcg(reinterpret_cast<const float4*>(r));
+          const float4 w = __ldcg(reinterpret_cast<const float4*>(r + 4));
+          A[ch][0] += u.x * f[e]; A[ch][1] += u.y * f[e]; A[ch][2] += u.z * f[e]; A[ch][3] += u.w * f[e];
+          A[ch][4] += w.x * f[e]; A[ch][5] += w.y * f[e]; A[ch][6] += w.z * f[e]; A[ch][7] += w.w * f[e];
+        }
+      }
+    }
+  }
+  const float inv = 1.f / Lc;
+#pragma unroll
+  for (int ch = 0; ch < NCH; ++ch) {
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[ch][e] * inv);
+    *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0 + 8 * ch) =
+        *reinterpret_cast<uint4*>(o);
+  }
+}
+
 __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* tile_off = reinterpret_cast<uint32_t*>(smem + SM_TILE_OFF);
+  uint32_t* cost_off = reinterpret_cast<uint32_t*>(smem + SM_COST_OFF);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM_BARS);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* q_full = empty_bar + STAGES;   // [2] rotated q (and the append) of a sequence are done
@@ -167,6 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   uint64_t* app_free = q_empty + 2;        // [2] the copy warp has left the slot's sequence
   uint64_t* merge_full = app_free + 2;     // every consumer warp wrote its (O, m, l)
   uint64_t* merge_empty = merge_full + 1;  // the merge warp has read the merge buffer
+  uint64_t* app_done = merge_empty + 1;    // [2] the KV append of a sequence is visible
   __half* qs = reinterpret_cast<__half*>(smem + SM_Q);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   // misc[0]: abort flag, misc[1]: "this CTA combines" flag
@@ -187,6 +266,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   for (uint32_t bb = tid; bb < B; bb += THREADS) tile_off[bb + 1] = seq_tiles(p, bb, blockIdx.x == 0);
   if (tid == 0) {
     tile_off[0] = 0;
+    cost_off[0] = 0;
     misc[0] = 0;
     misc[1] = 0;
     for (int s = 0; s < STAGES; ++s) {
@@ -197,6 +277,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       mbar_init(&q_full[s], 32);     // the sequence warp's lanes
       mbar_init(&q_empty[s], CONSUMER_WARPS);
       mbar_init(&app_free[s], 1);
+      mbar_init(&app_done[s], 32);   // the sequence warp's lanes
     }
     mbar_init(merge_full, CONSUMER_WARPS);
     mbar_init(merge_empty, 1);
@@ -204,20 +285,33 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   }
   __syncthreads();
   if (warp == 0) {
+    // prefix sums of the tile counts and of the split costs (tiles + the
+    // allowance of the sequence's end), one pass
     const uint32_t per = (B + 31) / 32;
     const uint32_t b0 = min(B, lane * per), b1 = min(B, b0 + per);
-    uint32_t s = 0;
-    for (uint32_t bb = b0; bb < b1; ++bb) s += tile_off[bb + 1];
-    uint32_t incl = s;
+    uint32_t s = 0, sc = 0;
+    for (uint32_t bb = b0; bb < b1; ++bb) {
+      const uint32_t n = tile_off[bb + 1];
+      s += n;
+      sc += n ? n + END_WEIGHT : 0u;
+    }
+    uint32_t incl = s, inclc = sc;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      const uint32_t yc = __shfl_up_sync(0xffffffffu, inclc, o);
+      if (lane >= o) {
+        incl += y;
+        inclc += yc;
+      }
     }
-    uint32_t run = incl - s;
+    uint32_t run = incl - s, runc = inclc - sc;
     for (uint32_t bb = b0; bb < b1; ++bb) {
-      run += tile_off[bb + 1];
+      const uint32_t n = tile_off[bb + 1];
+      run += n;
+      runc += n ? n + END_WEIGHT : 0u;
       tile_off[bb + 1] = run;
+      cost_off[bb + 1] = runc;
     }
   }
   __syncthreads();
@@ -233,10 +327,28 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     }
   }
   if (NT == 0) return;
+  // Stream-K split of the cost line: sequence b covers [cost_off[b],
+  // cost_off[b+1]) = its tiles, then END_WEIGHT units for its end-merge.  CTA
+  // c takes the tiles whose cost positions fall in [c C / G, (c+1) C / G):
+  // contiguous, monotone tile ranges that give the CTAs holding sequence ends
+  // fewer tiles.  A range inside one allowance is empty.
+  const uint64_t C = cost_off[B];
   const uint64_t G = umin64(gridDim.x, NT);
   if (blockIdx.x >= G) return;
-  const uint64_t t0 = blockIdx.x * NT / G;
-  const uint64_t t1 = (blockIdx.x + 1) * NT / G;
+  auto tile_at = [&](uint64_t y) -> uint64_t {   // first tile at cost position >= y
+    if (y >= C) return NT;
+    uint32_t lo = 0, hi = B;  // invariant: cost_off[lo] <= y < cost_off[hi]
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (cost_off[mid] <= y) lo = mid; else hi = mid;
+    }
+    const uint64_t u = y - cost_off[lo];
+    const uint64_t n = tile_off[lo + 1] - tile_off[lo];
+    return u < n ? tile_off[lo] + u : tile_off[lo + 1];
+  };
+  const uint64_t t0 = tile_at(blockIdx.x * C / G);
+  const uint64_t t1 = tile_at((blockIdx.x + 1) * C / G);
+  if (t0 == t1) return;
 
   // first sequence touching t0: last b with tile_off[b] <= t0 < tile_off[b+1]
   auto seq_of = [&](uint64_t t) -> uint32_t {
@@ -258,12 +370,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     // Warp 9, the sequence warp, does the per-sequence work ahead of the
     // stream: for each sequence of the CTA's range, in order, it writes the
     // decode-M-RoPE-rotated q into a double-buffered shared-memory slot and,
-    // when the range holds the sequence's appended row, first stores the
-    // rotated new key and the new value in cache row cache_tokens[b] (the KV
-    // append); then it announces the slot (q_full).  The copy warp waits for
-    // that announcement before copying the tile that holds the appended row,
-    // and releases the slot's append (app_free) when it leaves the sequence,
-    // which keeps the slot's barrier phases in step.
+    // announces the slot to the consumers (q_full); then, when the range
+    // holds the sequence's appended row, it stores the rotated new key and
+    // the new value in cache row cache_tokens[b] (the KV append) and announces
+    // that (app_done), so the append never delays the consumers' start.  The
+    // copy warp waits for app_done before copying the tile that holds the
+    // appended row, and releases the slot's append (app_free) when it leaves
+    // the sequence, which keeps the slot's barrier phases in step.
     bool aborted = false;
     uint32_t b = seq_of(t0);
     if (warp == CONSUMER_WARPS) {
@@ -290,7 +403,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           break;
         }
         if (row0 + n == L &&   // the tile that holds the appended row L - 1
-            (misc[0] || !mbar_wait(&q_full[nseq & 1u], (nseq >> 1) & 1u))) {
+            (misc[0] || !mbar_wait(&app_done[nseq & 1u], (nseq >> 1) & 1u))) {
           aborted = true;
           break;
         }
@@ -327,6 +440,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           *reinterpret_cast<uint4*>(qdst + d) = mrope8(lo, hi, d, p, rrow);
           *reinterpret_cast<uint4*>(qdst + d + 64) = mrope8(hi, lo, d + 64, p, rrow);
         }
+        // the consumers need only the rotated q: announce it before the append
+        mbar_arrive(&q_full[slot]);
         const uint64_t append_tile = tile_off[b] + ct / TILE;
         if (append_tile >= t0 && append_tile < t1) {
           // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
@@ -344,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.v_cache[b]) + off) = vx;
           __threadfence();   // visible before the copy warp reads the row back
         }
-        mbar_arrive(&q_full[slot]);
+        mbar_arrive(&app_done[slot]);
         ++nseq;
         const uint64_t s1 = umin64(t1, tile_off[b + 1]);
         if (s1 >= t1) break;
@@ -428,8 +543,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           __syncwarp();
           uint32_t first = 0, last = 0, mine = 0;
           if (lane == 0) {
-            first = owner_cta(tile_off[b], G, NT);
-            last = owner_cta(tile_off[b + 1] - 1, G, NT);
+            first = owner_cta(cost_off[b], G, C);
+            last = owner_cta(cost_off[b] + (tile_off[b + 1] - tile_off[b]) - 1, G, C);
             const uint32_t prev = atomicAdd(p.tickets + b, 1u);
             mine = prev == last - first;
             if (mine) {
@@ -440,37 +555,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           mine = __shfl_sync(0xffffffffu, mine, 0);
           first = __shfl_sync(0xffffffffu, first, 0);
           last = __shfl_sync(0xffffffffu, last, 0);
-          if (mine) {
-            float Mc = -CUDART_INF_F;
-            for (uint32_t i = first; i <= last; ++i)
-              Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
-            float Lc = 0.f;
-            for (uint32_t i = first; i <= last; ++i) {
-              const float* ri = p.partials + (size_t)(i + b) * PART_FLOATS;
-              const float mi = __ldcg(ri + QH * HD + hq);
-              Lc += __ldcg(ri + QH * HD + QH + hq) * (mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc));
-            }
-            const float invc = 1.f / Lc;
-#pragma unroll 2
-            for (int ch = 0; ch < 8; ++ch) {
-              const int d0 = dbase + 8 * ch;
-              float Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-              for (uint32_t i = first; i <= last; ++i) {
-                const float* ri = p.partials + (size_t)(i + b) * PART_FLOATS;
-                const float mi = __ldcg(ri + QH * HD + hq);
-                const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
-                const float4 u = __ldcg(reinterpret_cast<const float4*>(ri + hq * HD + d0));
-                const float4 w = __ldcg(reinterpret_cast<const float4*>(ri + hq * HD + d0 + 4));
-                Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
-                Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
-              }
-              __align__(16) __half o[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * invc);
-              *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
-                  *reinterpret_cast<uint4*>(o);
-            }
-          }
+          if (mine) combine_split<8>(p, b, first, last, hq, dbase);
         }
         ++j;
         ++b;
@@ -706,8 +791,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       named_bar_sync(1, CONSUMER_THREADS);
       if (!whole) {
         if (tid == 0) {
-          const uint32_t first = owner_cta(tile_off[b], G, NT);
-          const uint32_t last = owner_cta(tile_off[b + 1] - 1, G, NT);
+          const uint32_t first = owner_cta(cost_off[b], G, C);
+          const uint32_t last = owner_cta(cost_off[b] + (tile_off[b + 1] - tile_off[b]) - 1, G, C);
           const uint32_t prev = atomicAdd(p.tickets + b, 1u);
           const bool mine = prev == last - first;
           if (mine) {
@@ -719,30 +804,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           misc[3] = last;
         }
         named_bar_sync(1, CONSUMER_THREADS);
-        if (misc[1]) {
-          // combine every CTA's record of sequence b in CTA (= token) order
-          const uint32_t first = misc[2], last = misc[3];
-          float Mc = -CUDART_INF_F;
-          for (uint32_t i = first; i <= last; ++i)
-            Mc = fmaxf(Mc, __ldcg(p.partials + (size_t)(i + b) * PART_FLOATS + QH * HD + hq));
-          float Lc = 0.f, Ac[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (uint32_t i = first; i <= last; ++i) {
-            const float* rec = p.partials + (size_t)(i + b) * PART_FLOATS;
-            const float mi = __ldcg(rec + QH * HD + hq);
-            const float fi = mi == -CUDART_INF_F ? 0.f : fast_exp2(mi - Mc);
-            Lc += __ldcg(rec + QH * HD + QH + hq) * fi;
-            const float4 u = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0));
-            const float4 w = __ldcg(reinterpret_cast<const float4*>(rec + hq * HD + d0 + 4));
-            Ac[0] += u.x * fi; Ac[1] += u.y * fi; Ac[2] += u.z * fi; Ac[3] += u.w * fi;
-            Ac[4] += w.x * fi; Ac[5] += w.y * fi; Ac[6] += w.z * fi; Ac[7] += w.w * fi;
-          }
-          const float inv = 1.f / Lc;
-          __align__(16) __half o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(Ac[e] * inv);
-          *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
-              *reinterpret_cast<uint4*>(o);
-        }
+        // combine every CTA's record of sequence b in CTA (= token) order
+        if (misc[1]) combine_split<1>(p, b, misc[2], misc[3], hq, d0);
         named_bar_sync(1, CONSUMER_THREADS);
       }
       break;
