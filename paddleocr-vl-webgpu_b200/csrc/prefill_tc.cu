@@ -66,8 +66,8 @@ constexpr int QT = 1;            // Q tiles per CTA
 constexpr int STREAMS = 2;       // K-tile streams per CTA (even / odd K tiles)
 constexpr int BN = 128;          // keys per K/V tile
 constexpr int THREADS = 12 * 32;
-// launch: 384 threads x 168 registers; softmax warpgroups take 200, control 56
-constexpr uint32_t REGS_SOFTMAX = 200, REGS_CTRL = 56;
+// launch: 384 threads x 168 registers; softmax warpgroups take 200, control 104
+constexpr uint32_t REGS_SOFTMAX = 200, REGS_CTRL = 104;
 static_assert(256 * REGS_SOFTMAX + 128 * REGS_CTRL <= 384 * 168, "register split");
 
 constexpr uint32_t SZ_W = 128 * 128;          // 128 rows x 64 dims fp16, 128B swizzle
@@ -78,6 +78,10 @@ constexpr uint32_t ST_K = 0, ST_V = 2 * SZ_W;
 constexpr uint32_t STAGE_BYTES = 4 * SZ_W;
 constexpr int STAGES = 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
+// pair CTAs: Q buffer 1 then PAIR_STAGES stages inside the same region
+constexpr int PAIR_STAGES = 2;
+constexpr uint32_t OFF_STAGE_PAIR = 2 * Q_BYTES;
+static_assert(OFF_STAGE_PAIR + PAIR_STAGES * STAGE_BYTES <= OFF_BARS, "pair layout overflows");
 // q_full, q_ready, kv_full[3], kv_empty[3], s_full[2], p_ready[2], o_done[2], ml_ready
 constexpr int NBARS = 15;
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
@@ -101,6 +105,8 @@ struct Params {
   const float* rope_sin;
   uint32_t rope_rows;
   uint32_t tokens;
+  uint32_t n_split;       // split CTAs per KV head (the heaviest Q tiles)
+  uint32_t n_light;       // lightest Q tiles, paired two per CTA
   __half* out;            // [T, 16, 128]
 };
 
@@ -158,18 +164,42 @@ __device__ __forceinline__ uint8_t* chunk_addr(uint8_t* blk, int r, int c) {
   return blk + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in
-// place: chunks c0..c0+3 of 8 dims (dims 8c..8c+7 and their partners 64 above).
-__device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const Params& p,
-                                          uint32_t token, int c0) {
-#pragma unroll 2
-  for (int c = c0; c < c0 + 4; ++c) {
+// M-RoPE table entries of one Q row's chunks c0..c0+3 (dims 8c..8c+7 and
+// their partners 64 above): [chunk][cos lo 2, cos hi 2, sin lo 2, sin hi 2].
+// Loaded before the Q tile lands, so the table latency overlaps the TMA load.
+struct RowTables {
+  float4 v[4][8];
+};
+
+__device__ __forceinline__ void mrope_tables(RowTables& t, const Params& p, uint32_t token,
+                                             int c0) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = c0 + u;
     const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
     const size_t tb = ((size_t)axis * p.rope_rows + token) * HD + 8 * c;
     const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + tb);
     const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + tb);
-    const float4 cl0 = __ldg(cs), cl1 = __ldg(cs + 1), ch0 = __ldg(cs + 16), ch1 = __ldg(cs + 17);
-    const float4 sl0 = __ldg(sn), sl1 = __ldg(sn + 1), sh0 = __ldg(sn + 16), sh1 = __ldg(sn + 17);
+    t.v[u][0] = __ldg(cs);
+    t.v[u][1] = __ldg(cs + 1);
+    t.v[u][2] = __ldg(cs + 16);
+    t.v[u][3] = __ldg(cs + 17);
+    t.v[u][4] = __ldg(sn);
+    t.v[u][5] = __ldg(sn + 1);
+    t.v[u][6] = __ldg(sn + 16);
+    t.v[u][7] = __ldg(sn + 17);
+  }
+}
+
+// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in
+// place: chunks c0..c0+3 of 8 dims (dims 8c..8c+7 and their partners 64 above).
+__device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const RowTables& t,
+                                          int c0) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int c = c0 + u;
+    const float4 cl0 = t.v[u][0], cl1 = t.v[u][1], ch0 = t.v[u][2], ch1 = t.v[u][3];
+    const float4 sl0 = t.v[u][4], sl1 = t.v[u][5], sh0 = t.v[u][6], sh1 = t.v[u][7];
     uint4* pa = reinterpret_cast<uint4*>(chunk_addr(b0, r, c));
     uint4* pb = reinterpret_cast<uint4*>(chunk_addr(b1, r, c));
     const uint4 a = *pa, b = *pb;
@@ -216,12 +246,36 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t g = blockIdx.x;                      // KV head
   const uint32_t n_qt = (p.tokens + TOK - 1) / TOK;
-  const uint32_t qt = n_qt - 1 - blockIdx.y;          // heaviest (latest) first
-  const uint32_t tok0 = qt * TOK;                     // first token of the Q tile
-  const uint32_t last_tok = umin32(tok0 + TOK, p.tokens) - 1;
-  const int nk = static_cast<int>(last_tok / BN) + 1;  // K tiles 0 .. the diagonal
-  // stream t takes K tiles t, t + 2, ...
-  const int nks[STREAMS] = {(nk + 1) / 2, nk / 2};
+  // Two kinds of CTA (both heaviest first):
+  //  split: one Q tile; stream t takes its K tiles t, t + 2, ... and the two
+  //         streams' (O, m, l) merge at the end (the long causal ranges);
+  //  pair:  two light Q tiles, one per stream, sharing every K/V tile (the
+  //         lightest tiles, paired so that the grid is one wave).
+  const bool pair = blockIdx.y >= p.n_split;
+  uint32_t tile0[STREAMS];   // first token of each stream's Q tile
+  int nks[STREAMS];          // K tiles of each stream
+  int ntiles;                // K/V tiles the CTA loads
+  if (!pair) {
+    const uint32_t qt = n_qt - 1 - blockIdx.y;
+    const uint32_t last_tok = umin32(qt * TOK + TOK, p.tokens) - 1;
+    const int nk = static_cast<int>(last_tok / BN) + 1;    // K tiles 0 .. the diagonal
+    tile0[0] = tile0[1] = qt * TOK;
+    nks[0] = (nk + 1) / 2;
+    nks[1] = nk / 2;
+    ntiles = nk;
+  } else {
+    const uint32_t i = blockIdx.y - p.n_split;
+    const uint32_t qa = p.n_light - 1 - i, qb = i;     // stream 0 takes the heavier tile
+    tile0[0] = qa * TOK;
+    tile0[1] = qb * TOK;
+    nks[0] = static_cast<int>((umin32(qa * TOK + TOK, p.tokens) - 1) / BN) + 1;
+    nks[1] = static_cast<int>((umin32(qb * TOK + TOK, p.tokens) - 1) / BN) + 1;
+    ntiles = nks[0];
+  }
+  // shared memory: Q buffer 0, then (split) 3 K/V stages or (pair) Q buffer 1
+  // and 2 K/V stages
+  const int nst = pair ? PAIR_STAGES : STAGES;
+  const uint32_t off_stage = pair ? OFF_STAGE_PAIR : OFF_STAGE;
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -256,16 +310,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tma_prefetch_desc(&maps.q);
       tc::tma_prefetch_desc(&maps.k);
       tc::tma_prefetch_desc(&maps.v);
-      mbar_arrive_expect_tx(q_full, Q_BYTES);
-      for (int b = 0; b < 2; ++b)
-        tc::tma_load_3d(smem + OFF_Q + b * SZ_W, &maps.q, 64 * b, GROUP * g, tok0, q_full);
+      const int nq = pair ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+        if (t < nq)
+          for (int b = 0; b < 2; ++b)
+            tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + b * SZ_W, &maps.q, 64 * b, GROUP * g,
+                            tile0[t], q_full);
       // keys are read from the cache that kv_rope_kernel (the preceding launch) writes
       pdl_wait();
       int issued = 0;
-      for (int j = 0; j < nk; ++j) {
-        const int s = j % STAGES;
-        if (misc[1] || !mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1)) { misc[1] = 1; break; }
-        uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % nst;
+        if (misc[1] || !mbar_wait(&kv_empty[s], ((j / nst) & 1) ^ 1)) { misc[1] = 1; break; }
+        uint8_t* st = smem + off_stage + s * STAGE_BYTES;
         mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
         for (int b = 0; b < 2; ++b) {
           tc::tma_load_3d(st + ST_K + b * SZ_W, &maps.k, 64 * b, g, j * BN, &kv_full[s]);
@@ -273,17 +332,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         issued = j + 1;
       }
-      for (int j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j)
-        mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1);
+      for (int j = (issued > nst ? issued - nst : 0); j < issued; ++j)
+        mbar_wait(&kv_full[j % nst], (j / nst) & 1);
     } else if (warp == 9) {
       // ---------------------------------------------------- MMA issuer
-      // Tile j lives in stage j % 3; stream t = j % 2.  Per step: PV of the
-      // stream's current tile, then QK of its next tile (two ahead), so PV
-      // and QK reach the tensor pipe back to back and the other stream's
-      // softmax overlaps them.
+      // split: tile j lives in stage j % 3, stream t = j % 2; per step the PV
+      // of the stream's current tile, then the QK of its next tile (two
+      // ahead).  pair: tile j lives in stage j % 2 and serves both streams;
+      // per step and stream the PV of tile j, then the QK of tile j + 1.
       constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
-      const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + OFF_STAGE);
+      const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + off_stage);
       const uint64_t dq = tc::smem_desc(sq, 16, 1024, tc::kSw128);
       const uint64_t dk = tc::smem_desc(st0 + ST_K, 16, 1024, tc::kSw128);
       // MN-major V: the two 64-dim blocks are SZ_W apart (LBO), 8-key groups 1 KB apart
@@ -291,17 +350,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       auto qk = [&](int t, int s) {
         const uint32_t tS = tmem + 128u * t;
         const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        const uint64_t qo = pair ? (uint64_t)t * (Q_BYTES >> 4) : 0;
         if (tc::elect_one()) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {   // block ks/4, 32 bytes per K step within a block
             const uint64_t off = (uint64_t)(ks >> 2) * (SZ_W >> 4) + 2 * (ks & 3);
-            tc::mma_ss(tS, dq + off, dk + so + off, idesc_qk, ks > 0);
+            tc::mma_ss(tS, dq + qo + off, dk + so + off, idesc_qk, ks > 0);
           }
           tc::commit(&s_full[t]);
         }
         __syncwarp();
       };
-      auto pv = [&](int t, int s, bool first) {
+      auto pv = [&](int t, int s, bool first, bool release) {
         const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
         const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
         if (tc::elect_one()) {
@@ -309,43 +369,63 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int ks = 0; ks < 8; ++ks)     // 16 keys = two 1 KB groups per K step
             tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
           tc::commit(&o_done[t]);
-          tc::commit(&kv_empty[s]);          // the stage's only tile is consumed
+          if (release) tc::commit(&kv_empty[s]);   // every stream reading the stage is done
         }
         __syncwarp();
       };
       constexpr uint32_t kAll = 0xffffffffu;
-      auto kv_ready = [&](int j) { return mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1); };
+      auto kv_ready = [&](int j) { return mbar_wait(&kv_full[j % nst], (j / nst) & 1); };
       bool ok = __all_sync(kAll, mbar_wait(q_ready, 0) && kv_ready(0));
-      int done = 0;   // K tiles whose PV was issued
-      if (ok) {
+      int done = 0;   // K tiles whose last PV was issued
+      if (ok && !pair) {
         tc::fence_after_sync();
         qk(0, 0);
-        if (nk > 1) {
+        if (ntiles > 1) {
           ok = __all_sync(kAll, kv_ready(1));
           if (ok) {
             tc::fence_after_sync();
             qk(1, 1);
           }
         }
-        for (int j = 0; j < nk && ok && !__any_sync(kAll, misc[1] != 0); ++j) {
+        for (int j = 0; j < ntiles && ok && !__any_sync(kAll, misc[1] != 0); ++j) {
           const int t = j & 1, i = j >> 1;   // stream, its step
           if (!__all_sync(kAll, mbar_wait(&p_ready[t], i & 1))) { ok = false; break; }
-          const bool more = j + 2 < nk;
+          const bool more = j + 2 < ntiles;
           if (more && !__all_sync(kAll, kv_ready(j + 2))) { ok = false; break; }
           tc::fence_after_sync();
-          pv(t, j % STAGES, i == 0);
+          pv(t, j % STAGES, i == 0, true);
           if (more) qk(t, (j + 2) % STAGES);
           done = j + 1;
+        }
+      } else if (ok) {
+        tc::fence_after_sync();
+        qk(0, 0);
+        qk(1, 0);
+        for (int j = 0; j < ntiles && ok && !__any_sync(kAll, misc[1] != 0); ++j) {
+          const int s = j % PAIR_STAGES, s1 = (j + 1) % PAIR_STAGES;
+          if (j + 1 < ntiles && !__all_sync(kAll, kv_ready(j + 1))) { ok = false; break; }
+#pragma unroll
+          for (int t = 0; t < STREAMS; ++t) {
+            if (j >= nks[t]) continue;
+            if (!__all_sync(kAll, mbar_wait(&p_ready[t], j & 1))) { ok = false; break; }
+            tc::fence_after_sync();
+            // stream 1's tiles are a prefix of stream 0's: the last reader of
+            // tile j is stream 1 while it still has tiles
+            pv(t, s, j == 0, t == 1 || j >= nks[1]);
+            if (j + 1 < nks[t]) qk(t, s1);
+          }
+          if (ok) done = j + 1;
         }
       }
       if (!ok && lane == 0) misc[1] = 1;
       // never exit with MMAs in flight or commit arrivals still pending
+#pragma unroll
       for (int t = 0; t < STREAMS; ++t) {
-        const int issued_t = (done + 1 - t) / 2;   // PVs issued on stream t
+        const int issued_t = pair ? (done < nks[t] ? done : nks[t]) : (done + 1 - t) / 2;
         if (issued_t > 0) mbar_wait(&o_done[t], (issued_t - 1) & 1);
       }
-      for (int j = (done > STAGES ? done - STAGES : 0); j < done; ++j)
-        mbar_wait(&kv_empty[j % STAGES], (j / STAGES) & 1);
+      for (int j = (done > nst ? done - nst : 0); j < done; ++j)
+        mbar_wait(&kv_empty[j % nst], (j / nst) & 1);
     }
   } else {
     tc::regs_inc<REGS_SOFTMAX>();
@@ -354,12 +434,26 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_base + 128u * t;
-    const uint32_t token = tok0 + (i >> 3);
-    const uint32_t head = GROUP * g + (i & 7);
-    bool ok = mbar_wait(q_full, 0);
-    if (ok && token < p.tokens) {
-      // the two warpgroups rotate disjoint halves of the row's dims
-      mrope_row(smem + OFF_Q, smem + OFF_Q + SZ_W, i, p, token, 4 * t);
+    const uint32_t my_tile0 = t ? tile0[1] : tile0[0];
+    const int my_nk = t ? nks[1] : nks[0];
+    const uint32_t token = my_tile0 + (i >> 3);
+    // Q rotation: split -- the two warpgroups rotate disjoint halves of the
+    // shared tile's dims; pair -- each rotates its own tile.  The table
+    // entries are fetched while the Q tiles are still in flight.
+    uint8_t* qb0 = smem + OFF_Q + (pair ? t * Q_BYTES : 0);
+    bool ok = true;
+    {
+      RowTables rt;
+      const int c0 = pair ? 0 : 4 * t;
+      if (token < p.tokens) mrope_tables(rt, p, token, c0);
+      ok = mbar_wait(q_full, 0);
+      if (ok && token < p.tokens) {
+        mrope_row(qb0, qb0 + SZ_W, i, rt, c0);
+        if (pair) {
+          mrope_tables(rt, p, token, 4);
+          mrope_row(qb0, qb0 + SZ_W, i, rt, 4);
+        }
+      }
     }
     fence_proxy_async_smem();
     __syncwarp();
@@ -371,10 +465,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_run = -CUDART_INF_F, l_run = 0.f;
     bool good = __all_sync(0xffffffffu, ok);
     // rows 32w'..32w'+31 of this warp hold tokens +4w' .. +4w'+3
-    const uint32_t warp_tok_lo = tok0 + ((warp & 3) * 32 >> 3);
+    const uint32_t warp_tok_lo = my_tile0 + ((warp & 3) * 32 >> 3);
     const uint32_t tO = tmem + lane_base + 256u + 128u * t;
-    for (int step = 0; step < nks[t] && good; ++step) {
-      const int j = 2 * step + t;                    // K tile
+    // K tile of step `step`: step (pair) or 2 step + t (split)
+    const int j0 = pair ? 0 : t, jstride = pair ? 1 : 2;
+    for (int step = 0; step < my_nk && good; ++step) {
+      const int j = j0 + jstride * step;
       if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], step & 1))) {
         good = false;
         break;
@@ -462,64 +558,90 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&p_ready[t]);
     }
     if (!good) misc[1] = 1;
-    // epilogue: each warpgroup waits for its own stream's last PV (its own
-    // o_done phases, which it tracks exactly) and posts (m, l) in its
-    // stream's S columns, which no MMA touches after that PV; ml_ready
-    // completing means both streams are done.  Then this warpgroup writes
-    // output columns 64t..64t+63 =
-    //   (O0 2^(m0-M) + O1 2^(m1-M)) / (l0 2^(m0-M) + l1 2^(m1-M))
     const bool fin = __all_sync(0xffffffffu,
-                                good && (nks[t] == 0 || mbar_wait(&o_done[t], (nks[t] - 1) & 1)));
-    if (fin) {
-      tc::fence_after_sync();
-      uint32_t ml[16] = {};
-      ml[0] = __float_as_uint(m_run);
-      ml[1] = __float_as_uint(l_run);
-      tc::tmem_st16(tS, ml);
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(ml_ready);
-    if (__all_sync(0xffffffffu, fin && mbar_wait(ml_ready, 0))) {
-      tc::fence_after_sync();
-      uint32_t x0[16], x1[16];
-      tc::tmem_ld16(tmem + lane_base, x0);           // stream 0's (m, l)
-      tc::tmem_ld16(tmem + lane_base + 128u, x1);    // stream 1's (m, l)
-      tc::tmem_wait_ld();
-      const float m0 = __uint_as_float(x0[0]), l0 = __uint_as_float(x0[1]);
-      const float m1 = nks[1] > 0 ? __uint_as_float(x1[0]) : -CUDART_INF_F;
-      const float l1 = nks[1] > 0 ? __uint_as_float(x1[1]) : 0.f;
-      const float M = fmaxf(m0, m1);
-      const float f0 = m0 == -CUDART_INF_F ? 0.f : fast_exp2(m0 - M);
-      const float f1 = m1 == -CUDART_INF_F ? 0.f : fast_exp2(m1 - M);
-      const float inv = 1.f / (l0 * f0 + l1 * f1);
-      const float a0 = f0 * inv, a1 = f1 * inv;
-      const bool store = token < p.tokens;
-      __half* orow = p.out + ((size_t)token * QH + head) * HD;
-      const uint32_t tO0 = tmem + lane_base + 256u, tO1 = tmem + lane_base + 384u;
+                                good && (my_nk == 0 || mbar_wait(&o_done[t], (my_nk - 1) & 1)));
+    const bool store = token < p.tokens;
+    const bool two = nks[1] > 0;                     // stream 1 had work
+    __half* orow = p.out + ((size_t)token * QH + GROUP * g + (i & 7)) * HD;
+    if (pair) {
+      // epilogue of a paired tile: this stream's O / l -> all 128 columns
+      if (fin) {
+        tc::fence_after_sync();
+        const float inv = 1.f / l_run;
 #pragma unroll
-      for (int cc = 64 * t; cc < 64 * t + 64; cc += 16) {
-        uint32_t o0[16], o1[16];
-        tc::tmem_ld16(tO0 + cc, o0);
-        if (nks[1] > 0) tc::tmem_ld16(tO1 + cc, o1);
-        tc::tmem_wait_ld();
-        float v[16];
+        for (int cc = 0; cc < 128; cc += 16) {
+          uint32_t ov[16];
+          tc::tmem_ld16(tO + cc, ov);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          v[e] = __uint_as_float(o0[e]) * a0 + (nks[1] > 0 ? __uint_as_float(o1[e]) * a1 : 0.f);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint4 w;
-          w.x = pack_half2(v[8 * h + 0], v[8 * h + 1]);
-          w.y = pack_half2(v[8 * h + 2], v[8 * h + 3]);
-          w.z = pack_half2(v[8 * h + 4], v[8 * h + 5]);
-          w.w = pack_half2(v[8 * h + 6], v[8 * h + 7]);
-          if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
+          for (int h = 0; h < 2; ++h) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
+            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
+          }
         }
+      } else {
+        misc[1] = 1;
       }
     } else {
-      misc[1] = 1;
+      // epilogue of a split tile: each warpgroup waits for its own stream's
+      // last PV (its own o_done phases, which it tracks exactly) and posts
+      // (m, l) in its stream's S columns, which no MMA touches after that PV;
+      // ml_ready completing means both streams are done.  Then this
+      // warpgroup writes output columns 64t..64t+63 =
+      //   (O0 2^(m0-M) + O1 2^(m1-M)) / (l0 2^(m0-M) + l1 2^(m1-M))
+      if (fin) {
+        tc::fence_after_sync();
+        uint32_t ml[16] = {};
+        ml[0] = __float_as_uint(m_run);
+        ml[1] = __float_as_uint(l_run);
+        tc::tmem_st16(tS, ml);
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ml_ready);
+      if (__all_sync(0xffffffffu, fin && mbar_wait(ml_ready, 0))) {
+        tc::fence_after_sync();
+        uint32_t x0[16], x1[16];
+        tc::tmem_ld16(tmem + lane_base, x0);           // stream 0's (m, l)
+        tc::tmem_ld16(tmem + lane_base + 128u, x1);    // stream 1's (m, l)
+        tc::tmem_wait_ld();
+        const float m0 = __uint_as_float(x0[0]), l0 = __uint_as_float(x0[1]);
+        const float m1 = two ? __uint_as_float(x1[0]) : -CUDART_INF_F;
+        const float l1 = two ? __uint_as_float(x1[1]) : 0.f;
+        const float M = fmaxf(m0, m1);
+        const float f0 = m0 == -CUDART_INF_F ? 0.f : fast_exp2(m0 - M);
+        const float f1 = m1 == -CUDART_INF_F ? 0.f : fast_exp2(m1 - M);
+        const float inv = 1.f / (l0 * f0 + l1 * f1);
+        const float a0 = f0 * inv, a1 = f1 * inv;
+        const uint32_t tO0 = tmem + lane_base + 256u, tO1 = tmem + lane_base + 384u;
+#pragma unroll
+        for (int cc = 64 * t; cc < 64 * t + 64; cc += 16) {
+          uint32_t o0[16], o1[16];
+          tc::tmem_ld16(tO0 + cc, o0);
+          if (two) tc::tmem_ld16(tO1 + cc, o1);
+          tc::tmem_wait_ld();
+          float v[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            v[e] = __uint_as_float(o0[e]) * a0 + (two ? __uint_as_float(o1[e]) * a1 : 0.f);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4 w;
+            w.x = pack_half2(v[8 * h + 0], v[8 * h + 1]);
+            w.y = pack_half2(v[8 * h + 2], v[8 * h + 3]);
+            w.z = pack_half2(v[8 * h + 4], v[8 * h + 5]);
+            w.w = pack_half2(v[8 * h + 6], v[8 * h + 7]);
+            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
+          }
+        }
+      } else {
+        misc[1] = 1;
+      }
     }
   }
 
@@ -568,6 +690,18 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t rows, uint32_t heads,
 }  // namespace ptc
 
 int prefill_query_tile() { return ptc::QT * ptc::TOK; }
+
+// Q tiles per KV head, split into the heaviest (one CTA each, K range split
+// between the two streams) and the lightest (paired two per CTA) so that the
+// CTAs of both KV heads fit one wave of `sms`.
+void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_light) {
+  const uint32_t n_qt = (tokens + ptc::TOK - 1) / ptc::TOK;
+  const uint32_t per_head = sms > 0 ? (uint32_t)sms / ptc::KVH : n_qt;
+  uint32_t light = n_qt > per_head ? 2 * (n_qt - per_head) : 0;
+  if (light > n_qt) light = n_qt & ~1u;
+  *n_light = light;
+  *n_split = n_qt - light;
+}
 int prefill_block_threads() { return ptc::THREADS; }
 
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
@@ -601,10 +735,14 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   p.rope_rows = a.rope_rows;
   p.tokens = a.tokens;
   p.out = reinterpret_cast<__half*>(a.out);
+  // one wave: pair the lightest Q tiles so that the CTAs fit the SMs
+  const int sms = device_sm_count();
+  if (sms <= 0) return PVLC_CUDA_ERROR;
+  prefill_schedule(a.tokens, sms, &p.n_split, &p.n_light);
   // programmatic dependent launch: the attention CTAs' prologue overlaps
   // kv_rope_kernel; only their cache reads wait for it (pdl_wait)
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ptc::KVH, n_qt);
+  cfg.gridDim = dim3(ptc::KVH, p.n_split + p.n_light / 2);
   cfg.blockDim = dim3(ptc::THREADS);
   cfg.dynamicSmemBytes = ptc::SMEM_BYTES;
   cfg.stream = stream;

@@ -261,12 +261,16 @@ int pvlc_plan_decoder_prefill(uint32_t tokens, uint32_t capacity, uint32_t rope_
   if (!plan) return PVLC_NULL_POINTER;
   memset(plan, 0, sizeof(*plan));
   const uint32_t bm = (uint32_t)prefill_query_tile();
-  plan->grid[0] = PVLC_DECODER_KV_HEADS;   // one CTA per (KV group, 16-token Q tile)
-  plan->grid[1] = (tokens + bm - 1) / bm;
+  // one CTA per (KV group, 16-token Q tile), the lightest tiles paired two per
+  // CTA so that the grid is one wave
+  uint32_t n_split = 0, n_light = 0;
+  prefill_schedule(tokens, sms_or_default(), &n_split, &n_light);
+  plan->grid[0] = PVLC_DECODER_KV_HEADS;
+  plan->grid[1] = n_split + n_light / 2;
   plan->grid[2] = 1;
   plan->block[0] = (uint32_t)prefill_block_threads();
   plan->block[1] = plan->block[2] = 1;
-  plan->work_items = plan->grid[0] * plan->grid[1];
+  plan->work_items = PVLC_DECODER_KV_HEADS * ((tokens + bm - 1) / bm);
   plan->output_elements = (uint64_t)tokens * 16 * 128;
   plan->output_bytes = plan->output_elements * 2;
   plan->flops = 4.0 * 128 * 16 * (double)tokens * (tokens + 1) / 2.0;

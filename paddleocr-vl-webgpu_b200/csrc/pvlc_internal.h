@@ -65,6 +65,7 @@ struct PrefillArgs {
   pvlc_half* out;
 };
 int prefill_query_tile();
+void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_light);
 int prefill_block_threads();
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream);
 

@@ -76,6 +76,9 @@ def test_decoder_prefill_plan():
     plan = abi.Plan()
     assert abi.lib().pvlc_plan_decoder_prefill(1564, 1820, 1820, ctypes.byref(plan)) == abi.OK
     assert plan.flops == pytest.approx(1.00256e10, rel=1e-4)   # 4*128*16*T(T+1)/2
+    # 98 Q tiles per KV head: the 48 lightest paired, so 2 x (50 + 24) = 148 CTAs
+    assert plan.work_items == 2 * 98
+    assert (plan.grid[0], plan.grid[1]) == (2, 74)
     assert abi.lib().pvlc_plan_decoder_prefill(0, 10, 10, ctypes.byref(plan)) == abi.ZERO_DIMENSION
     assert abi.lib().pvlc_plan_decoder_prefill(11, 10, 20, ctypes.byref(plan)) == abi.CAPACITY_EXHAUSTED
     assert (abi.lib().pvlc_plan_decoder_prefill(11, 20, 10, ctypes.byref(plan))

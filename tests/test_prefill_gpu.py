@@ -75,3 +75,11 @@ def test_config3_prefill(cuda_lib):
     ids, grids = image_prompt(20, (40, 37), 64)
     assert len(ids) == 1564
     _run_case(ids, grids, 1564 + 256, seed=3)
+
+
+@pytest.mark.parametrize("T", [1190, 2500, 4100])
+def test_long_prefill_paired_tiles(cuda_lib, T):
+    """Past 74 Q tiles per KV head the lightest tiles run two per CTA (one per
+    stream, sharing K/V tiles): one pair (1190), many pairs (2500), and every
+    tile paired with more CTAs than SMs (4100)."""
+    _run_case(list(range(3, 3 + T)), [], T + 5, seed=T)
