@@ -45,9 +45,9 @@ UNIT = "GB/s"
 # profiles/vision_tc_kernel_config1.txt, profiles/prefill_attn_kernel_config2.txt).
 # The decode capture is one 64-sequence launch: its traffic / algorithmic-bytes
 # ratio scales the figure to the bench's average launch.
-DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 282.96e6 / 278.20e6
-VISION_TC_TRAFFIC_BYTES = 59.09e6
-PREFILL_ATTN_TRAFFIC_BYTES = 11.34e6
+DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 283.27e6 / 278.20e6
+VISION_TC_TRAFFIC_BYTES = 61.00e6
+PREFILL_ATTN_TRAFFIC_BYTES = 11.37e6
 
 
 def peaks():
