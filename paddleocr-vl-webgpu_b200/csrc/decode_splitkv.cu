@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   uint64_t* app_done = merge_empty + 1;    // [2] the KV append of a sequence is visible
   __half* qs = reinterpret_cast<__half*>(smem + SM_Q);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
-  // misc[0]: abort flag, misc[1]: "this CTA combines" flag
+  // misc[0]: abort flag, misc[1]: "this CTA combines" flag, misc[2..3]: the
+  // combine's CTA range, misc[4]: the sequence warp's opening loads are issued
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -269,6 +270,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     cost_off[0] = 0;
     misc[0] = 0;
     misc[1] = 0;
+    misc[4] = 0;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 32);   // the copy warp's lanes
       mbar_init(&empty_bar[s], 4);
@@ -380,6 +382,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     bool aborted = false;
     uint32_t b = seq_of(t0);
     if (warp == CONSUMER_WARPS) {
+      // Give the sequence warp's few opening loads (the first sequence's q,
+      // tables and new row) a head start on this launch's DRAM burst: they
+      // are on the consumers' critical path, the stream is not yet (bounded
+      // wait).
+      {
+        const uint64_t w0 = globaltimer();
+        while (misc[4] == 0 && globaltimer() - w0 < 20000ull) {
+        }
+      }
       uint32_t nseq = 0;
       uint8_t* kc = reinterpret_cast<uint8_t*>(p.k_cache[b]);
       uint8_t* vc = reinterpret_cast<uint8_t*>(p.v_cache[b]);
@@ -419,6 +430,27 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     } else if (warp == CONSUMER_WARPS + 1) {
       // sequence warp: lane l rotates query head l/2, dims 32(l%2)..+31 and
       // their partners 64 above
+      {
+        // pull the first sequence's q row (32 lines), table rows (3 planes x
+        // cos/sin x 4 lines) and new K/V rows (2 x 4 lines) toward L2, then
+        // release the copy warp
+        const uint32_t ct0 = __ldg(p.cache_tokens + b);
+        const uint32_t rr0 = p.rope_row ? __ldg(p.rope_row + b) : ct0;
+        prefetch_l2(reinterpret_cast<const uint8_t*>(p.q + (size_t)b * QH * HD) + lane * 128);
+        if (lane < 24 && rr0 < p.rope_rows) {
+          const float* tab = (lane & 4) ? p.rope_sin : p.rope_cos;
+          prefetch_l2(reinterpret_cast<const uint8_t*>(tab + ((size_t)(lane >> 3) * p.rope_rows + rr0) * HD) +
+                      (lane & 3) * 128);
+        } else if (lane >= 24) {
+          const __half* nr = (lane & 4) ? p.v_new : p.k_new;
+          prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * KVH * HD) + (lane & 3) * 128);
+        }
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile("" ::: "memory");
+          misc[4] = 1;
+        }
+      }
       uint32_t nseq = 0;
       while (true) {
         const uint32_t slot = nseq & 1u, round = nseq >> 1;

@@ -86,6 +86,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Prefetch the 128-byte line holding `p` into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // ------------------------------------------------------ bulk async copies
 // 1-D bulk copy global -> shared, completion signalled on `bar` (tx bytes).
 // Both addresses 16-byte aligned, bytes a multiple of 16.
