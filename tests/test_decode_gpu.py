@@ -141,6 +141,27 @@ def test_decode_large_batch_stream_k(cuda_lib):
     assert t["ws"].errors() == 0
 
 
+@pytest.mark.parametrize("n,lo,hi,seed", [(600, 0, 40, 21), (300, 0, 300, 22)])
+def test_decode_many_short_sequences(cuda_lib, n, lo, hi, seed):
+    """Hundreds of short sequences: the work-weighted split then gives many CTAs
+    an empty range (a sequence end's allowance only) and others several sequence
+    ends each; two steps in a row on one workspace."""
+    rng = np.random.default_rng(seed)
+    lengths = rng.integers(lo, hi + 1, size=n).tolist()
+    cap = hi + 4
+    t, host = _setup(lengths, cap, seed=seed, poison_tail=False)
+    out = _run(t, cap, max(lengths)).cpu().numpy().astype(np.float32)
+    assert np.isfinite(out).all()
+    for b in range(0, n, 7):
+        ref, _, _ = _oracle(host, b, lengths[b])
+        err = np.abs(out[b] - ref).max()
+        assert err <= ATOL, f"seq {b} (L={lengths[b]}) err {err}"
+    t["ct"] += 1
+    out2 = _run(t, cap, max(lengths) + 1).cpu().numpy().astype(np.float32)
+    assert np.isfinite(out2).all()
+    assert t["ws"].errors() == 0
+
+
 def test_decode_rejects_out_of_range_rows_without_faulting(cuda_lib):
     """A device-side row past max_cache_tokens is skipped, zero-filled and flagged."""
     lengths = [10, 20]
