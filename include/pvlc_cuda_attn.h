@@ -221,6 +221,31 @@ int pvlc_image_patches(const uint8_t* rgb, uint32_t height, uint32_t width, uint
                        size_t workspace_bytes, float* patches, void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Engine glue: the elementwise work between the dense layers, each one pass.
+ *
+ * Replaces the reference's LayerNorm / RMSNorm / SiLU / GELU kernels of the
+ * vision and decoder layers (WGSL catalog crates/pvlc-wgsl/src/lib.rs:438-499;
+ * arithmetic crates/pvlc-cpu-ref/src/lib.rs:280-367) with the engine's storage:
+ * residual streams f32, GEMM operands fp16, math in f32.
+ *
+ * pvlc_add_norm: per row of [rows, width] (width a multiple of 8):
+ *   residual += delta (fp16, when delta is not NULL), then
+ *   out = LayerNorm(residual) * weight + bias   (bias not NULL; eps as given), or
+ *   out = RMSNorm(residual) * weight            (bias NULL), as fp16.
+ * pvlc_gelu: in place on n fp16 values (n even): tanh form (erf_form = 0,
+ *   gelu_pytorch_tanh) or erf form (erf_form = 1).
+ * pvlc_silu_mul: gate_up [rows, 2*width] (gate | up) -> out [rows, width] =
+ *   silu(gate) * up, fp16.
+ * All pointers 16-byte aligned device pointers; work on `stream`.
+ */
+int pvlc_add_norm(float* residual, const pvlc_half* delta, uint32_t rows, uint32_t width,
+                  const float* weight, const float* bias, float eps, pvlc_half* out,
+                  void* stream);
+int pvlc_gelu(pvlc_half* x, uint64_t n, int erf_form, void* stream);
+int pvlc_silu_mul(const pvlc_half* gate_up, uint32_t rows, uint32_t width, pvlc_half* out,
+                  void* stream);
+
+/* ----------------------------------------------------------------------------
  * Plans: the host-side half of the contract, callable without a GPU.
  * They run the same validation as the launch entry points and report the
  * launch geometry the library will use.

@@ -17,11 +17,12 @@ Architecture (the reference's pinned PaddleOCR-VL-1.6 shapes; random-init fp16 w
 Precision: weights and every intermediate activation in fp16; residual streams,
 normalisation statistics and logits in f32.  Attention runs on this library's
 kernels through the C ABI (vision varlen, decoder causal prefill with the KV
-cache written in place, batched split-KV decode with the KV append fused);
-the dense layers are cuBLAS GEMMs and torch elementwise kernels on the same
-stream.  The batched decode step is captured once in a CUDA graph and
-replayed; tokens are read back once per chunk of steps, as the reference's
-chunked greedy driver does (lib.rs:2309-2366).
+cache written in place, batched split-KV decode with the KV append fused), and
+so do the elementwise passes (residual add + LayerNorm / RMSNorm, GELU, SiLU
+gate; each residual add rides in the next norm's pass); the dense layers are
+cuBLAS GEMMs on the same stream.  The batched decode step is captured once in
+a CUDA graph and replayed; tokens are read back once per chunk of steps, as
+the reference's chunked greedy driver does (lib.rs:2309-2366).
 
 Weight lists are in the canonical order shared with the CPU oracle
 (oracle/pvlc_model_oracle.cpp, pvlc_oracle_generate).
@@ -133,10 +134,6 @@ def ocr_prompt_ids(image_tokens: int, cfg: ModelConfig = ModelConfig()):
         list(OCR_PROMPT_SUFFIX_IDS)
 
 
-def _rms(x32, w32, eps):
-    return (x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps) * w32).half()
-
-
 def _bilinear_axis(source: int, target: int):
     """crates/pvlc-cpu-ref/src/lib.rs:265-278 in f32 for every target index."""
     idx = np.arange(target, dtype=np.float32)
@@ -240,29 +237,33 @@ class OcrEngine:
         ws = torch.empty(ops.vision_workspace_bytes(N, heads, hd), dtype=torch.uint8,
                          device=self.device)
         ctx = torch.empty((N, heads, hd), dtype=torch.float16, device=self.device)
+        # each residual add rides in the next norm's pass (ops.add_norm)
+        pending = None
         for L in self.vlayers:
-            n1 = F.layer_norm(h32, (H,), *L["ln1"], eps=c.vision_eps).half()
+            n1 = ops.add_norm(h32, L["ln1"][0], c.vision_eps, bias=L["ln1"][1], delta=pending)
             q = F.linear(n1, *L["q"]).view(N, heads, hd)
             k = F.linear(n1, *L["k"]).view(N, heads, hd)
             v = F.linear(n1, *L["v"]).view(N, heads, hd)
             ops.vision_varlen_attention(q, k, v, cu, rcos, rsin, out=ctx, workspace=ws)
-            h32 += F.linear(ctx.view(N, H), *L["o"]).float()
-            n2 = F.layer_norm(h32, (H,), *L["ln2"], eps=c.vision_eps).half()
-            a = F.gelu(F.linear(n2, *L["fc1"]).float(), approximate="tanh").half()
-            h32 += F.linear(a, *L["fc2"]).float()
-        return F.layer_norm(h32, (H,), *self.post_ln, eps=c.vision_eps).half()
+            o = F.linear(ctx.view(N, H), *L["o"])
+            n2 = ops.add_norm(h32, L["ln2"][0], c.vision_eps, bias=L["ln2"][1], delta=o)
+            a = ops.gelu_(F.linear(n2, *L["fc1"]))
+            pending = F.linear(a, *L["fc2"])
+        return ops.add_norm(h32, self.post_ln[0], c.vision_eps, bias=self.post_ln[1],
+                            delta=pending)
 
     def project(self, feats, grids):
         """crates/pvlc-cpu-ref/src/lib.rs:2598-2678: [N, 1152] fp16 -> [N/4, 1024] fp16."""
         c = self.cfg
         H, M = c.vision_hidden, c.vision_hidden * c.merge * c.merge
-        pre = F.layer_norm(feats.float(), (H,), *self.proj["ln"], eps=c.projector_eps).half()
+        pre = ops.add_norm(feats.float(), self.proj["ln"][0], c.projector_eps,
+                           bias=self.proj["ln"][1])
         order, base = [], 0
         for g in grids:
             order.append(self._grid_tables(g)[3] + base)
             base += g[0] * g[1] * g[2]
         merged = pre.index_select(0, torch.cat(order)).view(-1, M)
-        a = F.gelu(F.linear(merged, *self.proj["l1"]).float()).half()
+        a = ops.gelu_(F.linear(merged, *self.proj["l1"]), erf=True)
         return F.linear(a, *self.proj["l2"])
 
     def encode_images(self, patches_list, grids):
@@ -297,15 +298,14 @@ class OcrEngine:
             self._grid_cache[key] = hit
         return hit
 
-    def _layer_mlp(self, L, h32):
+    def _layer_mlp(self, L, h32, o):
+        """h32 += o; SwiGLU MLP of RMSNorm(h32); returns the MLP output (added to h32 by the
+        next norm)."""
         c = self.cfg
-        n2 = _rms(h32, L["n2"], c.rms_eps)
-        gu = F.linear(n2, L["gate_up"])
-        a = (F.silu(gu[:, : c.intermediate].float()) * gu[:, c.intermediate:].float()).half()
-        h32 += F.linear(a, L["down"]).float()
+        n2 = ops.add_norm(h32, L["n2"], c.rms_eps, delta=o)
+        return F.linear(ops.silu_mul(F.linear(n2, L["gate_up"])), L["down"])
 
-    def _logits(self, last32):
-        fn = _rms(last32, self.final_norm, self.cfg.rms_eps)
+    def _logits(self, fn):
         return torch.mm(fn, self.lm_head.t(), out_dtype=torch.float32)
 
     def recognize(self, images, max_new_tokens: int = 512, chunk: int = 32,
@@ -371,8 +371,9 @@ class OcrEngine:
         offs = np.concatenate([[0], np.cumsum(Ts)])
         NT = int(offs[-1])
         ctx = torch.empty((NT, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
+        pending = None
         for l, L in enumerate(self.dlayers):
-            n1 = _rms(h32, L["n1"], c.rms_eps)
+            n1 = ops.add_norm(h32, L["n1"], c.rms_eps, delta=pending)
             q = F.linear(n1, L["q"]).view(NT, c.query_heads, c.head_dim)
             k = F.linear(n1, L["k"]).view(NT, c.kv_heads, c.head_dim)
             v = F.linear(n1, L["v"]).view(NT, c.kv_heads, c.head_dim)
@@ -380,10 +381,10 @@ class OcrEngine:
                 s, e = int(offs[b]), int(offs[b + 1])
                 ops.decoder_prefill(q[s:e], k[s:e], v[s:e], tables[b][0], tables[b][1],
                                     kc[l, b], vc[l, b], out=ctx[s:e])
-            h32 += F.linear(ctx.view(NT, QW), L["o"]).float()
-            self._layer_mlp(L, h32)
+            pending = self._layer_mlp(L, h32, F.linear(ctx.view(NT, QW), L["o"]))
         last = torch.tensor(offs[1:] - 1, dtype=torch.int64, device=dev)
-        logits0 = self._logits(h32.index_select(0, last))
+        fn = ops.add_norm(h32, self.final_norm, c.rms_eps, delta=pending)
+        logits0 = self._logits(fn.index_select(0, last))
         first = torch.argmax(logits0, dim=-1)
         if ev:
             ev[2].record()
@@ -446,17 +447,17 @@ class _DecodeGraph:
         eng, c = self.eng, self.eng.cfg
         B = self.B
         h32 = eng.embed.index_select(0, self.tok).float()
+        pending = None
         for l, L in enumerate(eng.dlayers):
-            n1 = _rms(h32, L["n1"], c.rms_eps)
+            n1 = ops.add_norm(h32, L["n1"], c.rms_eps, delta=pending)
             torch.mm(n1, L["q"].t(), out=self.q.view(B, -1))
             torch.mm(n1, L["k"].t(), out=self.k.view(B, -1))
             torch.mm(n1, L["v"].t(), out=self.v.view(B, -1))
             ops.decode(self.q, self.k, self.v, self.rcos, self.rsin, self.kp[l], self.vp[l],
                        self.ct, self.cap, self.cap - 1, self.ws[l], rope_row=self.rope_row,
                        out=self.ctx)
-            h32 += F.linear(self.ctx.view(B, -1), L["o"]).float()
-            eng._layer_mlp(L, h32)
-        self.logits = eng._logits(h32)
+            pending = eng._layer_mlp(L, h32, F.linear(self.ctx.view(B, -1), L["o"]))
+        self.logits = eng._logits(ops.add_norm(h32, eng.final_norm, c.rms_eps, delta=pending))
         self.tok.copy_(torch.argmax(self.logits, dim=-1))
         self.ct += 1
         self.rope_row += 1

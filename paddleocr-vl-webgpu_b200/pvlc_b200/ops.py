@@ -171,3 +171,41 @@ def image_patches(rgb, out_height: int, out_width: int, patch_size: int = 14, ou
                                       _ptr(workspace), workspace.numel(), _ptr(out), _stream())
     abi.check(st, "pvlc_image_patches")
     return out
+
+
+def add_norm(residual, weight, eps: float, bias=None, delta=None, out=None):
+    """residual [rows, width] f32 CUDA (+= delta [rows, width] fp16 in place when given), then
+    LayerNorm (with bias) or RMSNorm (bias None) of each row * weight (+ bias), as fp16."""
+    rows, width = residual.shape
+    _need(residual, torch.float32, (rows, width), "residual")
+    _need(weight, torch.float32, (width,), "weight")
+    if bias is not None:
+        _need(bias, torch.float32, (width,), "bias")
+    if delta is not None:
+        _need(delta, torch.float16, (rows, width), "delta")
+    if out is None:
+        out = torch.empty((rows, width), dtype=torch.float16, device=residual.device)
+    _need(out, torch.float16, (rows, width), "out")
+    st = abi.lib().pvlc_add_norm(_ptr(residual), _ptr(delta), rows, width, _ptr(weight),
+                                 _ptr(bias), float(eps), _ptr(out), _stream())
+    abi.check(st, "pvlc_add_norm")
+    return out
+
+
+def gelu_(x, erf: bool = False):
+    """In-place GELU (tanh form, or erf form) of an fp16 CUDA tensor."""
+    _need(x, torch.float16, None, "x")
+    abi.check(abi.lib().pvlc_gelu(_ptr(x), x.numel(), 1 if erf else 0, _stream()), "pvlc_gelu")
+    return x
+
+
+def silu_mul(gate_up, out=None):
+    """[rows, 2I] fp16 (gate | up) -> [rows, I] fp16 silu(gate) * up."""
+    rows, w2 = gate_up.shape
+    _need(gate_up, torch.float16, (rows, w2), "gate_up")
+    if out is None:
+        out = torch.empty((rows, w2 // 2), dtype=torch.float16, device=gate_up.device)
+    _need(out, torch.float16, (rows, w2 // 2), "out")
+    abi.check(abi.lib().pvlc_silu_mul(_ptr(gate_up), rows, w2 // 2, _ptr(out), _stream()),
+              "pvlc_silu_mul")
+    return out
