@@ -29,8 +29,7 @@ Weight lists are in the canonical order shared with the CPU oracle
 """
 from __future__ import annotations
 
-import ctypes
-from dataclasses import dataclass, asdict
+from dataclasses import dataclass
 
 import numpy as np
 import torch

@@ -5,7 +5,6 @@ crates/pvlc-cpu-ref/src/lib.rs:280-367 (torch on the same device), rounded to fp
 Tolerance: 2e-3 absolute + 2e-3 relative on the fp16 outputs; the updated f32 residual
 stream is compared exactly (the same single f32 addition).
 """
-import numpy as np
 import pytest
 import torch
 
