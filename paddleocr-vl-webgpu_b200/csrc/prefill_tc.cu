@@ -692,13 +692,23 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t rows, uint32_t heads,
 int prefill_query_tile() { return ptc::QT * ptc::TOK; }
 
 // Q tiles per KV head, split into the heaviest (one CTA each, K range split
-// between the two streams) and the lightest (paired two per CTA) so that the
-// CTAs of both KV heads fit one wave of `sms`.
+// between the two streams) and the lightest (paired two per CTA).  Pairing
+// is used only where it makes the CTAs of both KV heads one wave of `sms`
+// AND each pair's heavier tile, whose K tiles one stream walks alone, ends no
+// later than the heaviest split CTA (ceil(nk_max / 2) steps); otherwise every
+// Q tile is a split CTA and the grid runs in several waves, heaviest first.
+// (Pairing a long tile with a 1-tile one at T = 4100 ran its 32 K tiles on
+// one stream: 109 us per call against ~86 us for the split waves.)
 void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_light) {
   const uint32_t n_qt = (tokens + ptc::TOK - 1) / ptc::TOK;
   const uint32_t per_head = sms > 0 ? (uint32_t)sms / ptc::KVH : n_qt;
-  uint32_t light = n_qt > per_head ? 2 * (n_qt - per_head) : 0;
-  if (light > n_qt) light = n_qt & ~1u;
+  uint32_t light = 0;
+  if (n_qt > per_head && 2 * (n_qt - per_head) <= n_qt) {
+    const uint32_t l1 = 2 * (n_qt - per_head);
+    const uint32_t nk_pair = ((l1 - 1) * ptc::TOK + ptc::TOK - 1) / ptc::BN + 1;
+    const uint32_t nk_max = (tokens - 1) / ptc::BN + 1;
+    if (nk_pair <= (nk_max + 1) / 2) light = l1;
+  }
   *n_light = light;
   *n_split = n_qt - light;
 }

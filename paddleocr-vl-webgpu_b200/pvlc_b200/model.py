@@ -338,10 +338,32 @@ class OcrEngine:
 
         images_patches: list of [N_i, 588] device tensors; grids: list of (t, h, w).
         Returns dict(tokens=list of lists, stop=list of reasons, logits=optional list of
-        [steps_i, vocab] f32 CPU tensors (the logits each token was chosen from))."""
+        [steps_i, vocab] f32 CPU tensors (the logits each token was chosen from)).
+
+        Nothing between the first encoder launch and the last decode chunk waits for the
+        device except the reads of the first tokens and of each chunk's tokens: the
+        prompt plan is built and uploaded (pinned, asynchronous) before the encoder is
+        queued, and the next decode chunk is queued before a chunk's tokens are read."""
         c, dev = self.cfg, self.device
         B = len(grids)
         m2 = c.merge * c.merge
+        # ---- host-side prompt plan
+        ids = [ocr_prompt_ids(g[0] * g[1] * g[2] // m2, c) for g in grids]
+        Ts = [len(x) for x in ids]
+        cap = max(Ts) + max_new_tokens + 1
+        offs = np.concatenate([[0], np.cumsum(Ts)]).astype(np.int64)
+        NT = int(offs[-1])
+        flat = np.concatenate([np.asarray(x, dtype=np.int64) for x in ids])
+        img_pos = np.flatnonzero(flat == c.image_token_id)
+        if img_pos.size != sum(g[0] * g[1] * g[2] // m2 for g in grids):
+            raise ValueError("image placeholder count does not match the images")
+        tables, deltas = [], []
+        for x, g in zip(ids, grids):
+            tc, ts, delta = self._prompt_tables(x, g)
+            tables.append((tc, ts))
+            deltas.append(delta)
+        plan = _upload(np.concatenate([flat, img_pos, offs[1:] - 1]), dev)
+        ids_t, img_idx, last = torch.split(plan, [NT, int(img_pos.size), B])
         ev = None
         if timings is not None:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
@@ -349,26 +371,14 @@ class OcrEngine:
         img = self.encode_images(images_patches, grids)
         if ev:
             ev[1].record()
-        ids = [ocr_prompt_ids(g[0] * g[1] * g[2] // m2, c) for g in grids]
-        Ts = [len(x) for x in ids]
-        cap = max(Ts) + max_new_tokens + 1
-        QW, KW = c.query_heads * c.head_dim, c.kv_heads * c.head_dim
+        QW = c.query_heads * c.head_dim
         Lyr = c.decoder_layers
         kc = torch.empty((Lyr, B, cap, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
         vc = torch.empty_like(kc)
         # ---- prefill: GEMMs over all prompts, attention per prompt
-        ids_t = torch.tensor([t for x in ids for t in x], dtype=torch.int64, device=dev)
         emb = self.embed.index_select(0, ids_t)
-        is_img = ids_t == c.image_token_id
-        emb[is_img] = torch.cat(img, 0)
+        emb.index_copy_(0, img_idx, torch.cat(img, 0))
         h32 = emb.float()
-        tables, deltas = [], []
-        for x, g in zip(ids, grids):
-            tc, ts, delta = self._prompt_tables(x, g)
-            tables.append((tc, ts))
-            deltas.append(delta)
-        offs = np.concatenate([[0], np.cumsum(Ts)])
-        NT = int(offs[-1])
         ctx = torch.empty((NT, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
         pending = None
         for l, L in enumerate(self.dlayers):
@@ -376,28 +386,43 @@ class OcrEngine:
             q = F.linear(n1, L["q"]).view(NT, c.query_heads, c.head_dim)
             k = F.linear(n1, L["k"]).view(NT, c.kv_heads, c.head_dim)
             v = F.linear(n1, L["v"]).view(NT, c.kv_heads, c.head_dim)
-            for b in range(B):
-                s, e = int(offs[b]), int(offs[b + 1])
-                ops.decoder_prefill(q[s:e], k[s:e], v[s:e], tables[b][0], tables[b][1],
-                                    kc[l, b], vc[l, b], out=ctx[s:e])
+            ops.decoder_prefill_packed(q, k, v, offs, tables, kc[l], vc[l], ctx)
             pending = self._layer_mlp(L, h32, F.linear(ctx.view(NT, QW), L["o"]))
-        last = torch.tensor(offs[1:] - 1, dtype=torch.int64, device=dev)
         fn = ops.add_norm(h32, self.final_norm, c.rms_eps, delta=pending)
         logits0 = self._logits(fn.index_select(0, last))
         first = torch.argmax(logits0, dim=-1)
         if ev:
             ev[2].record()
-        rec = [logits0.cpu()] if record_logits else None
-        state = greedy.BatchedGreedyState(first.cpu().numpy(), max_new_tokens, c.eos_token_id)
-        # ---- batched decode, one CUDA graph per step shape
-        dec = _DecodeGraph(self, kc, vc, cap, first, torch.tensor(Ts, dtype=torch.int32),
-                           torch.tensor(deltas, dtype=torch.int32))
-        while not state.all_done():
-            n = min(chunk, state.remaining_decode_steps())
+        first_host = _download(first)
+        rec = [_download(logits0)] if record_logits else None
+        # ---- batched decode, one CUDA graph per step shape; one chunk always queued
+        # ahead of the chunk whose tokens are being applied
+        dec = _DecodeGraph(self, kc, vc, cap, first, np.asarray(Ts), np.asarray(deltas))
+        inflight = []
+        budget = max_new_tokens - 1        # decode steps a request can still need
+
+        def queue(n):
             hist, lg = dec.run(n, record_logits)
-            state.apply_steps(hist.cpu().numpy())
+            inflight.append((n, _download(hist), _download(lg) if record_logits else None))
+
+        if budget > 0:
+            queue(min(chunk, budget))
+        first_host[1].synchronize()
+        state = greedy.BatchedGreedyState(first_host[0].numpy(), max_new_tokens, c.eos_token_id)
+        if record_logits:
+            rec[0][1].synchronize()
+            rec[0] = rec[0][0]
+        while inflight:
+            ahead = state.remaining_decode_steps() - sum(x[0] for x in inflight)
+            if ahead > 0:
+                queue(min(chunk, ahead))
+            _, (tok_host, done), lg = inflight.pop(0)
+            done.synchronize()
+            state.apply_steps(tok_host.numpy())
             if record_logits:
-                rec.append(lg.cpu())
+                lg[1].synchronize()
+                rec.append(lg[0])
+        dec.check_faults()
         if ev:
             ev[3].record()
             ev[3].synchronize()
@@ -413,28 +438,50 @@ class OcrEngine:
         return out
 
 
+def _upload(arr, dev):
+    """Host array -> device tensor through pinned memory, without waiting for the device."""
+    return torch.from_numpy(np.ascontiguousarray(arr)).pin_memory().to(dev, non_blocking=True)
+
+
+def _download(t):
+    """Device tensor -> (pinned host tensor, event): the copy is queued on the current
+    stream; the host tensor is valid once the event has completed."""
+    host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    host.copy_(t, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record()
+    return host, done
+
+
 class _DecodeGraph:
     """One batched decode step (embedding -> 18 layers with the fused decode attention ->
     LM head -> argmax), captured in a CUDA graph over static buffers."""
 
     def __init__(self, eng: OcrEngine, kc, vc, cap, first_tokens, prompt_lens, deltas):
+        """prompt_lens, deltas: host integer arrays [B] (prompt rows, M-RoPE decode delta)."""
         c, dev = eng.cfg, eng.device
         self.eng, self.cap = eng, cap
         B = first_tokens.shape[0]
         self.B = B
-        self.tok = first_tokens.clone().to(torch.int64)
-        self.ct = prompt_lens.to(dev).clone()                      # rows before the append
-        self.rope_row = (prompt_lens + deltas).to(dev).clone()     # decode position ct + delta
-        if int(self.rope_row.min()) < 0:
+        pl = np.asarray(prompt_lens, dtype=np.int64)
+        pos = pl + np.asarray(deltas, dtype=np.int64)
+        if pos.min() < 0:
             raise positions.PositionError("decode position is negative")
-        rows = int((prompt_lens + deltas).max()) + cap + 1
+        self.tok = first_tokens.clone().to(torch.int64)
+        rows_i32 = _upload(np.concatenate([pl, pos]).astype(np.int32), dev)
+        self.ct = rows_i32[:B]                  # rows before the append
+        self.rope_row = rows_i32[B:]            # decode position ct + delta
+        self.ct_max = int(pl.max())             # host copy of ct.max() (all rows step together)
+        rows = int(pos.max()) + cap + 1
         rc, rs = positions.linear_rope_tables(rows, c.decoder_theta, c.head_dim)
-        self.rcos, self.rsin = torch.from_numpy(rc).to(dev), torch.from_numpy(rs).to(dev)
-        self.kp = [torch.tensor([kc[l, b].data_ptr() for b in range(B)], dtype=torch.int64,
-                                device=dev) for l in range(c.decoder_layers)]
-        self.vp = [torch.tensor([vc[l, b].data_ptr() for b in range(B)], dtype=torch.int64,
-                                device=dev) for l in range(c.decoder_layers)]
-        self.ws = [ops.DecodeWorkspace(B, dev) for _ in range(c.decoder_layers)]
+        self.rcos, self.rsin = _upload(rc, dev), _upload(rs, dev)
+        # per-layer device tables of the B cache bases (kc[l, b], vc[l, b])
+        Lyr = c.decoder_layers
+        lb = np.arange(Lyr * B, dtype=np.int64).reshape(Lyr, B) * (kc.stride(1) * kc.element_size())
+        ptrs = _upload(np.concatenate([kc.data_ptr() + lb, vc.data_ptr() + lb], 0), dev)
+        self.kp = [ptrs[l] for l in range(Lyr)]
+        self.vp = [ptrs[Lyr + l] for l in range(Lyr)]
+        self.ws = [ops.DecodeWorkspace(B, dev) for _ in range(Lyr)]
         self.q = torch.empty((B, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
         self.k = torch.empty((B, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
         self.v = torch.empty_like(self.k)
@@ -477,7 +524,9 @@ class _DecodeGraph:
             self._step()
 
     def run(self, steps: int, record_logits: bool = False):
-        if int(self.ct.max()) + steps >= self.cap:
+        """Queue `steps` decode steps; returns their [steps, B] tokens (device) and, with
+        record_logits, their [steps, B, vocab] logits (device).  Does not wait."""
+        if self.ct_max + steps >= self.cap:
             raise abi.PvlcError(abi.CAPACITY_EXHAUSTED, "decode past the cache capacity")
         if self.graph is None:
             self._capture()
@@ -488,7 +537,11 @@ class _DecodeGraph:
             hist[i].copy_(self.tok)
             if record_logits:
                 lg.append(self.logits.clone())
+        self.ct_max += steps
+        return hist, (torch.stack(lg, 0) if record_logits else None)
+
+    def check_faults(self):
+        """Raise if any decode launch set a device fault flag (waits for the device)."""
         flags = sum(w.errors() for w in self.ws)
         if flags:
             raise abi.PvlcError(abi.DEVICE_FAULT_FLAG, f"decode fault flags {flags:#x}")
-        return hist, (torch.stack(lg, 0) if record_logits else None)

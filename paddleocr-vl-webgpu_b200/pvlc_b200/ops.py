@@ -99,6 +99,42 @@ def decoder_prefill(q, k, v, rope_cos, rope_sin, k_cache, v_cache, out=None):
     return out
 
 
+def decoder_prefill_packed(q, k, v, offsets, tables, k_caches, v_caches, out):
+    """decoder_prefill over B prompts packed back to back, one C-ABI call per prompt.
+
+    q: [NT,16,128], k, v: [NT,2,128] fp16 with prompt b at rows offsets[b]:offsets[b+1]
+    (host integers); tables: B (rope_cos, rope_sin) pairs as decoder_prefill takes them;
+    k_caches, v_caches: [B, capacity, 2, 128] fp16 (prompt b's cache at [b]); out like q.
+    The tensors are checked once; the per-prompt calls pass precomputed pointers, so the
+    host cost per prompt is the C call alone."""
+    NT = q.shape[0]
+    _need(q, torch.float16, (NT, QH, HD), "q")
+    _need(k, torch.float16, (NT, KVH, HD), "k")
+    _need(v, torch.float16, (NT, KVH, HD), "v")
+    _need(out, torch.float16, (NT, QH, HD), "out")
+    B, cap = k_caches.shape[0], k_caches.shape[1]
+    _need(k_caches, torch.float16, (B, cap, KVH, HD), "k_caches")
+    _need(v_caches, torch.float16, (B, cap, KVH, HD), "v_caches")
+    if len(offsets) != B + 1 or len(tables) != B or offsets[0] != 0 or offsets[-1] != NT:
+        raise ValueError("offsets / tables do not describe the packed prompts")
+    for rc, rs in tables:
+        _need(rc, torch.float32, (3, rc.shape[1], HD), "rope_cos")
+        _need(rs, torch.float32, (3, rc.shape[1], HD), "rope_sin")
+    fn, st = abi.lib().pvlc_attn_decoder_prefill, _stream()
+    qp, kp, vp, op = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    kcp, vcp = k_caches.data_ptr(), v_caches.data_ptr()
+    cstride = cap * KVH * HD * 2
+    for b in range(B):
+        s, e = int(offsets[b]), int(offsets[b + 1])
+        rc, rs = tables[b]
+        status = fn(qp + s * QH * HD * 2, kp + s * KVH * HD * 2, vp + s * KVH * HD * 2,
+                    rc.data_ptr(), rs.data_ptr(), rc.shape[1], e - s, cap, kcp + b * cstride,
+                    vcp + b * cstride, op + s * QH * HD * 2, st)
+        if status:
+            abi.check(status, f"pvlc_attn_decoder_prefill (prompt {b})")
+    return out
+
+
 class DecodeWorkspace:
     """Device scratch for batched decode (split partials + combine tickets + fault flags)."""
 

@@ -77,9 +77,43 @@ def test_config3_prefill(cuda_lib):
     _run_case(ids, grids, 1564 + 256, seed=3)
 
 
-@pytest.mark.parametrize("T", [1190, 2500, 4100])
-def test_long_prefill_paired_tiles(cuda_lib, T):
-    """Past 74 Q tiles per KV head the lightest tiles run two per CTA (one per
-    stream, sharing K/V tiles): one pair (1190), many pairs (2500), and every
-    tile paired with more CTAs than SMs (4100)."""
+@pytest.mark.parametrize("T", [1190, 1600, 1800, 2500, 4100])
+def test_long_prefill_schedules(cuda_lib, T):
+    """Past 74 Q tiles per KV head: one pair of light tiles (1190), the most pairs
+    that keep one wave (1600, 52 light tiles), and split CTAs only, in several waves
+    heaviest first, where pairing would outlast the heaviest CTA (1800, 2500, 4100)."""
     _run_case(list(range(3, 3 + T)), [], T + 5, seed=T)
+
+
+def test_packed_prompts_match_single_calls(cuda_lib):
+    """ops.decoder_prefill_packed (the engine's path: prompts back to back, one cache
+    slab per prompt) gives exactly the per-prompt decoder_prefill results."""
+    from pvlc_b200 import ops, positions
+    dev = torch.device("cuda")
+    prompts = [image_prompt(3, (4, 5), 6), image_prompt(20, (12, 10), 40), image_prompt(1, (2, 2), 1)]
+    Ts = [len(ids) for ids, _ in prompts]
+    offs = np.concatenate([[0], np.cumsum(Ts)])
+    NT, cap = int(offs[-1]), max(Ts) + 8
+    rng = np.random.default_rng(11)
+    q = torch.from_numpy(rng.standard_normal((NT, QH, HD)).astype(np.float16)).to(dev)
+    k = torch.from_numpy(rng.standard_normal((NT, KVH, HD)).astype(np.float16)).to(dev)
+    v = torch.from_numpy(rng.standard_normal((NT, KVH, HD)).astype(np.float16)).to(dev)
+    tables = []
+    for ids, grids in prompts:
+        pos, delta = positions.mrope_position_ids(ids, grids)
+        c, s_ = positions.mrope_tables(pos, delta, cap)
+        tables.append((torch.from_numpy(c).to(dev), torch.from_numpy(s_).to(dev)))
+    kc = torch.zeros((len(prompts), cap, KVH, HD), dtype=torch.float16, device=dev)
+    vc = torch.zeros_like(kc)
+    out = torch.empty_like(q)
+    ops.decoder_prefill_packed(q, k, v, offs, tables, kc, vc, out)
+    for b in range(len(prompts)):
+        s, e = int(offs[b]), int(offs[b + 1])
+        kc1 = torch.zeros((cap, KVH, HD), dtype=torch.float16, device=dev)
+        vc1 = torch.zeros_like(kc1)
+        ref = ops.decoder_prefill(q[s:e].contiguous(), k[s:e].contiguous(), v[s:e].contiguous(),
+                                  tables[b][0], tables[b][1], kc1, vc1)
+        assert torch.equal(out[s:e], ref)
+        assert torch.equal(kc[b], kc1) and torch.equal(vc[b], vc1)
+    with pytest.raises(ValueError):
+        ops.decoder_prefill_packed(q, k, v, offs[:-1], tables, kc, vc, out)
