@@ -318,6 +318,10 @@ class OcrEngine:
         cfgp = preprocess_config or preprocess.MODEL_CONFIG
         patches, grids = [], []
         ws = None
+        ev = None
+        if timings is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            ev[0].record()
         for im in images:
             t = im if isinstance(im, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(im))
             if not t.is_pinned():
@@ -330,7 +334,12 @@ class OcrEngine:
                 ws = torch.empty(need, dtype=torch.uint8, device=self.device)
             patches.append(ops.image_patches(d, h, w, cfgp.patch_size, workspace=ws))
             grids.append((1, h // cfgp.patch_size, w // cfgp.patch_size))
-        return self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings)
+        if ev:
+            ev[1].record()
+        res = self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings)
+        if ev:
+            timings.update(pages_ms=ev[0].elapsed_time(ev[1]))
+        return res
 
     def generate(self, images_patches, grids, max_new_tokens: int, chunk: int = 16,
                  record_logits: bool = False, timings: dict | None = None):
@@ -347,6 +356,10 @@ class OcrEngine:
         c, dev = self.cfg, self.device
         B = len(grids)
         m2 = c.merge * c.merge
+        ev = None
+        if timings is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            ev[4].record()
         # ---- host-side prompt plan
         ids = [ocr_prompt_ids(g[0] * g[1] * g[2] // m2, c) for g in grids]
         Ts = [len(x) for x in ids]
@@ -364,9 +377,7 @@ class OcrEngine:
             deltas.append(delta)
         plan = _upload(np.concatenate([flat, img_pos, offs[1:] - 1]), dev)
         ids_t, img_idx, last = torch.split(plan, [NT, int(img_pos.size), B])
-        ev = None
-        if timings is not None:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        if ev:
             ev[0].record()
         img = self.encode_images(images_patches, grids)
         if ev:
@@ -426,7 +437,8 @@ class OcrEngine:
         if ev:
             ev[3].record()
             ev[3].synchronize()
-            timings.update(encode_ms=ev[0].elapsed_time(ev[1]),
+            timings.update(plan_ms=ev[4].elapsed_time(ev[0]),
+                           encode_ms=ev[0].elapsed_time(ev[1]),
                            prefill_ms=ev[1].elapsed_time(ev[2]),
                            decode_ms=ev[2].elapsed_time(ev[3]),
                            decode_steps=int(state.decode_steps.max()))

@@ -16,7 +16,8 @@ TOL = dict(atol=2e-3, rtol=2e-3)
 
 @pytest.mark.parametrize("rows,width,layer,with_delta", [
     (3, 1152, True, False), (257, 1152, True, True), (5, 1024, False, True),
-    (1000, 1024, False, False), (2, 4608, True, True)])
+    (1000, 1024, False, False), (9, 8, True, True), (17, 2048, False, True),
+    (4, 2056, True, True), (2, 4608, True, True)])
 def test_add_norm(cuda_lib, rows, width, layer, with_delta):
     g = torch.Generator(device="cuda")
     g.manual_seed(rows + width)
@@ -39,19 +40,22 @@ def test_add_norm(cuda_lib, rows, width, layer, with_delta):
 
 
 @pytest.mark.parametrize("erf", [False, True])
-def test_gelu(cuda_lib, erf):
-    x = (torch.linspace(-8, 8, 4304 * 3, device="cuda")).half().reshape(3, 4304)
+@pytest.mark.parametrize("n", [4304 * 3, 4304 * 3 + 6, 2])
+def test_gelu(cuda_lib, erf, n):
+    # n % 8 != 0 runs the pair tail after the 16-byte body
+    x = (torch.linspace(-8, 8, n, device="cuda")).half()
     ref = torch.nn.functional.gelu(x.float(), approximate="none" if erf else "tanh").half()
     got = ops.gelu_(x.clone(), erf=erf)
     torch.cuda.synchronize()
     torch.testing.assert_close(got.float(), ref.float(), **TOL)
 
 
-def test_silu_mul(cuda_lib):
+@pytest.mark.parametrize("width", [3072, 6])   # 8-wide and pair accesses
+def test_silu_mul(cuda_lib, width):
     g = torch.Generator(device="cuda")
     g.manual_seed(4)
-    gu = (torch.randn((77, 2 * 3072), generator=g, device="cuda") * 4).half()
-    ref = (torch.nn.functional.silu(gu[:, :3072].float()) * gu[:, 3072:].float()).half()
+    gu = (torch.randn((77, 2 * width), generator=g, device="cuda") * 4).half()
+    ref = (torch.nn.functional.silu(gu[:, :width].float()) * gu[:, width:].float()).half()
     got = ops.silu_mul(gu)
     torch.cuda.synchronize()
     torch.testing.assert_close(got.float(), ref.float(), **TOL)
