@@ -132,6 +132,32 @@ int pvlc_attn_decoder_prefill(const pvlc_half* q, const pvlc_half* k, const pvlc
                               uint32_t tokens, uint32_t cache_capacity, pvlc_half* k_cache,
                               pvlc_half* v_cache, pvlc_half* out, void* stream);
 
+/* Batched variant of pvlc_attn_decoder_prefill (no counterpart in the
+ * reference): `prompts` prompts packed back to back in one launch pair, so a
+ * serving engine makes one call per layer instead of one per prompt, and the
+ * Q tiles of all prompts share the GPU (each prompt's tiles heaviest first).
+ *   q: [rows, 16, 128], k, v: [rows, 2, 128], out: [rows, 16, 128] fp16,
+ *     prompt b at rows offsets[b] .. offsets[b + 1] (host array, offsets[0] = 0,
+ *     every prompt at least one token, rows = offsets[prompts]).
+ *   rope_cos[b], rope_sin[b]: host arrays of device pointers to prompt b's
+ *     [3, rope_rows[b], 128] f32 tables (rope_rows: host array).
+ *   k_cache, v_cache: prompt b's [cache_capacity, 2, 128] fp16 caches at
+ *     + b * cache_stride elements (cache_stride >= cache_capacity * 256, a
+ *     multiple of 8).
+ * Each prompt is held to pvlc_attn_decoder_prefill's checks, with the same
+ * codes; 1 <= prompts <= PVLC_PREFILL_MAX_PROMPTS and at most 65535 Q tiles
+ * of 16 tokens in all, else PVLC_INVALID_DECODER_GEOMETRY.  Results equal
+ * pvlc_attn_decoder_prefill's per prompt within the fp16 output rounding
+ * (bit-identical where the single call splits every Q tile, i.e. prompts of
+ * at most 1184 tokens). */
+#define PVLC_PREFILL_MAX_PROMPTS 256u
+int pvlc_attn_decoder_prefill_batch(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                                    const uint32_t* offsets, uint32_t prompts,
+                                    const float* const* rope_cos, const float* const* rope_sin,
+                                    const uint32_t* rope_rows, pvlc_half* k_cache,
+                                    pvlc_half* v_cache, uint64_t cache_stride,
+                                    uint32_t cache_capacity, pvlc_half* out, void* stream);
+
 /* ----------------------------------------------------------------------------
  * Path 3: batched single-token GQA decode against per-sequence fp16 KV caches
  * (split-KV flash decoding with an in-kernel combine), with the decode M-RoPE
@@ -168,6 +194,23 @@ int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half
                      pvlc_half* const* v_cache, const uint32_t* cache_tokens,
                      uint32_t cache_capacity, uint32_t max_cache_tokens, uint32_t batch,
                      void* workspace, size_t workspace_bytes, pvlc_half* out, void* stream);
+/* pvlc_attn_decode with row strides: sequence b's q row starts at
+ * q + b * q_row_stride and its k_new / v_new rows at k_new / v_new +
+ * b * kv_row_stride (elements; each row itself contiguous).  It has no
+ * counterpart in the reference.  It lets the three projections come out of
+ * one GEMM: with a [batch, 2560] output, q = base, k_new = base + 2048,
+ * v_new = base + 2304, q_row_stride = kv_row_stride = 2560.  Strides must be
+ * multiples of 8 and at least 2048 (q) / 256 (k_new, v_new); otherwise
+ * PVLC_LENGTH_MISMATCH.  pvlc_attn_decode is this call with strides 2048 and
+ * 256. */
+int pvlc_attn_decode_strided(const pvlc_half* q, uint32_t q_row_stride, const pvlc_half* k_new,
+                             const pvlc_half* v_new, uint32_t kv_row_stride,
+                             const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                             const uint32_t* rope_row, pvlc_half* const* k_cache,
+                             pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                             uint32_t cache_capacity, uint32_t max_cache_tokens, uint32_t batch,
+                             void* workspace, size_t workspace_bytes, pvlc_half* out,
+                             void* stream);
 /* Synchronously reads and clears the device-side fault flags of a decode
  * workspace (bit 0: cache row out of range, bit 1: rope row out of range,
  * bit 2: misaligned cache pointer, bit 3: pipeline wait timed out).  Returns
@@ -211,8 +254,9 @@ int pvlc_attn_decode_noalloc(const pvlc_half* q, const pvlc_half* k_new, const p
  * image to [out_height, out_width, 3] (22-bit fixed-point coefficients, int64
  * accumulation, :3092-3273) and the normalised patch-major f32 values
  * [(out_height/p)*(out_width/p), 3*p*p], bit-identical to the host path.
- * The coefficient tables are computed on the host and copied to `workspace`
- * on `stream` (pageable copies, so the call may block briefly).
+ * The coefficient tables are computed into `workspace` by a kernel on
+ * `stream` (bit-identical to the reference's f64 computation); the call
+ * copies nothing from the host.
  */
 size_t pvlc_image_patches_workspace_bytes(uint32_t height, uint32_t width, uint32_t out_height,
                                           uint32_t out_width);

@@ -111,6 +111,8 @@ struct Params {
   __half* const* k_cache;
   __half* const* v_cache;
   const uint32_t* cache_tokens;
+  uint32_t q_stride;     // elements between sequences' q rows (16 x 128 when packed)
+  uint32_t kv_stride;    // elements between sequences' k_new / v_new rows (2 x 128)
   uint32_t rope_rows;
   uint32_t capacity;
   uint32_t max_cache_tokens;
@@ -436,14 +438,14 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         // release the copy warp
         const uint32_t ct0 = __ldg(p.cache_tokens + b);
         const uint32_t rr0 = p.rope_row ? __ldg(p.rope_row + b) : ct0;
-        prefetch_l2(reinterpret_cast<const uint8_t*>(p.q + (size_t)b * QH * HD) + lane * 128);
+        prefetch_l2(reinterpret_cast<const uint8_t*>(p.q + (size_t)b * p.q_stride) + lane * 128);
         if (lane < 24 && rr0 < p.rope_rows) {
           const float* tab = (lane & 4) ? p.rope_sin : p.rope_cos;
           prefetch_l2(reinterpret_cast<const uint8_t*>(tab + ((size_t)(lane >> 3) * p.rope_rows + rr0) * HD) +
                       (lane & 3) * 128);
         } else if (lane >= 24) {
           const __half* nr = (lane & 4) ? p.v_new : p.k_new;
-          prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * KVH * HD) + (lane & 3) * 128);
+          prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * p.kv_stride) + (lane & 3) * 128);
         }
         __syncwarp();
         if (lane == 0) {
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         const uint32_t ct = __ldg(p.cache_tokens + b);
         const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + b) : ct;
         const int h = lane >> 1;
-        const __half* qrow = p.q + ((size_t)b * QH + h) * HD;
+        const __half* qrow = p.q + (size_t)b * p.q_stride + (size_t)h * HD;
         __half* qdst = qs + (slot * QH + h) * Q_PITCH;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -479,8 +481,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
           // 8(l%16)..+7; the M-RoPE partners (d +- 64) sit in lane l ^ 8
           const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
-          const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)b * KVH * HD) + lane);
-          const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)b * KVH * HD) + lane);
+          const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)b * p.kv_stride) + lane);
+          const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)b * p.kv_stride) + lane);
           uint4 ky;
           ky.x = __shfl_xor_sync(0xffffffffu, kx.x, 8);
           ky.y = __shfl_xor_sync(0xffffffffu, kx.y, 8);
@@ -879,6 +881,8 @@ int decode_launch(const DecodeArgs& a, cudaStream_t stream) {
   p.k_cache = reinterpret_cast<__half* const*>(a.k_cache);
   p.v_cache = reinterpret_cast<__half* const*>(a.v_cache);
   p.cache_tokens = a.cache_tokens;
+  p.q_stride = a.q_stride;
+  p.kv_stride = a.kv_stride;
   p.rope_rows = a.rope_rows;
   p.capacity = a.capacity;
   p.max_cache_tokens = a.max_cache_tokens;
@@ -976,6 +980,6 @@ extern "C" int pvlc_attn_decode_noalloc(const pvlc_half* q, const pvlc_half* k_n
   if (cudaMemsetAsync(scratch, 0, zero_bytes, s) != cudaSuccess) return PVLC_CUDA_ERROR;
   DecodeArgs a{q,       k_new,    v_new,   rope_cos,     rope_sin,       rope_rows,
                rope_row, k_cache, v_cache, cache_tokens, cache_capacity, max_cache_tokens,
-               batch,   scratch,  out,     sms};
+               batch,   scratch,  out,     sms,          16u * 128u,     2u * 128u};
   return decode_launch(a, s);
 }

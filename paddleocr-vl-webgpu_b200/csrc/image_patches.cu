@@ -5,9 +5,14 @@
 // 3092-3273).  The arithmetic is integer: 22-bit fixed-point coefficients
 // computed once per (input size, output size) in f64, int64 accumulation per
 // output byte, rounding by the 2^21 bias and an arithmetic shift, clamp to
-// [0, 255].  The coefficients are computed here on the host exactly as the
-// reference does; the two resample passes and the patch layout run on the GPU
-// and are bit-identical to the host computation.
+// [0, 255].  The coefficient tables are computed on the device by
+// coeff_kernel, one thread per output index, with the reference's f64
+// operations in the reference's order, each explicitly rounded (no fused
+// multiply-add), so the tables equal the reference's bit for bit; nothing is
+// uploaded, so a call never waits for the stream (an upload of host-computed
+// tables from pageable memory made every page wait for the previous one).
+// The two resample passes and the patch layout are bit-identical to the host
+// computation.
 //
 // Pass 1 (horizontal, only when the width changes): one thread per output
 //   byte (y, ox, c) of the [H, OW, 3] intermediate.
@@ -30,53 +35,57 @@
 namespace pvlc {
 namespace img {
 
-struct Coeffs {
-  int ksize;
-  std::vector<int32_t> table;   // [out][2 + ksize]: first tap, tap count, weights
-};
-
 // crates/pvlc-cpu-ref/src/lib.rs:3141-3208 (pillow_bicubic_coefficients,
-// pillow_bicubic_filter with a = -0.5).
-double bicubic_filter(double x) {
-  const double a = -0.5;
-  x = std::fabs(x);
-  if (x < 1.0) return ((a + 2.0) * x - (a + 3.0)) * x * x + 1.0;
-  if (x < 2.0) return (((x - 5.0) * x + 8.0) * x - 4.0) * a;
+// pillow_bicubic_filter with a = -0.5), one output index per thread: the
+// same f64 operations in the same order, each rounded once (__d*_rn are never
+// fused into a multiply-add).
+__device__ double bicubic_filter_dev(double x) {
+  x = fabs(x);
+  if (x < 1.0) return __dadd_rn(__dmul_rn(__dmul_rn(__dsub_rn(__dmul_rn(1.5, x), 2.5), x), x), 1.0);
+  if (x < 2.0)
+    return __dmul_rn(__dsub_rn(__dmul_rn(__dadd_rn(__dmul_rn(__dsub_rn(x, 5.0), x), 8.0), x), 4.0),
+                     -0.5);
   return 0.0;
 }
 
-Coeffs coefficients(uint32_t in_size, uint32_t out_size) {
-  const double scale = (double)in_size / (double)out_size;
+__global__ void __launch_bounds__(128) coeff_kernel(uint32_t in_size, uint32_t out_size, int ksize,
+                                                     int32_t* __restrict__ table) {
+  const uint32_t o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= out_size) return;
+  const double scale = __ddiv_rn((double)in_size, (double)out_size);
   const double filter_scale = scale > 1.0 ? scale : 1.0;
-  const double support = 2.0 * filter_scale;
-  Coeffs c;
-  c.ksize = (int)std::ceil(support) * 2 + 1;
-  c.table.assign((size_t)out_size * (2 + c.ksize), 0);
-  const double inv = 1.0 / filter_scale;
-  std::vector<double> w(c.ksize);
-  for (uint32_t o = 0; o < out_size; ++o) {
-    const double center = ((double)o + 0.5) * scale;
-    long long lo = (long long)(center - support + 0.5);
-    if (lo < 0) lo = 0;
-    long long hi = (long long)(center + support + 0.5);
-    if (hi > (long long)in_size) hi = in_size;
-    const int count = hi > lo ? (int)(hi - lo) : 0;
-    double sum = 0.0;
-    for (int j = 0; j < count; ++j) {
-      w[j] = bicubic_filter(((double)j + (double)lo - center + 0.5) * inv);
-      sum += w[j];
+  const double support = __dmul_rn(2.0, filter_scale);
+  const double inv = __ddiv_rn(1.0, filter_scale);
+  const double center = __dmul_rn(__dadd_rn((double)o, 0.5), scale);
+  long long lo = (long long)__dadd_rn(__dsub_rn(center, support), 0.5);
+  if (lo < 0) lo = 0;
+  long long hi = (long long)__dadd_rn(__dadd_rn(center, support), 0.5);
+  if (hi > (long long)in_size) hi = in_size;
+  const int count = hi > lo ? (int)(hi - lo) : 0;
+  auto weight = [&](int j) {
+    return bicubic_filter_dev(
+        __dmul_rn(__dadd_rn(__dsub_rn(__dadd_rn((double)j, (double)lo), center), 0.5), inv));
+  };
+  double sum = 0.0;
+  for (int j = 0; j < count; ++j) sum = __dadd_rn(sum, weight(j));
+  int32_t* row = table + (size_t)o * (2 + ksize);
+  row[0] = (int32_t)lo;
+  row[1] = count;
+  for (int j = 0; j < ksize; ++j) {
+    int32_t v = 0;
+    if (j < count) {
+      double w = weight(j);
+      if (sum != 0.0) w = __ddiv_rn(w, sum);
+      const double sc = __dmul_rn(w, (double)(1u << 22));
+      v = w < 0.0 ? (int32_t)__dadd_rn(-0.5, sc) : (int32_t)__dadd_rn(0.5, sc);
     }
-    if (sum != 0.0)
-      for (int j = 0; j < count; ++j) w[j] /= sum;
-    int32_t* row = &c.table[(size_t)o * (2 + c.ksize)];
-    row[0] = (int32_t)lo;
-    row[1] = count;
-    for (int j = 0; j < count; ++j) {
-      const double s = w[j] * (double)(1u << 22);
-      row[2 + j] = w[j] < 0.0 ? (int32_t)(-0.5 + s) : (int32_t)(0.5 + s);
-    }
+    row[2 + j] = v;
   }
-  return c;
+}
+
+int kernel_size(uint32_t in_size, uint32_t out_size) {
+  const double scale = (double)in_size / (double)out_size;
+  return (int)std::ceil(2.0 * (scale > 1.0 ? scale : 1.0)) * 2 + 1;
 }
 
 __device__ __forceinline__ uint8_t clip_u8(long long acc) {
@@ -183,27 +192,22 @@ int pvlc_image_patches(const uint8_t* rgb, uint32_t height, uint32_t width, uint
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const uint8_t* stage = rgb;
   if (out_width != width) {
-    const img::Coeffs ch = img::coefficients(width, out_width);
-    // pageable source: the call returns once the bytes are staged
-    if (cudaMemcpyAsync(ws + h_off, ch.table.data(), ch.table.size() * sizeof(int32_t),
-                        cudaMemcpyHostToDevice, s) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
+    const int kh = img::kernel_size(width, out_width);
+    int32_t* ht = reinterpret_cast<int32_t*>(ws + h_off);
+    img::coeff_kernel<<<(out_width + 127) / 128, 128, 0, s>>>(width, out_width, kh, ht);
     const size_t total = (size_t)height * out_width * 3;
     const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
-    img::resample_rows_kernel<<<blocks, 256, 0, s>>>(rgb, height, width, out_width,
-                                                      reinterpret_cast<int32_t*>(ws + h_off),
-                                                      ch.ksize, ws + mid_off);
+    img::resample_rows_kernel<<<blocks, 256, 0, s>>>(rgb, height, width, out_width, ht, kh,
+                                                      ws + mid_off);
     stage = ws + mid_off;
   }
   const int32_t* vt = nullptr;
   int kv = 0;
   if (out_height != height) {
-    const img::Coeffs cv = img::coefficients(height, out_height);
-    if (cudaMemcpyAsync(ws + v_off, cv.table.data(), cv.table.size() * sizeof(int32_t),
-                        cudaMemcpyHostToDevice, s) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
-    vt = reinterpret_cast<int32_t*>(ws + v_off);
-    kv = cv.ksize;
+    kv = img::kernel_size(height, out_height);
+    int32_t* t = reinterpret_cast<int32_t*>(ws + v_off);
+    img::coeff_kernel<<<(out_height + 127) / 128, 128, 0, s>>>(height, out_height, kv, t);
+    vt = t;
   }
   const size_t total = (size_t)out_height * out_width * 3;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);

@@ -97,18 +97,43 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
 
 struct Maps {
-  CUtensorMap q, k, v;   // k maps the KV cache (rotated keys), v the raw values
+  // q, v: the packed input rows; k: the KV caches (rotated keys) as
+  // {128, 2, capacity, prompts}
+  CUtensorMap q, k, v;
 };
 
 struct Params {
-  const float* rope_cos;  // [3, rope_rows, 128]
-  const float* rope_sin;
-  uint32_t rope_rows;
-  uint32_t tokens;
-  uint32_t n_split;       // split CTAs per KV head (the heaviest Q tiles)
-  uint32_t n_light;       // lightest Q tiles, paired two per CTA
-  __half* out;            // [T, 16, 128]
+  uint32_t n_split;       // single prompt: split CTAs per KV head (the heaviest Q tiles)
+  uint32_t n_light;       // single prompt: lightest Q tiles, paired two per CTA
+  uint64_t cache_stride;  // elements from one prompt's cache to the next
+  __half* k_cache;        // prompt b's [capacity, 2, 128] caches at + b * cache_stride
+  __half* v_cache;
+  __half* out;            // packed [rows, 16, 128]
 };
+
+// The prompts of one launch, packed back to back in q / k / v / out: one for
+// a single call, up to MAXB for a batched call (then every Q tile is a split
+// CTA, the tiles of each prompt heaviest first).  Passed by value as a grid
+// constant, so a launch copies nothing from the host.
+template <int MAXB>
+struct Prompts {
+  uint32_t count;
+  uint32_t tile_prefix[MAXB + 1];  // Q tiles of the prompts before b
+  uint32_t row0[MAXB + 1];         // first packed row of prompt b; row0[count] = rows
+  uint32_t rope_rows[MAXB];
+  const float* rope_cos[MAXB];     // [3, rope_rows[b], 128]
+  const float* rope_sin[MAXB];
+};
+
+// index b with v[b] <= x < v[b + 1] among v[0 .. n] (v ascending, v[0] <= x < v[n])
+__device__ __forceinline__ uint32_t find_segment(const uint32_t* v, uint32_t n, uint32_t x) {
+  uint32_t lo = 0, hi = n;
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (v[mid] <= x) lo = mid; else hi = mid;
+  }
+  return lo;
+}
 
 // ------------------------------------------------------------------------
 // 1. M-RoPE of the keys fused with the KV-cache write.  Thread = (token, KV
@@ -116,27 +141,28 @@ struct Params {
 // a 128-wide head takes table plane 0/1/2 for (d mod 64) in [0,16)/[16,40)/
 // [40,64); d < 64 becomes x[d] cos[d] - x[d+64] sin[d] and d+64 becomes
 // x[d+64] cos[d+64] + x[d] sin[d+64] (crates/pvlc-cpu-ref/src/lib.rs:645-668).
+template <int MAXB>
 __global__ void __launch_bounds__(256) kv_rope_kernel(const __half* __restrict__ k,
                                                       const __half* __restrict__ v,
-                                                      const float* __restrict__ rope_cos,
-                                                      const float* __restrict__ rope_sin,
-                                                      uint32_t rope_rows, uint32_t tokens,
-                                                      __half* __restrict__ k_cache,
-                                                      __half* __restrict__ v_cache) {
+                                                      const __grid_constant__ Prompts<MAXB> pr,
+                                                      const Params p) {
   // the attention launch may start its prologue (barriers, TMEM, Q load and
   // rotation) now; it waits for this kernel before reading the cache
   pdl_launch_dependents();
   const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t c = gid & 7, head = (gid >> 3) & 1, token = gid >> 4;
-  if (token >= tokens) return;
-  const size_t row = ((size_t)token * KVH + head) * HD;
-  const size_t tb = ((size_t)mrope_axis(8 * c) * rope_rows + token) * HD + 8 * c;
-  const float4* cs = reinterpret_cast<const float4*>(rope_cos + tb);
-  const float4* sn = reinterpret_cast<const float4*>(rope_sin + tb);
+  const uint32_t c = gid & 7, head = (gid >> 3) & 1, row = gid >> 4;   // packed row
+  if (row >= pr.row0[pr.count]) return;
+  const uint32_t pi = MAXB == 1 ? 0u : find_segment(pr.row0, pr.count, row);
+  const uint32_t token = row - pr.row0[pi];
+  const size_t in = ((size_t)row * KVH + head) * HD;
+  const size_t cr = (size_t)pi * p.cache_stride + ((size_t)token * KVH + head) * HD;
+  const size_t tb = ((size_t)mrope_axis(8 * c) * pr.rope_rows[pi] + token) * HD + 8 * c;
+  const float4* cs = reinterpret_cast<const float4*>(pr.rope_cos[pi] + tb);
+  const float4* sn = reinterpret_cast<const float4*>(pr.rope_sin[pi] + tb);
   const float4 cl0 = __ldg(cs), cl1 = __ldg(cs + 1), ch0 = __ldg(cs + 16), ch1 = __ldg(cs + 17);
   const float4 sl0 = __ldg(sn), sl1 = __ldg(sn + 1), sh0 = __ldg(sn + 16), sh1 = __ldg(sn + 17);
-  const uint4 a = *reinterpret_cast<const uint4*>(k + row + 8 * c);
-  const uint4 b = *reinterpret_cast<const uint4*>(k + row + 64 + 8 * c);
+  const uint4 a = *reinterpret_cast<const uint4*>(k + in + 8 * c);
+  const uint4 b = *reinterpret_cast<const uint4*>(k + in + 64 + 8 * c);
   const float cl[8] = {cl0.x, cl0.y, cl0.z, cl0.w, cl1.x, cl1.y, cl1.z, cl1.w};
   const float chh[8] = {ch0.x, ch0.y, ch0.z, ch0.w, ch1.x, ch1.y, ch1.z, ch1.w};
   const float sl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
@@ -150,12 +176,12 @@ __global__ void __launch_bounds__(256) kv_rope_kernel(const __half* __restrict__
     ra[e] = pack_half2(x.x * cl[2 * e] + (-y.x) * sl[2 * e], x.y * cl[2 * e + 1] + (-y.y) * sl[2 * e + 1]);
     rb[e] = pack_half2(y.x * chh[2 * e] + x.x * shh[2 * e], y.y * chh[2 * e + 1] + x.y * shh[2 * e + 1]);
   }
-  *reinterpret_cast<uint4*>(k_cache + row + 8 * c) = make_uint4(ra[0], ra[1], ra[2], ra[3]);
-  *reinterpret_cast<uint4*>(k_cache + row + 64 + 8 * c) = make_uint4(rb[0], rb[1], rb[2], rb[3]);
-  *reinterpret_cast<uint4*>(v_cache + row + 8 * c) =
-      *reinterpret_cast<const uint4*>(v + row + 8 * c);
-  *reinterpret_cast<uint4*>(v_cache + row + 64 + 8 * c) =
-      *reinterpret_cast<const uint4*>(v + row + 64 + 8 * c);
+  *reinterpret_cast<uint4*>(p.k_cache + cr + 8 * c) = make_uint4(ra[0], ra[1], ra[2], ra[3]);
+  *reinterpret_cast<uint4*>(p.k_cache + cr + 64 + 8 * c) = make_uint4(rb[0], rb[1], rb[2], rb[3]);
+  *reinterpret_cast<uint4*>(p.v_cache + cr + 8 * c) =
+      *reinterpret_cast<const uint4*>(v + in + 8 * c);
+  *reinterpret_cast<uint4*>(p.v_cache + cr + 64 + 8 * c) =
+      *reinterpret_cast<const uint4*>(v + in + 64 + 8 * c);
 }
 
 // ------------------------------------------------------------------------
@@ -171,15 +197,16 @@ struct RowTables {
   float4 v[4][8];
 };
 
-__device__ __forceinline__ void mrope_tables(RowTables& t, const Params& p, uint32_t token,
-                                             int c0) {
+__device__ __forceinline__ void mrope_tables(RowTables& t, const float* rope_cos,
+                                             const float* rope_sin, uint32_t rope_rows,
+                                             uint32_t token, int c0) {
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const int c = c0 + u;
     const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
-    const size_t tb = ((size_t)axis * p.rope_rows + token) * HD + 8 * c;
-    const float4* cs = reinterpret_cast<const float4*>(p.rope_cos + tb);
-    const float4* sn = reinterpret_cast<const float4*>(p.rope_sin + tb);
+    const size_t tb = ((size_t)axis * rope_rows + token) * HD + 8 * c;
+    const float4* cs = reinterpret_cast<const float4*>(rope_cos + tb);
+    const float4* sn = reinterpret_cast<const float4*>(rope_sin + tb);
     t.v[u][0] = __ldg(cs);
     t.v[u][1] = __ldg(cs + 1);
     t.v[u][2] = __ldg(cs + 16);
@@ -227,8 +254,10 @@ __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
   return r;
 }
 
+template <int MAXB>
 __global__ void __launch_bounds__(THREADS, 1)
-    prefill_attn_kernel(const __grid_constant__ Maps maps, const Params p) {
+    prefill_attn_kernel(const __grid_constant__ Maps maps, const Params p,
+                        const __grid_constant__ Prompts<MAXB> pr) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -245,19 +274,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t g = blockIdx.x;                      // KV head
-  const uint32_t n_qt = (p.tokens + TOK - 1) / TOK;
+  // prompt of this CTA and its Q tile rank within the prompt (heaviest first)
+  const uint32_t pi = MAXB == 1 ? 0u : find_segment(pr.tile_prefix, pr.count, blockIdx.y);
+  const uint32_t rank = blockIdx.y - pr.tile_prefix[pi];
+  const uint32_t row0 = pr.row0[pi];
+  const uint32_t tokens = pr.row0[pi + 1] - row0;
+  const uint32_t n_qt = (tokens + TOK - 1) / TOK;
   // Two kinds of CTA (both heaviest first):
   //  split: one Q tile; stream t takes its K tiles t, t + 2, ... and the two
   //         streams' (O, m, l) merge at the end (the long causal ranges);
   //  pair:  two light Q tiles, one per stream, sharing every K/V tile (the
   //         lightest tiles, paired so that the grid is one wave).
-  const bool pair = blockIdx.y >= p.n_split;
+  const bool pair = MAXB == 1 && blockIdx.y >= p.n_split;
   uint32_t tile0[STREAMS];   // first token of each stream's Q tile
   int nks[STREAMS];          // K tiles of each stream
   int ntiles;                // K/V tiles the CTA loads
   if (!pair) {
-    const uint32_t qt = n_qt - 1 - blockIdx.y;
-    const uint32_t last_tok = umin32(qt * TOK + TOK, p.tokens) - 1;
+    const uint32_t qt = n_qt - 1 - rank;
+    const uint32_t last_tok = umin32(qt * TOK + TOK, tokens) - 1;
     const int nk = static_cast<int>(last_tok / BN) + 1;    // K tiles 0 .. the diagonal
     tile0[0] = tile0[1] = qt * TOK;
     nks[0] = (nk + 1) / 2;
@@ -268,8 +302,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t qa = p.n_light - 1 - i, qb = i;     // stream 0 takes the heavier tile
     tile0[0] = qa * TOK;
     tile0[1] = qb * TOK;
-    nks[0] = static_cast<int>((umin32(qa * TOK + TOK, p.tokens) - 1) / BN) + 1;
-    nks[1] = static_cast<int>((umin32(qb * TOK + TOK, p.tokens) - 1) / BN) + 1;
+    nks[0] = static_cast<int>((umin32(qa * TOK + TOK, tokens) - 1) / BN) + 1;
+    nks[1] = static_cast<int>((umin32(qb * TOK + TOK, tokens) - 1) / BN) + 1;
     ntiles = nks[0];
   }
   // shared memory: Q buffer 0, then (split) 3 K/V stages or (pair) Q buffer 1
@@ -317,7 +351,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (t < nq)
           for (int b = 0; b < 2; ++b)
             tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + b * SZ_W, &maps.q, 64 * b, GROUP * g,
-                            tile0[t], q_full);
+                            row0 + tile0[t], q_full);
       // keys are read from the cache that kv_rope_kernel (the preceding launch) writes
       pdl_wait();
       int issued = 0;
@@ -327,8 +361,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t* st = smem + off_stage + s * STAGE_BYTES;
         mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
         for (int b = 0; b < 2; ++b) {
-          tc::tma_load_3d(st + ST_K + b * SZ_W, &maps.k, 64 * b, g, j * BN, &kv_full[s]);
-          tc::tma_load_3d(st + ST_V + b * SZ_W, &maps.v, 64 * b, g, j * BN, &kv_full[s]);
+          tc::tma_load_4d(st + ST_K + b * SZ_W, &maps.k, 64 * b, g, j * BN, pi, &kv_full[s]);
+          // values past the prompt (the next prompt's rows, or zero fill past
+          // the packed rows) meet P = 0
+          tc::tma_load_3d(st + ST_V + b * SZ_W, &maps.v, 64 * b, g, row0 + j * BN, &kv_full[s]);
         }
         issued = j + 1;
       }
@@ -445,12 +481,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     {
       RowTables rt;
       const int c0 = pair ? 0 : 4 * t;
-      if (token < p.tokens) mrope_tables(rt, p, token, c0);
+      const float* rcos = pr.rope_cos[pi];
+      const float* rsin = pr.rope_sin[pi];
+      const uint32_t rrows = pr.rope_rows[pi];
+      if (token < tokens) mrope_tables(rt, rcos, rsin, rrows, token, c0);
       ok = mbar_wait(q_full, 0);
-      if (ok && token < p.tokens) {
+      if (ok && token < tokens) {
         mrope_row(qb0, qb0 + SZ_W, i, rt, c0);
         if (pair) {
-          mrope_tables(rt, p, token, 4);
+          mrope_tables(rt, rcos, rsin, rrows, token, 4);
           mrope_row(qb0, qb0 + SZ_W, i, rt, 4);
         }
       }
@@ -560,9 +599,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!good) misc[1] = 1;
     const bool fin = __all_sync(0xffffffffu,
                                 good && (my_nk == 0 || mbar_wait(&o_done[t], (my_nk - 1) & 1)));
-    const bool store = token < p.tokens;
+    const bool store = token < tokens;
     const bool two = nks[1] > 0;                     // stream 1 had work
-    __half* orow = p.out + ((size_t)token * QH + GROUP * g + (i & 7)) * HD;
+    __half* orow = p.out + ((size_t)(row0 + token) * QH + GROUP * g + (i & 7)) * HD;
     if (pair) {
       // epilogue of a paired tile: this stream's O / l -> all 128 columns
       if (fin) {
@@ -687,6 +726,66 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t rows, uint32_t heads,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The caches of `prompts` prompts, prompt b's [capacity, 2, 128] fp16 at
+// base + b * prompt_stride elements, as a 4-D tensor {128, 2, capacity,
+// prompts}; box {64 dims, 1 head, 128 keys, 1 prompt}, 128B swizzle.
+bool make_cache_map(CUtensorMap* m, const void* base, uint32_t capacity, uint32_t prompts,
+                    uint64_t prompt_stride) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {HD, KVH, capacity, prompts};
+  const cuuint64_t strides[3] = {HD * 2, (cuuint64_t)KVH * HD * 2, prompt_stride * 2};
+  const cuuint32_t box[4] = {64, 1, BN, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// kv_rope_kernel then prefill_attn_kernel (programmatic dependent launch) for
+// the prompts of `pr`; grid_y CTAs per KV head.
+template <int MAXB>
+int launch(const void* q, const void* k, const void* v, uint32_t rows, const Prompts<MAXB>& pr,
+           Params p, uint32_t capacity, uint32_t grid_y, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(prefill_attn_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             SMEM_BYTES) != cudaSuccess)
+      return PVLC_CUDA_ERROR;
+    attr_set[dev] = true;
+  }
+  if (grid_y == 0 || grid_y > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
+  Maps maps;
+  // keys come from the caches (rotated by kv_rope_kernel): rows past a
+  // prompt are masked, rows past the capacity are TMA zero fill; values come
+  // from the packed input rows
+  if (!make_map(&maps.q, q, rows, QH, GROUP, TOK) ||
+      !make_cache_map(&maps.k, p.k_cache, capacity, pr.count, p.cache_stride) ||
+      !make_map(&maps.v, v, rows, KVH, 1, BN))
+    return PVLC_CUDA_ERROR;
+  const uint64_t rope_threads = (uint64_t)rows * KVH * 8;
+  kv_rope_kernel<MAXB><<<(unsigned)((rope_threads + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __half*>(k), reinterpret_cast<const __half*>(v), pr, p);
+  if (cudaPeekAtLastError() != cudaSuccess) return PVLC_CUDA_ERROR;
+  // programmatic dependent launch: the attention CTAs' prologue overlaps
+  // kv_rope_kernel; only their cache reads wait for it (pdl_wait)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(KVH, grid_y);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel<MAXB>, maps, p, pr) != cudaSuccess)
+    return PVLC_CUDA_ERROR;
+  return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
+}
+
 }  // namespace ptc
 
 int prefill_query_tile() { return ptc::QT * ptc::TOK; }
@@ -715,54 +814,53 @@ void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_l
 int prefill_block_threads() { return ptc::THREADS; }
 
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(ptc::prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ptc::SMEM_BYTES) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
-    attr_set[dev] = true;
-  }
-  ptc::Maps maps;
-  // keys come from the cache (rotated by kv_rope_kernel); only rows < tokens
-  // are read as valid keys, rows past the cache capacity are TMA zero-fill
-  if (!ptc::make_map(&maps.q, a.q, a.tokens, ptc::QH, ptc::GROUP, ptc::TOK) ||
-      !ptc::make_map(&maps.k, a.k_cache, a.capacity, ptc::KVH, 1, ptc::BN) ||
-      !ptc::make_map(&maps.v, a.v, a.tokens, ptc::KVH, 1, ptc::BN))
-    return PVLC_CUDA_ERROR;
-  const uint32_t n_qt = (a.tokens + ptc::TOK - 1) / ptc::TOK;
-  if (n_qt > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
-  const uint32_t rope_threads = a.tokens * ptc::KVH * 8;
-  ptc::kv_rope_kernel<<<(rope_threads + 255) / 256, 256, 0, stream>>>(
-      reinterpret_cast<const __half*>(a.k), reinterpret_cast<const __half*>(a.v), a.rope_cos,
-      a.rope_sin, a.rope_rows, a.tokens, reinterpret_cast<__half*>(a.k_cache),
-      reinterpret_cast<__half*>(a.v_cache));
-  if (cudaPeekAtLastError() != cudaSuccess) return PVLC_CUDA_ERROR;
-  ptc::Params p;
-  p.rope_cos = a.rope_cos;
-  p.rope_sin = a.rope_sin;
-  p.rope_rows = a.rope_rows;
-  p.tokens = a.tokens;
+  ptc::Prompts<1> pr{};
+  pr.count = 1;
+  pr.row0[0] = 0;
+  pr.row0[1] = a.tokens;
+  pr.tile_prefix[0] = 0;
+  pr.tile_prefix[1] = (a.tokens + ptc::TOK - 1) / ptc::TOK;
+  pr.rope_rows[0] = a.rope_rows;
+  pr.rope_cos[0] = a.rope_cos;
+  pr.rope_sin[0] = a.rope_sin;
+  ptc::Params p{};
+  p.cache_stride = (uint64_t)a.capacity * ptc::KVH * ptc::HD;
+  p.k_cache = reinterpret_cast<__half*>(a.k_cache);
+  p.v_cache = reinterpret_cast<__half*>(a.v_cache);
   p.out = reinterpret_cast<__half*>(a.out);
   // one wave: pair the lightest Q tiles so that the CTAs fit the SMs
   const int sms = device_sm_count();
   if (sms <= 0) return PVLC_CUDA_ERROR;
   prefill_schedule(a.tokens, sms, &p.n_split, &p.n_light);
-  // programmatic dependent launch: the attention CTAs' prologue overlaps
-  // kv_rope_kernel; only their cache reads wait for it (pdl_wait)
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ptc::KVH, p.n_split + p.n_light / 2);
-  cfg.blockDim = dim3(ptc::THREADS);
-  cfg.dynamicSmemBytes = ptc::SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, ptc::prefill_attn_kernel, maps, p) != cudaSuccess) return PVLC_CUDA_ERROR;
-  return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
+  return ptc::launch<1>(a.q, a.k, a.v, a.tokens, pr, p, a.capacity, p.n_split + p.n_light / 2,
+                        stream);
+}
+
+int prefill_batch_launch(const PrefillBatchArgs& a, cudaStream_t stream) {
+  static_assert(PVLC_PREFILL_MAX_PROMPTS <= 1024, "prompt table size");
+  ptc::Prompts<PVLC_PREFILL_MAX_PROMPTS> pr{};
+  pr.count = a.prompts;
+  uint32_t tiles = 0;
+  for (uint32_t b = 0; b < a.prompts; ++b) {
+    const uint32_t t = a.offsets[b + 1] - a.offsets[b];
+    pr.row0[b] = a.offsets[b];
+    pr.tile_prefix[b] = tiles;
+    tiles += (t + ptc::TOK - 1) / ptc::TOK;
+    pr.rope_rows[b] = a.rope_rows[b];
+    pr.rope_cos[b] = a.rope_cos[b];
+    pr.rope_sin[b] = a.rope_sin[b];
+  }
+  pr.row0[a.prompts] = a.offsets[a.prompts];
+  pr.tile_prefix[a.prompts] = tiles;
+  ptc::Params p{};
+  p.n_split = tiles;   // every Q tile a split CTA
+  p.n_light = 0;
+  p.cache_stride = a.cache_stride;
+  p.k_cache = reinterpret_cast<__half*>(a.k_cache);
+  p.v_cache = reinterpret_cast<__half*>(a.v_cache);
+  p.out = reinterpret_cast<__half*>(a.out);
+  return ptc::launch<PVLC_PREFILL_MAX_PROMPTS>(a.q, a.k, a.v, a.offsets[a.prompts], pr, p,
+                                               a.capacity, tiles, stream);
 }
 
 }  // namespace pvlc

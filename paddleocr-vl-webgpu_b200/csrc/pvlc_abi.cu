@@ -294,6 +294,40 @@ int pvlc_attn_decoder_prefill(const pvlc_half* q, const pvlc_half* k, const pvlc
   return prefill_launch(a, static_cast<cudaStream_t>(stream));
 }
 
+int pvlc_attn_decoder_prefill_batch(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
+                                    const uint32_t* offsets, uint32_t prompts,
+                                    const float* const* rope_cos, const float* const* rope_sin,
+                                    const uint32_t* rope_rows, pvlc_half* k_cache,
+                                    pvlc_half* v_cache, uint64_t cache_stride, uint32_t capacity,
+                                    pvlc_half* out, void* stream) {
+  if (prompts == 0) return PVLC_ZERO_DIMENSION;
+  if (prompts > PVLC_PREFILL_MAX_PROMPTS) return PVLC_INVALID_DECODER_GEOMETRY;
+  if (!offsets || !rope_cos || !rope_sin || !rope_rows) return PVLC_NULL_POINTER;
+  if (offsets[0] != 0) return PVLC_INVALID_SEQUENCE_BOUNDARIES;
+  uint64_t tiles = 0;
+  for (uint32_t b = 0; b < prompts; ++b) {
+    if (offsets[b + 1] <= offsets[b]) return PVLC_INVALID_SEQUENCE_BOUNDARIES;
+    const uint32_t t = offsets[b + 1] - offsets[b];
+    const int st = check_prefill(t, capacity, rope_rows[b]);
+    if (st) return st;
+    tiles += (t + 15) / 16;
+  }
+  if (tiles > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
+  if ((uint64_t)offsets[prompts] * 16 * 128 * 2 > (1ull << 40)) return PVLC_ARITHMETIC_OVERFLOW;
+  if (cache_stride < (uint64_t)capacity * 256 || cache_stride % 8) return PVLC_LENGTH_MISMATCH;
+  if (!q || !k || !v || !k_cache || !v_cache || !out) return PVLC_NULL_POINTER;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_cache) ||
+      !aligned16(v_cache) || !aligned16(out))
+    return PVLC_MISALIGNED_POINTER;
+  for (uint32_t b = 0; b < prompts; ++b) {
+    if (!rope_cos[b] || !rope_sin[b]) return PVLC_NULL_POINTER;
+    if (!aligned16(rope_cos[b]) || !aligned16(rope_sin[b])) return PVLC_MISALIGNED_POINTER;
+  }
+  PrefillBatchArgs a{q,        k,       v,       offsets, prompts,      rope_cos, rope_sin,
+                     rope_rows, k_cache, v_cache, cache_stride, capacity, out};
+  return prefill_batch_launch(a, static_cast<cudaStream_t>(stream));
+}
+
 // ------------------------------------------------------------------ decode
 int pvlc_plan_decoder_kv_session(uint32_t qh, uint32_t kvh, uint32_t hd, uint32_t prefix,
                                  uint32_t capacity, pvlc_plan* plan) {
@@ -343,14 +377,19 @@ int pvlc_attn_decode_workspace_init(void* workspace, size_t bytes, void* stream)
   return cuda_status(cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)));
 }
 
-int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half* v_new,
-                     const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
-                     const uint32_t* rope_row, pvlc_half* const* k_cache,
-                     pvlc_half* const* v_cache, const uint32_t* cache_tokens,
-                     uint32_t capacity, uint32_t max_cache_tokens, uint32_t batch,
-                     void* workspace, size_t workspace_bytes, pvlc_half* out, void* stream) {
+int pvlc_attn_decode_strided(const pvlc_half* q, uint32_t q_row_stride, const pvlc_half* k_new,
+                             const pvlc_half* v_new, uint32_t kv_row_stride,
+                             const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                             const uint32_t* rope_row, pvlc_half* const* k_cache,
+                             pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                             uint32_t capacity, uint32_t max_cache_tokens, uint32_t batch,
+                             void* workspace, size_t workspace_bytes, pvlc_half* out,
+                             void* stream) {
   const int st = check_decode(batch, capacity, max_cache_tokens, rope_rows);
   if (st) return st;
+  if (q_row_stride < 16u * 128u || kv_row_stride < 2u * 128u || q_row_stride % 8 ||
+      kv_row_stride % 8)
+    return PVLC_LENGTH_MISMATCH;
   if (!q || !k_new || !v_new || !rope_cos || !rope_sin || !k_cache || !v_cache ||
       !cache_tokens || !workspace || !out)
     return PVLC_NULL_POINTER;
@@ -360,10 +399,22 @@ int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half
   const int sms = device_sm_count();
   if (sms <= 0) return PVLC_CUDA_ERROR;
   if (workspace_bytes < decode_workspace_bytes(batch, sms)) return PVLC_WORKSPACE_TOO_SMALL;
-  DecodeArgs a{q,       k_new,    v_new,           rope_cos, rope_sin, rope_rows,
-               rope_row, k_cache, v_cache,         cache_tokens, capacity,
-               max_cache_tokens, batch, workspace, out, sms};
+  DecodeArgs a{q,       k_new,    v_new,           rope_cos,     rope_sin,  rope_rows,
+               rope_row, k_cache, v_cache,         cache_tokens, capacity,  max_cache_tokens,
+               batch,   workspace, out,            sms,          q_row_stride, kv_row_stride};
   return decode_launch(a, static_cast<cudaStream_t>(stream));
+}
+
+int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half* v_new,
+                     const float* rope_cos, const float* rope_sin, uint32_t rope_rows,
+                     const uint32_t* rope_row, pvlc_half* const* k_cache,
+                     pvlc_half* const* v_cache, const uint32_t* cache_tokens,
+                     uint32_t capacity, uint32_t max_cache_tokens, uint32_t batch,
+                     void* workspace, size_t workspace_bytes, pvlc_half* out, void* stream) {
+  return pvlc_attn_decode_strided(q, 16u * 128u, k_new, v_new, 2u * 128u, rope_cos, rope_sin,
+                                  rope_rows, rope_row, k_cache, v_cache, cache_tokens, capacity,
+                                  max_cache_tokens, batch, workspace, workspace_bytes, out,
+                                  stream);
 }
 
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream) {

@@ -27,6 +27,8 @@ struct DecodeArgs {
   void* workspace;
   pvlc_half* out;
   int num_ctas;
+  uint32_t q_stride;    // elements between consecutive sequences' q rows
+  uint32_t kv_stride;   // elements between consecutive sequences' k_new / v_new rows
 };
 size_t decode_workspace_bytes(uint32_t batch, int num_sms);
 int decode_block_threads();
@@ -64,6 +66,22 @@ struct PrefillArgs {
   pvlc_half* v_cache;
   pvlc_half* out;
 };
+struct PrefillBatchArgs {
+  const pvlc_half* q;          // packed [rows, 16, 128]
+  const pvlc_half* k;          // packed [rows, 2, 128]
+  const pvlc_half* v;
+  const uint32_t* offsets;     // host [prompts + 1]
+  uint32_t prompts;
+  const float* const* rope_cos;  // host [prompts] device pointers
+  const float* const* rope_sin;
+  const uint32_t* rope_rows;     // host [prompts]
+  pvlc_half* k_cache;            // prompt b's cache at + b * cache_stride elements
+  pvlc_half* v_cache;
+  uint64_t cache_stride;
+  uint32_t capacity;
+  pvlc_half* out;                // packed [rows, 16, 128]
+};
+int prefill_batch_launch(const PrefillBatchArgs& a, cudaStream_t stream);
 int prefill_query_tile();
 void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_light);
 int prefill_block_threads();

@@ -71,10 +71,15 @@ _SIGNATURES = {
                                                   _P, ctypes.c_size_t, _P, _P]),
     "pvlc_attn_decoder_prefill": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _P,
                                                  _P, _P]),
+    "pvlc_attn_decoder_prefill_batch": (ctypes.c_int, [_P, _P, _P, _P, _U32, _P, _P, _P, _P, _P,
+                                                       ctypes.c_uint64, _U32, _P, _P]),
     "pvlc_attn_decode_workspace_bytes": (ctypes.c_size_t, [_U32]),
     "pvlc_attn_decode_workspace_init": (ctypes.c_int, [_P, ctypes.c_size_t, _P]),
     "pvlc_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32, _U32,
                                         _U32, _P, ctypes.c_size_t, _P, _P]),
+    "pvlc_attn_decode_strided": (ctypes.c_int, [_P, _U32, _P, _P, _U32, _P, _P, _U32, _P, _P,
+                                                _P, _P, _U32, _U32, _U32, _P, ctypes.c_size_t,
+                                                _P, _P]),
     "pvlc_attn_decode_errors": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "pvlc_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32,
                                                 _U32, _U32, _P, _P]),

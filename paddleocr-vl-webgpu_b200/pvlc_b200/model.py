@@ -174,6 +174,7 @@ class OcrEngine:
             lw = dw[1 + 9 * l: 1 + 9 * (l + 1)]
             self.dlayers.append(dict(
                 n1=f32(lw[0]), q=lw[1], k=lw[2], v=lw[3], o=lw[4], n2=f32(lw[5]),
+                qkv=torch.cat([lw[1], lw[2], lw[3]], 0).contiguous(),
                 gate_up=torch.cat([lw[6], lw[7]], 0).contiguous(), down=lw[8]))
         self.final_norm = f32(dw[1 + 9 * c.decoder_layers])
         self.lm_head = dw[2 + 9 * c.decoder_layers]
@@ -275,7 +276,7 @@ class OcrEngine:
                                       self.vision_batch_tokens):
                 n += patches_list[j].shape[0]
                 j += 1
-            p = torch.cat(patches_list[i:j], 0) if j - i > 1 else patches_list[i]
+            p = _join_rows(patches_list[i:j])
             proj = self.project(self.vision_features(p, grids[i:j]), grids[i:j])
             m2 = self.cfg.merge * self.cfg.merge
             outs.extend(torch.split(proj, [g[0] * g[1] * g[2] // m2 for g in grids[i:j]]))
@@ -313,27 +314,41 @@ class OcrEngine:
 
         Each page is copied to the device (pinned staging), resized and cut into patches
         by the library's image kernel (smart_resize chooses the size), then generate()
-        runs the model.  Returns generate()'s dict."""
+        runs the model.  All pages share one device buffer and all patches another, in
+        page order, so the call makes two allocations whatever the page count and the
+        encoder reads each vision batch's patches in place.  Returns generate()'s dict."""
         from . import preprocess
         cfgp = preprocess_config or preprocess.MODEL_CONFIG
-        patches, grids = [], []
-        ws = None
+        ps = cfgp.patch_size
         ev = None
         if timings is not None:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
             ev[0].record()
+        hosts, sizes = [], []
         for im in images:
             t = im if isinstance(im, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(im))
+            if t.dim() != 3 or t.shape[2] != 3 or t.dtype != torch.uint8:
+                raise TypeError("pages must be [H, W, 3] uint8")
             if not t.is_pinned():
                 t = t.pin_memory()
-            d = t.to(self.device, non_blocking=True)
-            h, w = preprocess.smart_resize(int(t.shape[0]), int(t.shape[1]), cfgp)
-            need = int(abi.lib().pvlc_image_patches_workspace_bytes(int(t.shape[0]),
-                                                                    int(t.shape[1]), h, w))
-            if ws is None or ws.numel() < need:
-                ws = torch.empty(need, dtype=torch.uint8, device=self.device)
-            patches.append(ops.image_patches(d, h, w, cfgp.patch_size, workspace=ws))
-            grids.append((1, h // cfgp.patch_size, w // cfgp.patch_size))
+            H, W = int(t.shape[0]), int(t.shape[1])
+            hosts.append(t)
+            sizes.append((H, W) + tuple(preprocess.smart_resize(H, W, cfgp)))
+        nbytes = [H * W * 3 for H, W, _, _ in sizes]
+        npatch = [(h // ps) * (w // ps) for _, _, h, w in sizes]
+        rgb = torch.empty(sum(nbytes), dtype=torch.uint8, device=self.device)
+        allp = torch.empty((sum(npatch), 3 * ps * ps), dtype=torch.float32, device=self.device)
+        ws = torch.empty(max(int(abi.lib().pvlc_image_patches_workspace_bytes(*sz))
+                             for sz in sizes), dtype=torch.uint8, device=self.device)
+        patches, grids = [], []
+        o = r = 0
+        for t, (H, W, h, w), nb, n in zip(hosts, sizes, nbytes, npatch):
+            d = rgb[o:o + nb].view(H, W, 3)
+            d.copy_(t, non_blocking=True)
+            patches.append(ops.image_patches(d, h, w, ps, out=allp[r:r + n], workspace=ws))
+            grids.append((1, h // ps, w // ps))
+            o += nb
+            r += n
         if ev:
             ev[1].record()
         res = self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings)
@@ -450,6 +465,23 @@ class OcrEngine:
         return out
 
 
+def _join_rows(ts):
+    """torch.cat(ts, 0) of [n_i, C] tensors -- as a view, without a copy, when they are
+    consecutive row blocks of one buffer (the layout recognize() gives the pages)."""
+    first = ts[0]
+    if len(ts) == 1:
+        return first
+    C = first.shape[1]
+    expect = first.storage_offset()
+    for t in ts:
+        if (not t.is_contiguous() or t.dim() != 2 or t.shape[1] != C or t.dtype != first.dtype
+                or t.untyped_storage().data_ptr() != first.untyped_storage().data_ptr()
+                or t.storage_offset() != expect):
+            return torch.cat(ts, 0)
+        expect += t.numel()
+    return first.as_strided((sum(t.shape[0] for t in ts), C), (C, 1), first.storage_offset())
+
+
 def _upload(arr, dev):
     """Host array -> device tensor through pinned memory, without waiting for the device."""
     return torch.from_numpy(np.ascontiguousarray(arr)).pin_memory().to(dev, non_blocking=True)
@@ -480,9 +512,9 @@ class _DecodeGraph:
         if pos.min() < 0:
             raise positions.PositionError("decode position is negative")
         self.tok = first_tokens.clone().to(torch.int64)
-        rows_i32 = _upload(np.concatenate([pl, pos]).astype(np.int32), dev)
-        self.ct = rows_i32[:B]                  # rows before the append
-        self.rope_row = rows_i32[B:]            # decode position ct + delta
+        self.rows = _upload(np.concatenate([pl, pos]).astype(np.int32), dev)
+        self.ct = self.rows[:B]                 # rows before the append
+        self.rope_row = self.rows[B:]           # decode position ct + delta
         self.ct_max = int(pl.max())             # host copy of ct.max() (all rows step together)
         rows = int(pos.max()) + cap + 1
         rc, rs = positions.linear_rope_tables(rows, c.decoder_theta, c.head_dim)
@@ -494,10 +526,14 @@ class _DecodeGraph:
         self.kp = [ptrs[l] for l in range(Lyr)]
         self.vp = [ptrs[Lyr + l] for l in range(Lyr)]
         self.ws = [ops.DecodeWorkspace(B, dev) for _ in range(Lyr)]
-        self.q = torch.empty((B, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
-        self.k = torch.empty((B, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
-        self.v = torch.empty_like(self.k)
-        self.ctx = torch.empty_like(self.q)
+        # one projection GEMM per layer: [B, 2048 | 256 | 256]; decode reads the three
+        # column blocks as row-strided views
+        QW, KW = c.query_heads * c.head_dim, c.kv_heads * c.head_dim
+        self.qkv = torch.empty((B, QW + 2 * KW), dtype=torch.float16, device=dev)
+        self.q = self.qkv[:, :QW].view(B, c.query_heads, c.head_dim)
+        self.k = self.qkv[:, QW:QW + KW].view(B, c.kv_heads, c.head_dim)
+        self.v = self.qkv[:, QW + KW:].view(B, c.kv_heads, c.head_dim)
+        self.ctx = torch.empty((B, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
         self.graph = None
         self.logits = None
 
@@ -508,20 +544,17 @@ class _DecodeGraph:
         pending = None
         for l, L in enumerate(eng.dlayers):
             n1 = ops.add_norm(h32, L["n1"], c.rms_eps, delta=pending)
-            torch.mm(n1, L["q"].t(), out=self.q.view(B, -1))
-            torch.mm(n1, L["k"].t(), out=self.k.view(B, -1))
-            torch.mm(n1, L["v"].t(), out=self.v.view(B, -1))
+            torch.mm(n1, L["qkv"].t(), out=self.qkv)
             ops.decode(self.q, self.k, self.v, self.rcos, self.rsin, self.kp[l], self.vp[l],
                        self.ct, self.cap, self.cap - 1, self.ws[l], rope_row=self.rope_row,
                        out=self.ctx)
             pending = eng._layer_mlp(L, h32, F.linear(self.ctx.view(B, -1), L["o"]))
         self.logits = eng._logits(ops.add_norm(h32, eng.final_norm, c.rms_eps, delta=pending))
         self.tok.copy_(torch.argmax(self.logits, dim=-1))
-        self.ct += 1
-        self.rope_row += 1
+        self.rows += 1                          # ct and rope_row advance together
 
     def _capture(self):
-        saved = (self.tok.clone(), self.ct.clone(), self.rope_row.clone())
+        saved = (self.tok.clone(), self.rows.clone())
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -529,8 +562,7 @@ class _DecodeGraph:
         torch.cuda.current_stream().wait_stream(s)
         # the warm-up wrote cache rows at ct, which the first real step rewrites
         self.tok.copy_(saved[0])
-        self.ct.copy_(saved[1])
-        self.rope_row.copy_(saved[2])
+        self.rows.copy_(saved[1])
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._step()

@@ -99,14 +99,17 @@ def decoder_prefill(q, k, v, rope_cos, rope_sin, k_cache, v_cache, out=None):
     return out
 
 
+MAX_PREFILL_PROMPTS = 256       # PVLC_PREFILL_MAX_PROMPTS
+MAX_PREFILL_TILES = 65535       # 16-token Q tiles of one batched launch
+
+
 def decoder_prefill_packed(q, k, v, offsets, tables, k_caches, v_caches, out):
-    """decoder_prefill over B prompts packed back to back, one C-ABI call per prompt.
+    """decoder_prefill over B prompts packed back to back: pvlc_attn_decoder_prefill_batch,
+    one launch pair per group of at most 256 prompts (and 65535 Q tiles).
 
     q: [NT,16,128], k, v: [NT,2,128] fp16 with prompt b at rows offsets[b]:offsets[b+1]
     (host integers); tables: B (rope_cos, rope_sin) pairs as decoder_prefill takes them;
-    k_caches, v_caches: [B, capacity, 2, 128] fp16 (prompt b's cache at [b]); out like q.
-    The tensors are checked once; the per-prompt calls pass precomputed pointers, so the
-    host cost per prompt is the C call alone."""
+    k_caches, v_caches: [B, capacity, 2, 128] fp16 (prompt b's cache at [b]); out like q."""
     NT = q.shape[0]
     _need(q, torch.float16, (NT, QH, HD), "q")
     _need(k, torch.float16, (NT, KVH, HD), "k")
@@ -115,23 +118,35 @@ def decoder_prefill_packed(q, k, v, offsets, tables, k_caches, v_caches, out):
     B, cap = k_caches.shape[0], k_caches.shape[1]
     _need(k_caches, torch.float16, (B, cap, KVH, HD), "k_caches")
     _need(v_caches, torch.float16, (B, cap, KVH, HD), "v_caches")
-    if len(offsets) != B + 1 or len(tables) != B or offsets[0] != 0 or offsets[-1] != NT:
+    offs = [int(x) for x in offsets]
+    if len(offs) != B + 1 or len(tables) != B or offs[0] != 0 or offs[-1] != NT:
         raise ValueError("offsets / tables do not describe the packed prompts")
     for rc, rs in tables:
         _need(rc, torch.float32, (3, rc.shape[1], HD), "rope_cos")
         _need(rs, torch.float32, (3, rc.shape[1], HD), "rope_sin")
-    fn, st = abi.lib().pvlc_attn_decoder_prefill, _stream()
-    qp, kp, vp, op = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
-    kcp, vcp = k_caches.data_ptr(), v_caches.data_ptr()
-    cstride = cap * KVH * HD * 2
-    for b in range(B):
-        s, e = int(offsets[b]), int(offsets[b + 1])
-        rc, rs = tables[b]
-        status = fn(qp + s * QH * HD * 2, kp + s * KVH * HD * 2, vp + s * KVH * HD * 2,
-                    rc.data_ptr(), rs.data_ptr(), rc.shape[1], e - s, cap, kcp + b * cstride,
-                    vcp + b * cstride, op + s * QH * HD * 2, st)
-        if status:
-            abi.check(status, f"pvlc_attn_decoder_prefill (prompt {b})")
+    fn, st = abi.lib().pvlc_attn_decoder_prefill_batch, _stream()
+    cstride = cap * KVH * HD             # elements
+    b0 = 0
+    while b0 < B:
+        b1, tiles = b0, 0
+        while b1 < B and b1 - b0 < MAX_PREFILL_PROMPTS:
+            t = (offs[b1 + 1] - offs[b1] + 15) // 16
+            if b1 > b0 and tiles + t > MAX_PREFILL_TILES:
+                break
+            tiles += t
+            b1 += 1
+        n = b1 - b0
+        r0 = offs[b0]
+        offs_c = (ctypes.c_uint32 * (n + 1))(*[x - r0 for x in offs[b0:b1 + 1]])
+        cos_c = (ctypes.c_void_p * n)(*[tables[i][0].data_ptr() for i in range(b0, b1)])
+        sin_c = (ctypes.c_void_p * n)(*[tables[i][1].data_ptr() for i in range(b0, b1)])
+        rows_c = (ctypes.c_uint32 * n)(*[tables[i][0].shape[1] for i in range(b0, b1)])
+        status = fn(q.data_ptr() + r0 * QH * HD * 2, k.data_ptr() + r0 * KVH * HD * 2,
+                    v.data_ptr() + r0 * KVH * HD * 2, offs_c, n, cos_c, sin_c, rows_c,
+                    k_caches.data_ptr() + b0 * cstride * 2, v_caches.data_ptr() + b0 * cstride * 2,
+                    cstride, cap, out.data_ptr() + r0 * QH * HD * 2, st)
+        abi.check(status, f"pvlc_attn_decoder_prefill_batch (prompts {b0}..{b1 - 1})")
+        b0 = b1
     return out
 
 
@@ -153,20 +168,39 @@ class DecodeWorkspace:
         return int(flags.value)
 
 
+def _rows(t, dtype, shape, name):
+    """Check a [B, H, 128] tensor whose rows may sit at any 16-byte multiple apart (the
+    inner [H, 128] contiguous); returns the row stride in elements."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if t.stride(2) != 1 or t.stride(1) != shape[2] or (shape[0] > 1 and t.stride(0) % 8):
+        raise ValueError(f"{name} rows must be contiguous and 16-byte aligned")
+    return t.stride(0) if shape[0] > 1 else shape[1] * shape[2]
+
+
 def decode(q, k_new, v_new, rope_cos, rope_sin, k_cache_ptrs, v_cache_ptrs, cache_tokens,
            capacity: int, max_cache_tokens: int, workspace: DecodeWorkspace, rope_row=None,
            out=None):
     """Batched single-token decode with fused M-RoPE and KV append.
 
-    q: [B,16,128] fp16; k_new/v_new: [B,2,128] fp16; rope tables [3, R, 128] f32;
-    k_cache_ptrs/v_cache_ptrs: int64 CUDA tensors of B device pointers to
-    [capacity, 2, 128] fp16 caches; cache_tokens: int32 CUDA [B] rows before the append;
-    rope_row: optional int32 CUDA [B] (defaults to cache_tokens).  Returns [B,16,128] fp16.
+    q: [B,16,128] fp16; k_new/v_new: [B,2,128] fp16 -- each may be a row-strided view
+    (e.g. column slices of one [B, 2560] QKV projection; rows contiguous, k_new and v_new
+    with the same stride), passed through pvlc_attn_decode_strided; rope tables
+    [3, R, 128] f32; k_cache_ptrs/v_cache_ptrs: int64 CUDA tensors of B device pointers
+    to [capacity, 2, 128] fp16 caches; cache_tokens: int32 CUDA [B] rows before the
+    append; rope_row: optional int32 CUDA [B] (defaults to cache_tokens).
+    Returns [B,16,128] fp16.
     """
     B = q.shape[0]
-    _need(q, torch.float16, (B, QH, HD), "q")
-    _need(k_new, torch.float16, (B, KVH, HD), "k_new")
-    _need(v_new, torch.float16, (B, KVH, HD), "v_new")
+    qs = _rows(q, torch.float16, (B, QH, HD), "q")
+    ks = _rows(k_new, torch.float16, (B, KVH, HD), "k_new")
+    vs = _rows(v_new, torch.float16, (B, KVH, HD), "v_new")
+    if ks != vs:
+        raise ValueError("k_new and v_new must share one row stride")
     R = rope_cos.shape[1]
     _need(rope_cos, torch.float32, (3, R, HD), "rope_cos")
     _need(rope_sin, torch.float32, (3, R, HD), "rope_sin")
@@ -176,12 +210,14 @@ def decode(q, k_new, v_new, rope_cos, rope_sin, k_cache_ptrs, v_cache_ptrs, cach
     if rope_row is not None:
         _need(rope_row, torch.int32, (B,), "rope_row")
     if out is None:
-        out = torch.empty_like(q)
-    st = abi.lib().pvlc_attn_decode(
-        _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(rope_cos), _ptr(rope_sin), R, _ptr(rope_row),
-        _ptr(k_cache_ptrs), _ptr(v_cache_ptrs), _ptr(cache_tokens), int(capacity),
-        int(max_cache_tokens), B, _ptr(workspace.buffer), workspace.nbytes, _ptr(out), _stream())
-    abi.check(st, "pvlc_attn_decode")
+        out = torch.empty((B, QH, HD), dtype=torch.float16, device=q.device)
+    _need(out, torch.float16, (B, QH, HD), "out")
+    st = abi.lib().pvlc_attn_decode_strided(
+        _ptr(q), qs, _ptr(k_new), _ptr(v_new), ks, _ptr(rope_cos), _ptr(rope_sin), R,
+        _ptr(rope_row), _ptr(k_cache_ptrs), _ptr(v_cache_ptrs), _ptr(cache_tokens),
+        int(capacity), int(max_cache_tokens), B, _ptr(workspace.buffer), workspace.nbytes,
+        _ptr(out), _stream())
+    abi.check(st, "pvlc_attn_decode_strided")
     return out
 
 

@@ -116,3 +116,36 @@ def test_decode_plan_balances_tiles():
     bad = np.array([5, 9000], np.uint32)
     assert abi.lib().pvlc_plan_decode(bad.ctypes.data_as(ctypes.c_void_p), 2, 9000,
                                       ctypes.byref(plan)) == abi.CAPACITY_EXHAUSTED
+
+
+@pytest.mark.parametrize("q_stride,kv_stride", [(2047, 256), (2048, 255), (2052, 256),
+                                                (2560, 260)])
+def test_decode_strided_rejects_bad_strides_before_any_device_call(q_stride, kv_stride):
+    """Row strides below one row or not a 16-byte multiple return LengthMismatch from the
+    host-side checks (no device is touched: this runs without a GPU)."""
+    fake = ctypes.c_void_p(256)     # never dereferenced: the call returns first
+    st = abi.lib().pvlc_attn_decode_strided(
+        fake, q_stride, fake, fake, kv_stride, fake, fake, 64, None, fake, fake, fake,
+        64, 10, 4, fake, 1 << 20, fake, None)
+    assert st == abi.LENGTH_MISMATCH
+
+
+def test_batched_prefill_host_validation():
+    """Geometry errors of pvlc_attn_decoder_prefill_batch come from host checks, before
+    any device call (this runs without a GPU)."""
+    fake = ctypes.c_void_p(256)
+    tab = (ctypes.c_void_p * 2)(256, 512)
+    rows = (ctypes.c_uint32 * 2)(64, 64)
+    fn = abi.lib().pvlc_attn_decoder_prefill_batch
+
+    def call(offsets, prompts, stride=64 * 256, cap=64):
+        offs = (ctypes.c_uint32 * len(offsets))(*offsets)
+        return fn(fake, fake, fake, offs, prompts, tab, tab, rows, fake, fake, stride, cap,
+                  fake, None)
+
+    assert call([0, 10, 20], 0) == abi.ZERO_DIMENSION
+    assert call([0, 10, 20], 257) == abi.INVALID_DECODER_GEOMETRY
+    assert call([1, 10, 20], 2) == abi.INVALID_SEQUENCE_BOUNDARIES
+    assert call([0, 10, 10], 2) == abi.INVALID_SEQUENCE_BOUNDARIES     # empty prompt
+    assert call([0, 10, 90], 2) == abi.CAPACITY_EXHAUSTED               # 80 tokens > 64
+    assert call([0, 10, 20], 2, stride=64 * 256 - 8) == abi.LENGTH_MISMATCH

@@ -126,6 +126,37 @@ def test_decode_two_steps_reuse_workspace(cuda_lib):
     assert t["ws"].errors() == 0
 
 
+def test_decode_strided_qkv_matches_packed(cuda_lib):
+    """q / k_new / v_new as column blocks of one [B, 2560] projection (row stride 2560,
+    pvlc_attn_decode_strided) give exactly the packed-input results, outputs and the
+    appended cache rows alike."""
+    from pvlc_b200 import ops
+    lengths = [5, 300, 64, 1777]
+    cap = max(lengths) + 3
+    t, host = _setup(lengths, cap, seed=13, poison_tail=False)
+    B = len(lengths)
+    qkv = torch.empty((B, 2560), dtype=torch.float16, device="cuda")
+    qkv[:, :2048] = t["q"].view(B, -1)
+    qkv[:, 2048:2304] = t["kn"].view(B, -1)
+    qkv[:, 2304:] = t["vn"].view(B, -1)
+    q, k, v = qkv[:, :2048].view(B, QH, HD), qkv[:, 2048:2304].view(B, KVH, HD), \
+        qkv[:, 2304:].view(B, KVH, HD)
+    kc0, vc0 = t["kc"].clone(), t["vc"].clone()
+    ref = _run(t, cap, max(lengths))
+    kc_ref, vc_ref = t["kc"].clone(), t["vc"].clone()
+    t["kc"].copy_(kc0)
+    t["vc"].copy_(vc0)
+    got = ops.decode(q, k, v, t["cos"], t["sin"], t["kp"], t["vp"], t["ct"], cap, max(lengths),
+                     t["ws"])
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    assert torch.equal(t["kc"], kc_ref) and torch.equal(t["vc"], vc_ref)
+    assert t["ws"].errors() == 0
+    with pytest.raises(ValueError):      # k_new and v_new strides must agree
+        ops.decode(q, k, t["vn"], t["cos"], t["sin"], t["kp"], t["vp"], t["ct"], cap,
+                   max(lengths), t["ws"])
+
+
 def test_decode_large_batch_stream_k(cuda_lib):
     """64 sequences with lengths in [512, 8192] (config-4 shape), every sequence checked."""
     rng = np.random.default_rng(1)

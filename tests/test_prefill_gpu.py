@@ -117,3 +117,72 @@ def test_packed_prompts_match_single_calls(cuda_lib):
         assert torch.equal(kc[b], kc1) and torch.equal(vc[b], vc1)
     with pytest.raises(ValueError):
         ops.decoder_prefill_packed(q, k, v, offs[:-1], tables, kc, vc, out)
+
+
+def _packed_case(Ts, cap, seed):
+    from pvlc_b200 import positions
+    dev = torch.device("cuda")
+    offs = np.concatenate([[0], np.cumsum(Ts)]).astype(np.int64)
+    NT = int(offs[-1])
+    rng = np.random.default_rng(seed)
+    host = dict(q=rng.standard_normal((NT, QH, HD)).astype(np.float16),
+                k=rng.standard_normal((NT, KVH, HD)).astype(np.float16),
+                v=rng.standard_normal((NT, KVH, HD)).astype(np.float16))
+    tables, host_tables = [], []
+    for b, T in enumerate(Ts):
+        ids = list(range(3 + b, 3 + b + T))
+        pos, delta = positions.mrope_position_ids(ids, [])
+        c, s_ = positions.mrope_tables(pos, delta, cap)
+        host_tables.append((c, s_))
+        tables.append((torch.from_numpy(c).to(dev), torch.from_numpy(s_).to(dev)))
+    t = {n: torch.from_numpy(a).to(dev) for n, a in host.items()}
+    kc = torch.full((len(Ts), cap, KVH, HD), float("nan"), dtype=torch.float16, device=dev)
+    vc = torch.full_like(kc, float("nan"))
+    return offs, host, host_tables, t, tables, kc, vc
+
+
+def test_batched_prefill_long_and_short_prompts_vs_oracle(cuda_lib):
+    """One batched launch over a configs[2]-length prompt (1564 tokens: 98 Q tiles, every
+    one a split CTA here, paired in the single call), a short one and a 1190-token one:
+    each prompt's output within tolerance of the oracle, caches written only up to its
+    length (the NaN tails stay untouched)."""
+    from pvlc_b200 import ops
+    Ts = [1564, 40, 1190]
+    cap = 1600
+    offs, host, host_tables, t, tables, kc, vc = _packed_case(Ts, cap, seed=17)
+    out = torch.empty_like(t["q"])
+    ops.decoder_prefill_packed(t["q"], t["k"], t["v"], offs, tables, kc, vc, out)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    for b, T in enumerate(Ts):
+        s, e = int(offs[b]), int(offs[b + 1])
+        kc_o = np.zeros((cap, KVH, HD), np.float32)
+        vc_o = np.zeros((cap, KVH, HD), np.float32)
+        ref = O.decoder_prefill(host["q"][s:e].astype(np.float32), host["k"][s:e].astype(np.float32),
+                                host["v"][s:e].astype(np.float32), host_tables[b][0],
+                                host_tables[b][1], T, kc_o, vc_o)
+        err = np.abs(got[s:e] - ref).max()
+        assert err <= ATOL, f"prompt {b} (T={T}) max abs err {err}"
+        kcg = kc[b].float().cpu().numpy()
+        np.testing.assert_allclose(kcg[:T], kc_o[:T], atol=2e-3, rtol=1e-3)
+        assert np.isnan(kcg[T:]).all()
+
+
+def test_batched_prefill_many_prompts_in_groups(cuda_lib):
+    """300 short prompts (two launches of at most 256 prompts) equal the per-prompt calls
+    bit for bit (prompts this short split every Q tile in both paths)."""
+    from pvlc_b200 import ops
+    rng = np.random.default_rng(4)
+    Ts = [int(x) for x in rng.integers(1, 41, size=300)]
+    cap = 48
+    offs, host, host_tables, t, tables, kc, vc = _packed_case(Ts, cap, seed=5)
+    out = torch.empty_like(t["q"])
+    ops.decoder_prefill_packed(t["q"], t["k"], t["v"], offs, tables, kc, vc, out)
+    for b in (0, 1, 255, 256, 299):
+        s, e = int(offs[b]), int(offs[b + 1])
+        kc1 = torch.full((cap, KVH, HD), float("nan"), dtype=torch.float16, device="cuda")
+        vc1 = torch.full_like(kc1, float("nan"))
+        ref = ops.decoder_prefill(t["q"][s:e].contiguous(), t["k"][s:e].contiguous(),
+                                  t["v"][s:e].contiguous(), tables[b][0], tables[b][1], kc1, vc1)
+        assert torch.equal(out[s:e], ref), b
+        assert torch.equal(kc[b].nan_to_num(7.0), kc1.nan_to_num(7.0)), b
