@@ -459,8 +459,10 @@ int vision_encoder(const pvlc_oracle_model_dims& d, const uint16_t* const* vw,
     store(n2, f16);
     Vec f1;
     {
+      // the engine applies the GELU in the fc1 GEMM's epilogue, to the f32
+      // result: the one fp16 storage point is after it
       Vec w = widen(lw[12], I * H), b = widen(lw[13], I);
-      f1 = linear_v(n2, n, H, w.data(), b.data(), I, f16);
+      f1 = linear_v(n2, n, H, w.data(), b.data(), I, false);
     }
     for (auto& e : f1) e = gelu_tanh(e);
     store(f1, f16);

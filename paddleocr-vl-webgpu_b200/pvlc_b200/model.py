@@ -247,7 +247,8 @@ class OcrEngine:
             ops.vision_varlen_attention(q, k, v, cu, rcos, rsin, out=ctx, workspace=ws)
             o = F.linear(ctx.view(N, H), *L["o"])
             n2 = ops.add_norm(h32, L["ln2"][0], c.vision_eps, bias=L["ln2"][1], delta=o)
-            a = ops.gelu_(F.linear(n2, *L["fc1"]))
+            # fc1 + bias + GELU-tanh in one cuBLASLt GEMM (GELU epilogue on the f32 result)
+            a = torch._addmm_activation(L["fc1"][1], n2, L["fc1"][0].t(), use_gelu=True)
             pending = F.linear(a, *L["fc2"])
         return ops.add_norm(h32, self.post_ln[0], c.vision_eps, bias=self.post_ln[1],
                             delta=pending)
