@@ -267,9 +267,12 @@ class OcrEngine:
         a = ops.gelu_(F.linear(merged, *self.proj["l1"]), erf=True)
         return F.linear(a, *self.proj["l2"])
 
-    def encode_images(self, patches_list, grids):
+    def encode_images(self, patches_list, grids, prepare=None):
         """Vision + projector over many images, packed into sub-batches of at most
-        vision_batch_tokens patches.  Returns one [tokens_i, 1024] fp16 tensor per image."""
+        vision_batch_tokens patches.  Returns one [tokens_i, 1024] fp16 tensor per image.
+        prepare(i, j), when given, queues the work that fills patches_list[i:j] (page
+        uploads and the image kernel) just before their sub-batch, so the host's share of
+        it overlaps the device's encoding of the previous sub-batch."""
         outs, i = [], 0
         while i < len(grids):
             j, n = i, 0
@@ -277,6 +280,8 @@ class OcrEngine:
                                       self.vision_batch_tokens):
                 n += patches_list[j].shape[0]
                 j += 1
+            if prepare is not None:
+                prepare(i, j)
             p = _join_rows(patches_list[i:j])
             proj = self.project(self.vision_features(p, grids[i:j]), grids[i:j])
             m2 = self.cfg.merge * self.cfg.merge
@@ -317,14 +322,11 @@ class OcrEngine:
         by the library's image kernel (smart_resize chooses the size), then generate()
         runs the model.  All pages share one device buffer and all patches another, in
         page order, so the call makes two allocations whatever the page count and the
-        encoder reads each vision batch's patches in place.  Returns generate()'s dict."""
+        encoder reads each vision batch's patches in place; each vision batch's pages are
+        uploaded and cut just before that batch is encoded.  Returns generate()'s dict."""
         from . import preprocess
         cfgp = preprocess_config or preprocess.MODEL_CONFIG
         ps = cfgp.patch_size
-        ev = None
-        if timings is not None:
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-            ev[0].record()
         hosts, sizes = [], []
         for im in images:
             t = im if isinstance(im, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(im))
@@ -341,29 +343,31 @@ class OcrEngine:
         allp = torch.empty((sum(npatch), 3 * ps * ps), dtype=torch.float32, device=self.device)
         ws = torch.empty(max(int(abi.lib().pvlc_image_patches_workspace_bytes(*sz))
                              for sz in sizes), dtype=torch.uint8, device=self.device)
-        patches, grids = [], []
+        patches, grids, jobs = [], [], []
         o = r = 0
         for t, (H, W, h, w), nb, n in zip(hosts, sizes, nbytes, npatch):
-            d = rgb[o:o + nb].view(H, W, 3)
-            d.copy_(t, non_blocking=True)
-            patches.append(ops.image_patches(d, h, w, ps, out=allp[r:r + n], workspace=ws))
+            patches.append(allp[r:r + n])
             grids.append((1, h // ps, w // ps))
+            jobs.append((t, rgb[o:o + nb].view(H, W, 3), h, w))
             o += nb
             r += n
-        if ev:
-            ev[1].record()
-        res = self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings)
-        if ev:
-            timings.update(pages_ms=ev[0].elapsed_time(ev[1]))
-        return res
+
+        def prepare(i, j):
+            for (t, d, h, w), out in zip(jobs[i:j], patches[i:j]):
+                d.copy_(t, non_blocking=True)
+                ops.image_patches(d, h, w, ps, out=out, workspace=ws)
+
+        return self.generate(patches, grids, max_new_tokens, chunk=chunk, timings=timings,
+                             prepare=prepare)
 
     def generate(self, images_patches, grids, max_new_tokens: int, chunk: int = 16,
-                 record_logits: bool = False, timings: dict | None = None):
+                 record_logits: bool = False, timings: dict | None = None, prepare=None):
         """Greedy OCR of B requests (one image each, same prompt template).
 
         images_patches: list of [N_i, 588] device tensors; grids: list of (t, h, w).
         Returns dict(tokens=list of lists, stop=list of reasons, logits=optional list of
         [steps_i, vocab] f32 CPU tensors (the logits each token was chosen from)).
+        prepare: optional encode_images hook that fills the patches batch by batch.
 
         Nothing between the first encoder launch and the last decode chunk waits for the
         device except the reads of the first tokens and of each chunk's tokens: the
@@ -395,7 +399,7 @@ class OcrEngine:
         ids_t, img_idx, last = torch.split(plan, [NT, int(img_pos.size), B])
         if ev:
             ev[0].record()
-        img = self.encode_images(images_patches, grids)
+        img = self.encode_images(images_patches, grids, prepare)
         if ev:
             ev[1].record()
         QW = c.query_heads * c.head_dim
