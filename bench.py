@@ -320,7 +320,8 @@ def run_gpu(args, rank, world, local_rank, dist):
     return line
 
 
-def run_components(args, dev, tf_peak, peak_src, which=("vision", "prefill"), iters=20, warm=3):
+def run_components(args, dev, tf_peak, peak_src, which=("vision", "prefill", "prefill_batch"),
+                   iters=20, warm=3):
     import torch
 
     res = {}
@@ -344,6 +345,8 @@ def run_components(args, dev, tf_peak, peak_src, which=("vision", "prefill"), it
         res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src)
     if "prefill" in which:
         res["decoder_prefill"] = bench_prefill(dev, timeit, tf_peak, peak_src)
+    if "prefill_batch" in which:
+        res["decoder_prefill_batch"] = bench_prefill_batch(dev, timeit, tf_peak, peak_src)
     return res
 
 
@@ -420,6 +423,49 @@ def bench_prefill(dev, timeit, tf_peak, peak_src):
                          "peak_source": peak_src, "traffic": PREFILL_ATTN_TRAFFIC_BYTES,
                          "traffic_kernel": "pvlc::ptc::prefill_attn_kernel (ncu, one launch)"},
             "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
+
+
+def bench_prefill_batch(dev, timeit, tf_peak, peak_src):
+    """Decoder causal prefill of one layer over the configs[4] batch: 256 OCR prompts of
+    1238 tokens (1225 image tokens of a 980x980 page) packed back to back, one
+    pvlc_attn_decoder_prefill_batch launch pair -- the e2e engine's per-layer call."""
+    import numpy as np
+    import torch
+
+    from pvlc_b200 import ops, positions
+    from pvlc_b200 import model as M
+    B = 256
+    ids = M.ocr_prompt_ids(1225)
+    T = len(ids)
+    pos, delta = positions.mrope_position_ids(ids, [(1, 70, 70)])
+    cap = T + 16
+    pc, ps = positions.mrope_tables(pos, delta, cap)
+    tab = (torch.from_numpy(pc).to(dev), torch.from_numpy(ps).to(dev))
+    offs = np.arange(B + 1, dtype=np.int64) * T
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    # 0.8 GB of q per set: larger than L2, so no rotation of input sets is needed
+    q = torch.randn((B * T, 16, 128), generator=g, device=dev).half()
+    k = torch.randn((B * T, 2, 128), generator=g, device=dev).half()
+    v = torch.randn((B * T, 2, 128), generator=g, device=dev).half()
+    kc = torch.empty((B, cap, 2, 128), dtype=torch.float16, device=dev)
+    vc = torch.empty_like(kc)
+    out = torch.empty_like(q)
+    tables = [tab] * B
+
+    def pre():
+        ops.decoder_prefill_packed(q, k, v, offs, tables, kc, vc, out)
+
+    ms = timeit(pre)
+    flops = B * 4.0 * 128 * 16 * T * (T + 1) / 2
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": f"configs[4] decoder prefill, {B} prompts x {T} tokens packed, one "
+                        "launch pair per layer, Q16/KV2/D128, M-RoPE",
+            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                         "peak_source": peak_src},
+            "kernel": "pvlc::ptc::kv_rope_kernel<256> + pvlc::ptc::prefill_attn_kernel<256>"}
 
 
 def run_e2e(args, dev, rank, world, dist):
@@ -587,7 +633,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true", help="skip configs[4] e2e greedy OCR")
     ap.add_argument("--e2e-requests", type=int, default=256)
     ap.add_argument("--e2e-tokens", type=int, default=512)
-    ap.add_argument("--only", choices=["vision", "prefill", "e2e"], default=None,
+    ap.add_argument("--only", choices=["vision", "prefill", "prefill_batch", "e2e"], default=None,
                     help="time one prefill component alone (profiling runs); prints its line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
