@@ -146,10 +146,10 @@ int pvlc_attn_decoder_prefill(const pvlc_half* q, const pvlc_half* k, const pvlc
  *     multiple of 8).
  * Each prompt is held to pvlc_attn_decoder_prefill's checks, with the same
  * codes; 1 <= prompts <= PVLC_PREFILL_MAX_PROMPTS and at most 65535 Q tiles
- * of 16 tokens in all, else PVLC_INVALID_DECODER_GEOMETRY.  Results equal
- * pvlc_attn_decoder_prefill's per prompt within the fp16 output rounding
- * (bit-identical where the single call splits every Q tile, i.e. prompts of
- * at most 1184 tokens). */
+ * of 16 tokens in all, else PVLC_INVALID_DECODER_GEOMETRY.  Each CTA takes two
+ * adjacent 16-token Q tiles of one prompt, so the outputs equal
+ * pvlc_attn_decoder_prefill's per prompt within the fp16 output rounding (the
+ * key order of the online softmax differs); the caches are bit-identical. */
 #define PVLC_PREFILL_MAX_PROMPTS 256u
 int pvlc_attn_decoder_prefill_batch(const pvlc_half* q, const pvlc_half* k, const pvlc_half* v,
                                     const uint32_t* offsets, uint32_t prompts,

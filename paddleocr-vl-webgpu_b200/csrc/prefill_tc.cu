@@ -112,13 +112,13 @@ struct Params {
 };
 
 // The prompts of one launch, packed back to back in q / k / v / out: one for
-// a single call, up to MAXB for a batched call (then every Q tile is a split
-// CTA, the tiles of each prompt heaviest first).  Passed by value as a grid
-// constant, so a launch copies nothing from the host.
+// a single call, up to MAXB for a batched call (then each CTA takes two
+// adjacent Q tiles of one prompt, the prompt's heaviest first).  Passed by
+// value as a grid constant, so a launch copies nothing from the host.
 template <int MAXB>
 struct Prompts {
   uint32_t count;
-  uint32_t tile_prefix[MAXB + 1];  // Q tiles of the prompts before b
+  uint32_t cta_prefix[MAXB + 1];   // CTAs (per KV head) of the prompts before b
   uint32_t row0[MAXB + 1];         // first packed row of prompt b; row0[count] = rows
   uint32_t rope_rows[MAXB];
   const float* rope_cos[MAXB];     // [3, rope_rows[b], 128]
@@ -274,23 +274,38 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t g = blockIdx.x;                      // KV head
-  // prompt of this CTA and its Q tile rank within the prompt (heaviest first)
-  const uint32_t pi = MAXB == 1 ? 0u : find_segment(pr.tile_prefix, pr.count, blockIdx.y);
-  const uint32_t rank = blockIdx.y - pr.tile_prefix[pi];
+  // prompt of this CTA and its rank among the prompt's CTAs (heaviest first)
+  const uint32_t pi = MAXB == 1 ? 0u : find_segment(pr.cta_prefix, pr.count, blockIdx.y);
+  const uint32_t rank = blockIdx.y - pr.cta_prefix[pi];
   const uint32_t row0 = pr.row0[pi];
   const uint32_t tokens = pr.row0[pi + 1] - row0;
   const uint32_t n_qt = (tokens + TOK - 1) / TOK;
-  // Two kinds of CTA (both heaviest first):
+  // Two kinds of CTA:
   //  split: one Q tile; stream t takes its K tiles t, t + 2, ... and the two
   //         streams' (O, m, l) merge at the end (the long causal ranges);
-  //  pair:  two light Q tiles, one per stream, sharing every K/V tile (the
-  //         lightest tiles, paired so that the grid is one wave).
-  const bool pair = MAXB == 1 && blockIdx.y >= p.n_split;
+  //  pair:  two Q tiles, one per stream, sharing every K/V tile.
+  // Single prompt: the heaviest tiles split, the lightest paired two per CTA
+  // (light tile n_light - 1 - i with i) so that the grid is one wave.
+  // Batched: CTA r of a prompt pairs its adjacent tiles n_qt - 1 - 2r and
+  // n_qt - 2 - 2r (nearly equal K ranges, so both streams stay busy and the
+  // CTA's fixed costs cover two tiles of work); an odd prompt's last CTA
+  // takes tile 0 alone, split.
+  bool pair;
+  uint32_t qa, qb = 0;       // pair: stream 0 / stream 1 tile (qb's K tiles a prefix of qa's)
+  if (MAXB == 1) {
+    pair = blockIdx.y >= p.n_split;
+    qa = pair ? p.n_light - 1 - (blockIdx.y - p.n_split) : n_qt - 1 - rank;
+    qb = pair ? blockIdx.y - p.n_split : 0u;
+  } else {
+    qa = n_qt - 1 - 2 * rank;
+    pair = qa >= 1;
+    qb = pair ? qa - 1 : 0u;
+  }
   uint32_t tile0[STREAMS];   // first token of each stream's Q tile
   int nks[STREAMS];          // K tiles of each stream
   int ntiles;                // K/V tiles the CTA loads
   if (!pair) {
-    const uint32_t qt = n_qt - 1 - rank;
+    const uint32_t qt = qa;
     const uint32_t last_tok = umin32(qt * TOK + TOK, tokens) - 1;
     const int nk = static_cast<int>(last_tok / BN) + 1;    // K tiles 0 .. the diagonal
     tile0[0] = tile0[1] = qt * TOK;
@@ -298,8 +313,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     nks[1] = nk / 2;
     ntiles = nk;
   } else {
-    const uint32_t i = blockIdx.y - p.n_split;
-    const uint32_t qa = p.n_light - 1 - i, qb = i;     // stream 0 takes the heavier tile
     tile0[0] = qa * TOK;
     tile0[1] = qb * TOK;
     nks[0] = static_cast<int>((umin32(qa * TOK + TOK, tokens) - 1) / BN) + 1;
@@ -818,8 +831,7 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   pr.count = 1;
   pr.row0[0] = 0;
   pr.row0[1] = a.tokens;
-  pr.tile_prefix[0] = 0;
-  pr.tile_prefix[1] = (a.tokens + ptc::TOK - 1) / ptc::TOK;
+  pr.cta_prefix[0] = 0;
   pr.rope_rows[0] = a.rope_rows;
   pr.rope_cos[0] = a.rope_cos;
   pr.rope_sin[0] = a.rope_sin;
@@ -832,6 +844,7 @@ int prefill_launch(const PrefillArgs& a, cudaStream_t stream) {
   const int sms = device_sm_count();
   if (sms <= 0) return PVLC_CUDA_ERROR;
   prefill_schedule(a.tokens, sms, &p.n_split, &p.n_light);
+  pr.cta_prefix[1] = p.n_split + p.n_light / 2;
   return ptc::launch<1>(a.q, a.k, a.v, a.tokens, pr, p, a.capacity, p.n_split + p.n_light / 2,
                         stream);
 }
@@ -840,27 +853,25 @@ int prefill_batch_launch(const PrefillBatchArgs& a, cudaStream_t stream) {
   static_assert(PVLC_PREFILL_MAX_PROMPTS <= 1024, "prompt table size");
   ptc::Prompts<PVLC_PREFILL_MAX_PROMPTS> pr{};
   pr.count = a.prompts;
-  uint32_t tiles = 0;
+  uint32_t ctas = 0;
   for (uint32_t b = 0; b < a.prompts; ++b) {
     const uint32_t t = a.offsets[b + 1] - a.offsets[b];
     pr.row0[b] = a.offsets[b];
-    pr.tile_prefix[b] = tiles;
-    tiles += (t + ptc::TOK - 1) / ptc::TOK;
+    pr.cta_prefix[b] = ctas;
+    ctas += ((t + ptc::TOK - 1) / ptc::TOK + 1) / 2;   // adjacent Q tiles paired
     pr.rope_rows[b] = a.rope_rows[b];
     pr.rope_cos[b] = a.rope_cos[b];
     pr.rope_sin[b] = a.rope_sin[b];
   }
   pr.row0[a.prompts] = a.offsets[a.prompts];
-  pr.tile_prefix[a.prompts] = tiles;
+  pr.cta_prefix[a.prompts] = ctas;
   ptc::Params p{};
-  p.n_split = tiles;   // every Q tile a split CTA
-  p.n_light = 0;
   p.cache_stride = a.cache_stride;
   p.k_cache = reinterpret_cast<__half*>(a.k_cache);
   p.v_cache = reinterpret_cast<__half*>(a.v_cache);
   p.out = reinterpret_cast<__half*>(a.out);
   return ptc::launch<PVLC_PREFILL_MAX_PROMPTS>(a.q, a.k, a.v, a.offsets[a.prompts], pr, p,
-                                               a.capacity, tiles, stream);
+                                               a.capacity, ctas, stream);
 }
 
 }  // namespace pvlc

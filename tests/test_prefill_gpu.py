@@ -87,7 +87,9 @@ def test_long_prefill_schedules(cuda_lib, T):
 
 def test_packed_prompts_match_single_calls(cuda_lib):
     """ops.decoder_prefill_packed (the engine's path: prompts back to back, one cache
-    slab per prompt) gives exactly the per-prompt decoder_prefill results."""
+    slab per prompt, adjacent Q tiles paired in a CTA) gives the per-prompt
+    decoder_prefill results within the fp16 output tolerance and the same caches bit for
+    bit."""
     from pvlc_b200 import ops, positions
     dev = torch.device("cuda")
     prompts = [image_prompt(3, (4, 5), 6), image_prompt(20, (12, 10), 40), image_prompt(1, (2, 2), 1)]
@@ -113,7 +115,7 @@ def test_packed_prompts_match_single_calls(cuda_lib):
         vc1 = torch.zeros_like(kc1)
         ref = ops.decoder_prefill(q[s:e].contiguous(), k[s:e].contiguous(), v[s:e].contiguous(),
                                   tables[b][0], tables[b][1], kc1, vc1)
-        assert torch.equal(out[s:e], ref)
+        assert (out[s:e].float() - ref.float()).abs().max().item() <= ATOL
         assert torch.equal(kc[b], kc1) and torch.equal(vc[b], vc1)
     with pytest.raises(ValueError):
         ops.decoder_prefill_packed(q, k, v, offs[:-1], tables, kc, vc, out)
@@ -142,8 +144,8 @@ def _packed_case(Ts, cap, seed):
 
 
 def test_batched_prefill_long_and_short_prompts_vs_oracle(cuda_lib):
-    """One batched launch over a configs[2]-length prompt (1564 tokens: 98 Q tiles, every
-    one a split CTA here, paired in the single call), a short one and a 1190-token one:
+    """One batched launch over a configs[2]-length prompt (1564 tokens: 98 Q tiles, paired
+    adjacent here, heaviest split in the single call), a short one and a 1190-token one:
     each prompt's output within tolerance of the oracle, caches written only up to its
     length (the NaN tails stay untouched)."""
     from pvlc_b200 import ops
@@ -169,12 +171,12 @@ def test_batched_prefill_long_and_short_prompts_vs_oracle(cuda_lib):
 
 
 def test_batched_prefill_many_prompts_in_groups(cuda_lib):
-    """300 short prompts (two launches of at most 256 prompts) equal the per-prompt calls
-    bit for bit (prompts this short split every Q tile in both paths)."""
+    """300 short prompts (two launches of at most 256 prompts, odd and even Q-tile counts)
+    match the per-prompt calls: outputs within the fp16 tolerance, caches bit for bit."""
     from pvlc_b200 import ops
     rng = np.random.default_rng(4)
-    Ts = [int(x) for x in rng.integers(1, 41, size=300)]
-    cap = 48
+    Ts = [int(x) for x in rng.integers(1, 300, size=300)]
+    cap = 304
     offs, host, host_tables, t, tables, kc, vc = _packed_case(Ts, cap, seed=5)
     out = torch.empty_like(t["q"])
     ops.decoder_prefill_packed(t["q"], t["k"], t["v"], offs, tables, kc, vc, out)
@@ -184,5 +186,5 @@ def test_batched_prefill_many_prompts_in_groups(cuda_lib):
         vc1 = torch.full_like(kc1, float("nan"))
         ref = ops.decoder_prefill(t["q"][s:e].contiguous(), t["k"][s:e].contiguous(),
                                   t["v"][s:e].contiguous(), tables[b][0], tables[b][1], kc1, vc1)
-        assert torch.equal(out[s:e], ref), b
+        assert (out[s:e].float() - ref.float()).abs().max().item() <= ATOL, b
         assert torch.equal(kc[b].nan_to_num(7.0), kc1.nan_to_num(7.0)), b
