@@ -504,11 +504,18 @@ def run_e2e(args, dev, rank, world, dist):
     eng.recognize(pages[:16], 4)
     barrier()
     timings = {}
+    # clocks at a 20 ms period: the engine's host thread shares the interpreter lock
+    # with the sampler, so it samples less often than around the kernel-only regions
+    sampler = ClockSampler(torch.cuda.current_device(), period_s=0.02)
+    load0 = os.getloadavg()[0]
+    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     res = eng.recognize(pages, args.e2e_tokens, timings=timings)
     e1.record()
     barrier()
+    clocks = sampler.stop()
+    clocks["host_loadavg_1m"] = [round(load0, 2), round(os.getloadavg()[0], 2)]
     ms = e0.elapsed_time(e1)
     tokens = sum(len(t) for t in res["tokens"])
     eos = sum(1 for r in res["stop"] if r == "eos_token")
@@ -529,6 +536,7 @@ def run_e2e(args, dev, rank, world, dist):
            "rank0_breakdown_ms": {k: (round(v, 2) if isinstance(v, float) else v)
                                   for k, v in timings.items()},
            "h2d_bytes_per_request": 1024 * 1024 * 3,
+           "clocks": clocks,
            "path": "pvlc_b200.model.OcrEngine.recognize (host pages in, token ids out)"}
     if rank == 0 and not args.skip_cpu:
         out["cpu_baseline"] = cpu_e2e_baseline(cfg, weights)

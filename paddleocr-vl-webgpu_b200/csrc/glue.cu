@@ -8,11 +8,14 @@
 //
 //   add_norm:   h += delta (fp16, optional) in f32, then LayerNorm (weight +
 //               bias, two-pass mean / variance) or RMSNorm (weight) of the row
-//               in f32, written as fp16.  One CTA per row: the row is read
-//               once from HBM and re-read from L1 for the second and third
-//               passes.  (A warp per row holding the row in registers was
-//               slower: 296 vs 241 us for 78,400 x 1152, 106 registers leave
-//               too few rows in flight per SM.)
+//               in f32, written as fp16.  Widths 1024 and 1152 (the
+//               decoder and vision rows) with many rows: one warp per row,
+//               the row in registers (width-exact, 72-80 registers, 3 CTAs
+//               of 8 rows per SM).  Otherwise one CTA per row: the row is
+//               read once from HBM and re-read from L1 for the second and
+//               third passes.  (A warp per row sized for rows up to 2048
+//               wide needed 106 registers and was slower than the CTA
+//               kernel: 296 vs 241 us for 78,400 x 1152.)
 //   gelu_*:     in place on fp16, math in f32, 16-byte accesses.  The tanh form
 //               is evaluated as x / (1 + e^(-2u)), the same function as
 //               0.5 x (1 + tanh u) (tanh u = 1 - 2 / (1 + e^(2u))), with the
@@ -112,6 +115,105 @@ __global__ void __launch_bounds__(NORM_THREADS) add_norm_kernel(
     orow[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
                          *reinterpret_cast<const uint32_t*>(&hi));
   }
+}
+
+// One warp per row for the engine's two row widths, 32 * VPL * 4 values (VPL =
+// 9: 1152, VPL = 8: 1024), the row held in registers between the passes and
+// the reductions done with shuffles alone; 8 rows per CTA, 3 CTAs per SM.
+// Used from ROW_KERNEL_MIN_ROWS rows up (the encoder's 78,400-row LayerNorms:
+// 162 vs 240 us, 6.7 TB/s); a decode step's few hundred rows would leave most
+// SMs idle, so they keep the CTA-per-row kernel.
+constexpr int ROW_WARPS = 8;
+constexpr uint32_t ROW_KERNEL_MIN_ROWS = 4096;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <bool LAYER, int VPL>
+__global__ void __launch_bounds__(ROW_WARPS * 32, 3) add_norm_row_kernel(
+    float* __restrict__ h, const __half* __restrict__ delta, uint32_t rows,
+    const float* __restrict__ weight, const float* __restrict__ bias, float eps,
+    __half* __restrict__ out) {
+  constexpr uint32_t width = 128u * VPL;
+  const size_t row = (size_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  float4* hr = reinterpret_cast<float4*>(h + row * width);
+  float4 v[VPL];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) v[k] = hr[lane + 32 * k];
+  if (delta) {
+    const uint2* dr = reinterpret_cast<const uint2*>(delta + row * width);
+    uint2 d[VPL];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) d[k] = dr[lane + 32 * k];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d[k].x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&d[k].y));
+      v[k].x += a.x;
+      v[k].y += a.y;
+      v[k].z += b.x;
+      v[k].w += b.y;
+      hr[lane + 32 * k] = v[k];
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
+    s += LAYER ? (v[k].x + v[k].y) + (v[k].z + v[k].w)
+               : (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+  float mean = 0.f, inv;
+  if (LAYER) {
+    mean = warp_sum(s) / (float)width;
+    float var = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+      var += (a * a + b * b) + (c * c + d * d);
+    }
+    inv = 1.f / sqrtf(warp_sum(var) / (float)width + eps);
+  } else {
+    inv = 1.f / sqrtf(warp_sum(s) / (float)width + eps);
+  }
+  const float4* w4 = reinterpret_cast<const float4*>(weight);
+  const float4* b4 = reinterpret_cast<const float4*>(bias);
+  uint2* orow = reinterpret_cast<uint2*>(out + row * width);
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int i = lane + 32 * k;
+    const float4 w = __ldg(w4 + i);
+    float4 y;
+    if (LAYER) {
+      const float4 b = __ldg(b4 + i);
+      y = make_float4((v[k].x - mean) * inv * w.x + b.x, (v[k].y - mean) * inv * w.y + b.y,
+                      (v[k].z - mean) * inv * w.z + b.z, (v[k].w - mean) * inv * w.w + b.w);
+    } else {
+      y = make_float4(v[k].x * inv * w.x, v[k].y * inv * w.y, v[k].z * inv * w.z,
+                      v[k].w * inv * w.w);
+    }
+    const __half2 lo = __floats2half2_rn(y.x, y.y), hi = __floats2half2_rn(y.z, y.w);
+    orow[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
+                         *reinterpret_cast<const uint32_t*>(&hi));
+  }
+}
+
+template <bool LAYER>
+bool launch_row_kernel(float* h, const __half* d, uint32_t rows, uint32_t width, const float* w,
+                       const float* b, float eps, __half* o, cudaStream_t s) {
+  const uint32_t grid = (rows + ROW_WARPS - 1) / ROW_WARPS;
+  if (width == 1152) {
+    add_norm_row_kernel<LAYER, 9><<<grid, ROW_WARPS * 32, 0, s>>>(h, d, rows, w, b, eps, o);
+    return true;
+  }
+  if (width == 1024) {
+    add_norm_row_kernel<LAYER, 8><<<grid, ROW_WARPS * 32, 0, s>>>(h, d, rows, w, b, eps, o);
+    return true;
+  }
+  return false;
 }
 
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -222,6 +324,10 @@ int pvlc_add_norm(float* residual, const pvlc_half* delta, uint32_t rows, uint32
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const __half* d = reinterpret_cast<const __half*>(delta);
   __half* o = reinterpret_cast<__half*>(out);
+  if (rows >= glue::ROW_KERNEL_MIN_ROWS &&
+      (bias ? glue::launch_row_kernel<true>(residual, d, rows, width, weight, bias, eps, o, s)
+            : glue::launch_row_kernel<false>(residual, d, rows, width, weight, nullptr, eps, o, s)))
+    return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
   if (bias)
     glue::add_norm_kernel<true><<<rows, glue::NORM_THREADS, 0, s>>>(residual, d, width, weight,
                                                                     bias, eps, o);

@@ -17,7 +17,11 @@ TOL = dict(atol=2e-3, rtol=2e-3)
 @pytest.mark.parametrize("rows,width,layer,with_delta", [
     (3, 1152, True, False), (257, 1152, True, True), (5, 1024, False, True),
     (1000, 1024, False, False), (9, 8, True, True), (17, 2048, False, True),
-    (4, 2056, True, True), (2, 4608, True, True)])
+    (4, 2056, True, True), (2, 4608, True, True),
+    # from 4096 rows, widths 1152 / 1024 take the warp-per-row kernel (8 rows per CTA;
+    # 8191 leaves a partial last CTA)
+    (5000, 1152, True, True), (8191, 1152, True, False), (4096, 1024, False, True),
+    (4100, 1024, False, False)])
 def test_add_norm(cuda_lib, rows, width, layer, with_delta):
     g = torch.Generator(device="cuda")
     g.manual_seed(rows + width)
