@@ -706,10 +706,10 @@ def main():
             import torch.distributed as tdist
 
             from pvlc_b200 import dist as pdist
-            # NCCL prints its version banner on stdout under NCCL_DEBUG=VERSION;
-            # stdout carries only the JSON line
-            if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-                os.environ["NCCL_DEBUG"] = "WARN"
+            # NCCL logs to stdout, and at any NCCL_DEBUG level from VERSION up (WARN
+            # included) it prints its version banner there; stdout carries only the
+            # JSON line, so NCCL's log goes to stderr unless the caller chose a file
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             torch.cuda.set_device(local_rank)
             pdist.init("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
             dist = tdist
