@@ -656,8 +656,32 @@ def run_reference(args, rank):
                     "C++ restatement in oracle/"}
 
 
+_JSON_FD = None
+
+
+def _stdout_for_json_only():
+    """Keep the process's stdout for the JSON line alone: libraries that print to file
+    descriptor 1 (NCCL's version banner at communicator creation, among others) are sent
+    to stderr, and emit() writes the line to the saved descriptor."""
+    global _JSON_FD
+    if _JSON_FD is None:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
+def emit(obj) -> None:
+    data = (json.dumps(obj) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 def main():
     global LAYERS, SEQS_PER_GPU, METRIC
+    _stdout_for_json_only()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
@@ -689,14 +713,14 @@ def main():
     if args.only == "e2e" and args.impl == "ours":
         import torch
         torch.cuda.set_device(0)
-        print(json.dumps(run_e2e(args, torch.device("cuda", 0), 0, 1, None)), flush=True)
+        emit(run_e2e(args, torch.device("cuda", 0), 0, 1, None))
         return
     if args.only is not None and args.impl == "ours":
         import torch
         hbm_peak, tf_peak, peak_src = peaks()
         res = run_components(args, torch.device("cuda", 0), tf_peak, peak_src,
                              which=(args.only,), iters=args.steps, warm=args.warmup)
-        print(json.dumps(res), flush=True)
+        emit(res)
         return
     if args.impl == "reference":
         line = run_reference(args, rank)
@@ -706,10 +730,6 @@ def main():
             import torch.distributed as tdist
 
             from pvlc_b200 import dist as pdist
-            # NCCL logs to stdout, and at any NCCL_DEBUG level from VERSION up (WARN
-            # included) it prints its version banner there; stdout carries only the
-            # JSON line, so NCCL's log goes to stderr unless the caller chose a file
-            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             torch.cuda.set_device(local_rank)
             pdist.init("nccl", timeout_s=120.0, device_id=torch.device("cuda", local_rank))
             dist = tdist
@@ -718,7 +738,7 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 if __name__ == "__main__":
