@@ -549,6 +549,9 @@ def run_e2e(args, dev, rank, world, dist):
     barrier()
     clocks = sampler.stop()
     clocks["host_loadavg_1m"] = [round(load0, 2), round(os.getloadavg()[0], 2)]
+    # every rank's own breakdown, for the record (stderr: stdout carries the JSON line)
+    print(f"e2e rank {rank}/{world}: {e0.elapsed_time(e1):.1f} ms {timings}", file=sys.stderr,
+          flush=True)
     ms = e0.elapsed_time(e1)
     tokens = sum(len(t) for t in res["tokens"])
     eos = sum(1 for r in res["stop"] if r == "eos_token")
