@@ -450,31 +450,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_after_sync();
         const bool store = row < seg_end;
         __half* orow = p.out + ((size_t)row * p.heads + head) * HD;
-        // columns 64..79 first: column 72 holds the row sum
-        uint32_t last[16];
-        tc::tmem_ld16(tO + 64, last);
+        // the whole O row (80 columns; column 72 holds the row sum) in one round trip
+        uint32_t ov[80];
+        tc::tmem_ld32(tO, ov);
+        tc::tmem_ld32(tO + 32, ov + 32);
+        tc::tmem_ld16(tO + 64, ov + 64);
         tc::tmem_wait_ld();
-        const float inv = 1.f / __uint_as_float(last[SUM_COL - 64]);
+        const float inv = 1.f / __uint_as_float(ov[SUM_COL]);
 #pragma unroll
-        for (int cc = 0; cc < 80; cc += 16) {
-          uint32_t ov[16];
-          if (cc < 64) {
-            tc::tmem_ld16(tO + cc, ov);
-            tc::tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] = last[e];
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (cc + 8 * h >= HD) break;   // columns 72..79: row sum and padding
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
-            v.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
-            v.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
-            v.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
-            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = v;
-          }
+        for (int c8 = 0; c8 < HD; c8 += 8) {   // columns 72..79: row sum and padding
+          uint4 v;
+          v.x = pack_half2(__uint_as_float(ov[c8 + 0]) * inv, __uint_as_float(ov[c8 + 1]) * inv);
+          v.y = pack_half2(__uint_as_float(ov[c8 + 2]) * inv, __uint_as_float(ov[c8 + 3]) * inv);
+          v.z = pack_half2(__uint_as_float(ov[c8 + 4]) * inv, __uint_as_float(ov[c8 + 5]) * inv);
+          v.w = pack_half2(__uint_as_float(ov[c8 + 6]) * inv, __uint_as_float(ov[c8 + 7]) * inv);
+          if (store) *reinterpret_cast<uint4*>(orow + c8) = v;
         }
       } else {
         misc[1] = 1;
