@@ -20,13 +20,18 @@
 //
 // GQA packing: a Q tile is 16 tokens x the 8 query heads of one KV group =
 // 128 MMA rows (row r = token r/8, head r%8), loaded by one 3-D TMA box, so a
-// K/V tile of 128 keys serves all 8 heads.  One CTA = (KV head, one Q tile);
-// its causal key range (K tiles 0 .. the diagonal) is split between two
-// streams, even and odd K tiles, with their own S and O in TMEM, which
-// ping-pong on the MMA warp.  The chain of dependent K tiles per CTA is
-// therefore at most ceil(13 / 2) = 7 at T = 1564 (a CTA holding all of a
-// 32-token block's keys had 13), over 2 x ceil(T / 16) CTAs; the two
-// streams' (O, m, l) are merged inside the CTA at the end.
+// K/V tile of 128 keys serves all 8 heads.  A CTA (one KV head) runs two
+// streams with their own S and O in TMEM, which ping-pong on the MMA warp:
+//   split: one Q tile whose causal key range (K tiles 0 .. the diagonal) is
+//          dealt to the streams as even and odd K tiles, the two streams'
+//          (O, m, l) merged inside the CTA at the end -- the chain of
+//          dependent K tiles is at most ceil(13 / 2) = 7 at T = 1564;
+//   pair:  two Q tiles, one per stream, sharing every K/V tile (the second
+//          tile's K tiles a prefix of the first's).
+// A single prompt splits its heaviest tiles and pairs the lightest (light
+// tile n - 1 - i with i) only while that keeps one wave within the heaviest
+// split CTA's time; a batched launch (up to 256 prompts packed back to back,
+// the prompt table a grid constant) pairs each prompt's adjacent tiles.
 // Causal masking inside tiles that cross the diagonal.
 // head_dim 128 = two 64-dim blocks of 128-byte rows (128B swizzle); QK = 8 x
 // K16 steps (M128 N128), PV = 8 x K16 steps (M128 N128, V MN-major across
@@ -38,7 +43,8 @@
 //                   softmax (f32, exp2 domain) and P (fp16) over S; at the
 //                   end each writes output columns 64t..64t+63 from both
 //                   streams' O
-//   warp 8          TMA producer: the Q tile, then K/V tiles (3 stages)
+//   warp 8          TMA producer: the Q tile(s), then K/V tiles (3 stages
+//                   split, 2 paired)
 //   warp 9          MMA issuer (the whole warp walks the schedule, one
 //                   elected lane issues)
 // TMEM (512 columns): S/P of stream t at [128t, 128t+128), O at [256+128t, +128).
