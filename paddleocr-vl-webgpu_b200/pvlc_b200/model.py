@@ -17,12 +17,14 @@ Architecture (the reference's pinned PaddleOCR-VL-1.6 shapes; random-init fp16 w
 Precision: weights and every intermediate activation in fp16; residual streams,
 normalisation statistics and logits in f32.  Attention runs on this library's
 kernels through the C ABI (vision varlen, decoder causal prefill with the KV
-cache written in place, batched split-KV decode with the KV append fused), and
-so do the elementwise passes (residual add + LayerNorm / RMSNorm, GELU, SiLU
-gate; each residual add rides in the next norm's pass); the dense layers are
-cuBLAS GEMMs on the same stream.  The batched decode step is captured once in
-a CUDA graph and replayed; tokens are read back once per chunk of steps, as
-the reference's chunked greedy driver does (lib.rs:2309-2366).
+cache written in place -- all prompts of a batch in one launch pair per layer --,
+batched split-KV decode with the KV append fused), and so do the elementwise
+passes (residual add + LayerNorm / RMSNorm, GELU, SiLU gate; each residual add
+rides in the next norm's pass); the dense layers are cuBLAS GEMMs on the same
+stream (the vision fc1's GELU in its cuBLASLt epilogue).  The batched decode
+step is captured once in a CUDA graph and replayed; tokens are read back once
+per chunk of steps, as the reference's chunked greedy driver does
+(lib.rs:2309-2366), with the next chunk already queued.
 
 Weight lists are in the canonical order shared with the CPU oracle
 (oracle/pvlc_model_oracle.cpp, pvlc_oracle_generate).
