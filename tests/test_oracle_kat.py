@@ -85,7 +85,10 @@ def test_decode_equals_last_causal_row(L):
 
 def test_decode_direct_boundary_digest_is_recorded():
     """The reference literal DIRECT_BOUNDARY_BLAKE3 (decoder_decode_contract.rs:17-21)
-    is NOT reproduced by glibc expf nor by a correctly rounded exp; this records the
+    is NOT reproduced by glibc expf, by a correctly rounded exp, nor by the FreeBSD
+    msun e_expf.c algorithm (the one Rust's `libm` crate ports).  The arithmetic
+    around exp follows independent_decode_gqa (:356-423) step for step, so the
+    literal was evidently made with another platform's expf.  This records the
     digest this oracle produces so any drift in the oracle is caught."""
     h = blake3.blake3()
     for L in [1, 2, 15, 16, 17, 31, 32, 33]:
