@@ -290,6 +290,32 @@ int pvlc_silu_mul(const pvlc_half* gate_up, uint32_t rows, uint32_t width, pvlc_
                   void* stream);
 
 /* ----------------------------------------------------------------------------
+ * Checkpoint import on the device: BF16 -> IEEE binary16, round to nearest,
+ * ties to even.
+ *
+ * Replaces the payload half of the reference's checkpoint converter
+ * (crates/pvlc-safetensors/src/fp16.rs:171-210 finite_bf16_to_f16_bits,
+ * :212-276 stream_bf16_payload_to_f16; conversion id
+ * "bf16_to_ieee_f16_rne_v1"): the engine uploads the BF16 payload and converts
+ * it in HBM instead of writing an FP16 file on the host.
+ *
+ * Converts `count` elements of `src` into `dst` (both 16-byte aligned device
+ * pointers).  A NaN / infinity source, or a finite one beyond the f16 range,
+ * is rejected as the reference rejects it: `*rejected` (an 8-byte aligned
+ * device word) is lowered with atomicMin to
+ *     (index_base + i) << 1 | out_of_range
+ * for the rejected element i (out_of_range = 0: non-finite, 1: finite but out
+ * of range), so after the launch it holds the lowest rejected payload index --
+ * the element the reference's stream converter names -- and its reason.  The
+ * call does not reset the word: set it to ~0 (no rejection) before the first
+ * call of a payload, and pass each chunk's first payload index as index_base
+ * when a payload is converted in several calls.  The contents of dst are
+ * unspecified for a payload with a rejection.
+ */
+int pvlc_bf16_to_f16(const uint16_t* src, uint16_t* dst, uint64_t count, uint64_t index_base,
+                     unsigned long long* rejected, void* stream);
+
+/* ----------------------------------------------------------------------------
  * Plans: the host-side half of the contract, callable without a GPU.
  * They run the same validation as the launch entry points and report the
  * launch geometry the library will use.

@@ -38,7 +38,8 @@ class OracleError(RuntimeError):
 
 def build() -> str:
     """Compile the oracle with its Makefile (only when the library is missing or stale)."""
-    srcs = [os.path.join(_HERE, f) for f in ("pvlc_oracle.cpp", "pvlc_model_oracle.cpp")]
+    srcs = [os.path.join(_HERE, f) for f in ("pvlc_oracle.cpp", "pvlc_model_oracle.cpp",
+                                                  "pvlc_checkpoint_oracle.cpp")]
     if not os.path.exists(_LIB_PATH) or \
             os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(f) for f in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
@@ -356,3 +357,27 @@ def generate(dims: dict, vision_w, projector_w, decoder_w, patches, grids, input
     if want_features:
         out["vision"], out["projector"] = vis, proj
     return out
+
+
+def bf16_to_f16_bits(bits):
+    """crates/pvlc-safetensors/src/fp16.rs:171-210 element-wise over uint16 BF16 bit
+    patterns: returns (f16 bits uint16, status uint8: 0 converted, 1 non-finite,
+    2 out of the f16 range)."""
+    src = np.ascontiguousarray(bits, dtype=np.uint16).reshape(-1)
+    dst = np.zeros_like(src)
+    status = np.zeros(src.shape, np.uint8)
+    lib().pvlc_oracle_bf16_to_f16_bits(_p(src), _p(dst), _p(status), ctypes.c_uint64(src.size))
+    return dst, status
+
+
+def stream_bf16_to_f16(bits):
+    """crates/pvlc-safetensors/src/fp16.rs:212-276: converts in order, stopping at the
+    first rejected element.  Returns (f16 bits, None) or (None, (index, status))."""
+    src = np.ascontiguousarray(bits, dtype=np.uint16).reshape(-1)
+    dst = np.zeros_like(src)
+    index = ctypes.c_uint64(0)
+    status = lib().pvlc_oracle_stream_bf16_to_f16(_p(src), _p(dst), ctypes.c_uint64(src.size),
+                                                  ctypes.byref(index))
+    if status:
+        return None, (index.value, status)
+    return dst, None

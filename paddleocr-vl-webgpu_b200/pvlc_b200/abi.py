@@ -89,6 +89,7 @@ _SIGNATURES = {
     "pvlc_add_norm": (ctypes.c_int, [_P, _P, _U32, _U32, _P, _P, ctypes.c_float, _P, _P]),
     "pvlc_gelu": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int, _P]),
     "pvlc_silu_mul": (ctypes.c_int, [_P, _U32, _U32, _P, _P]),
+    "pvlc_bf16_to_f16": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint64, _P, _P]),
     "pvlc_plan_vision_varlen": (ctypes.c_int, [_P, _U32, _U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_prefill": (ctypes.c_int, [_U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_kv_session": (ctypes.c_int, [_U32, _U32, _U32, _U32, _U32,

@@ -183,6 +183,15 @@ class OcrEngine:
         self._grid_cache = {}
         self._graph = None
 
+    @classmethod
+    def from_checkpoint(cls, path, cfg: ModelConfig | None = None, device=None, **kw):
+        """Engine over a PaddleOCR-VL-1.6 BF16 safetensors checkpoint: header checked
+        against the exact catalog, payload converted to fp16 on the device
+        (pvlc_b200.checkpoint.load_weights)."""
+        from . import checkpoint
+        cfg = cfg or ModelConfig()
+        return cls(cfg, checkpoint.load_weights(path, cfg, device), device, **kw)
+
     # ------------------------------------------------------------- vision side
     def _grid_tables(self, grid):
         """Per-grid device tables: interpolated position embedding (f32), 2-D RoPE, merge order."""
