@@ -49,6 +49,9 @@ UNIT = "GB/s"
 DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 283.27e6 / 278.20e6
 VISION_TC_TRAFFIC_BYTES = 61.00e6
 PREFILL_ATTN_TRAFFIC_BYTES = 11.37e6
+# checkpoint conversion, one launch over the whole payload
+# (profiles/bf16_to_f16_kernel_checkpoint.txt: 5.820 TB/s x 651.3 us)
+CONVERT_TRAFFIC_BYTES = 3.7907e9
 
 
 def peaks():
@@ -425,9 +428,9 @@ def bench_checkpoint(dev, timeit):
            "ms": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s", "checked": ok,
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
                         "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
-                        "peak_source": peak_src, "traffic": 4 * n,
-                        "traffic_source": "algorithmic (2 B read + 2 B written per element); "
-                                          "ncu summary in profiles/"},
+                        "peak_source": peak_src, "traffic": CONVERT_TRAFFIC_BYTES,
+                        "traffic_source": "ncu capture of one launch of this workload "
+                                          "(DRAM bytes per second x duration)"},
            "kernel": "pvlc::convert::bf16_to_f16_kernel"}
     del dst
     try:

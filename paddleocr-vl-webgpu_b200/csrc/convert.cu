@@ -9,6 +9,17 @@
 //   unbiased exponent -14..15                -> f16 normal, exact (fraction << 3);
 //   below -14                                -> f16 subnormal: the 8-bit
 //                                               significand shifted right, RNE.
+// Fast path: wherever that rule converts (every element finite and below 2^16
+// in magnitude) its result is IEEE binary16 round-to-nearest-even of the value,
+// checked on all 65,536 BF16 patterns, so a vector of eight such elements goes
+// through the hardware conversion (cvt.rn.f16x2.f32, two elements per
+// instruction; a BF16 value widens to f32 exactly by a shift).  Its range check
+// is branch-free: a half-word magnitude m >= 0x4780 (2^16, infinity, NaN) is
+// exactly m + 0x3880 >= 0x8000, with no carry between the two halves of a
+// 32-bit word.  Only a vector holding such an element re-runs the reference's
+// integer sequence below, element by element, to find the first one and its
+// reason.  (A per-element integer conversion made the kernel issue-bound: 71 %
+// of peak instruction issue, 52 % of peak DRAM throughput.)
 //
 // Rejections.  The reference's stream converter stops at the first rejected
 // element in payload order and names its index (fp16.rs:212-276).  Here every
@@ -65,6 +76,14 @@ __device__ __forceinline__ void reject(unsigned long long* word, uint64_t index,
   atomicMin(word, record);
 }
 
+// Two BF16 values (low, high half of w) to two f16 values, IEEE RNE.
+__device__ __forceinline__ uint32_t cvt2(uint32_t w) {
+  const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xffff0000u);
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // Converts one 16-byte vector; returns the converted vector and folds the
 // vector's first rejected element (if any) into *word.
 __device__ __forceinline__ uint4 convert_vec(const uint4 v, uint64_t first_index,
@@ -74,9 +93,8 @@ __device__ __forceinline__ uint4 convert_vec(const uint4 v, uint64_t first_index
   uint32_t flags = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = bf16_to_f16(in[i] & 0xffffu), hi = bf16_to_f16(in[i] >> 16);
-    out[i] = (lo & 0xffffu) | (hi << 16);
-    flags |= (lo | hi) & 0x30000u;
+    flags |= ((in[i] & 0x7fff7fffu) + 0x38803880u) & 0x80008000u;
+    out[i] = cvt2(in[i]);
   }
   if (flags) {
 #pragma unroll 1
