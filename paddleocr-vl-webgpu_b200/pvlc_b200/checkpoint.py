@@ -589,12 +589,24 @@ def _rejection_error(catalog, record: int):
                                name, element)
 
 
+def _pread_exact(fd, view, offset):
+    got = 0
+    while got < len(view):
+        r = os.preadv(fd, [view[got:]], offset + got)
+        if r <= 0:
+            raise Fp16CheckpointError("Io", "source checkpoint is truncated")
+        got += r
+
+
 class _DevicePayload:
     """Chunked host -> device pipeline: the payload is read into two pinned buffers in
-    turn, each copied to HBM and converted there in place; hashing and the consumer of
-    each converted chunk are optional hooks."""
+    turn (each chunk by several threads, one slice each: one thread copying out of the
+    page cache reads ~7.5 GB/s), each copied to HBM and converted there in place;
+    hashing and the consumer of each converted chunk are optional hooks."""
 
-    def __init__(self, device, chunk_bytes=DEVICE_CHUNK_BYTES):
+    READ_SLICE = 8 << 20
+
+    def __init__(self, device, chunk_bytes=DEVICE_CHUNK_BYTES, readers=None):
         import torch
         from . import abi
         abi.lib()
@@ -605,15 +617,24 @@ class _DevicePayload:
                        for _ in range(2)]
         self.ready = [None, None]
         self.word = torch.full((1,), -1, dtype=torch.int64, device=self.device)
+        self.readers = readers or max(1, min(8, os.cpu_count() or 1))
 
     def run(self, fh, body_len, dst=None, on_chunk=None, hasher=None):
-        """Reads body_len payload bytes from fh's position.  dst: a device uint8 buffer of
-        body_len bytes to convert into (in place), or None to convert through a device
-        chunk buffer handed to on_chunk(offset, device_chunk, n)."""
+        """Reads body_len payload bytes from fh's position (fh's own position is left
+        alone).  dst: a device uint8 buffer of body_len bytes to convert into (in place),
+        or None to convert through a device chunk buffer handed to
+        on_chunk(offset, device_chunk, n)."""
+        from concurrent.futures import ThreadPoolExecutor
         torch = self.torch
         stream = torch.cuda.current_stream(self.device)
         scratch = None if dst is not None else torch.empty(self.chunk, dtype=torch.uint8,
                                                            device=self.device)
+        fd, base = fh.fileno(), fh.tell()
+        with ThreadPoolExecutor(self.readers) as pool:
+            return self._run(pool, fd, base, body_len, dst, scratch, stream, on_chunk, hasher)
+
+    def _run(self, pool, fd, base, body_len, dst, scratch, stream, on_chunk, hasher):
+        torch = self.torch
         for i, off in enumerate(range(0, body_len, self.chunk)):
             slot = i & 1
             if self.ready[slot] is not None:
@@ -621,12 +642,10 @@ class _DevicePayload:
             n = min(self.chunk, body_len - off)
             host = self.pinned[slot][:n]
             view = memoryview(host.numpy())
-            got = 0
-            while got < n:
-                r = fh.readinto(view[got:])
-                if not r:
-                    raise Fp16CheckpointError("Io", "source checkpoint is truncated")
-                got += r
+            parts = [pool.submit(_pread_exact, fd, view[a:min(n, a + self.READ_SLICE)],
+                                 base + off + a) for a in range(0, n, self.READ_SLICE)]
+            for f in parts:
+                f.result()
             if hasher is not None:
                 hasher.update(view)
             target = dst[off:off + n] if dst is not None else scratch[:n]

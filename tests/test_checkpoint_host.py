@@ -300,3 +300,18 @@ def test_fp16_output_header_matches_the_reference_fixture():
 def test_library_exports_the_conversion_entry_point():
     assert "pvlc_bf16_to_f16" in abi.EXPORTED
     assert hasattr(abi.lib(), "pvlc_bf16_to_f16")
+
+
+def test_payload_reader_fills_slices_exactly(tmp_path):
+    """The device pipeline's reader threads each fill one slice of a pinned chunk with
+    positional reads; a short file is an Io error, never a partial chunk."""
+    data = bytes(range(256)) * 1000
+    p = tmp_path / "payload.bin"
+    p.write_bytes(data)
+    buf = bytearray(1000)
+    with open(p, "rb") as f:
+        C._pread_exact(f.fileno(), memoryview(buf), 12_345)
+        assert bytes(buf) == data[12_345:13_345]
+        with pytest.raises(C.Fp16CheckpointError) as e:
+            C._pread_exact(f.fileno(), memoryview(buf), len(data) - 10)
+    assert e.value.code == "Io"
