@@ -432,6 +432,7 @@ def bench_checkpoint(dev, timeit):
                         "traffic_source": "ncu capture of one launch of this workload "
                                           "(DRAM bytes per second x duration)"},
            "kernel": "pvlc::convert::bf16_to_f16_kernel"}
+    res["cpu_baseline"] = cpu_convert_baseline(src[:1 << 26].cpu().numpy())
     del dst
     try:
         header = C.safetensors_header(entries, {"format": "pt"})
@@ -689,6 +690,21 @@ def cpu_e2e_baseline(cfg, weights):
                       f"{len(r['tokens'])} greedy tokens, {el:.1f} s end to end "
                       "(reduced: a 980x980 page is ~4e12 FLOP of vision encoder on the CPU)"}
 
+
+
+def cpu_convert_baseline(sample_bits):
+    """The reference's host conversion (fp16.rs:171-276, one element at a time), restated
+    in the oracle, over a bounded sample of the payload; GB/s at 4 bytes per element."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    O.bf16_to_f16_bits(sample_bits[:1024])
+    t0 = time.perf_counter()
+    _, status = O.bf16_to_f16_bits(sample_bits)
+    dt = time.perf_counter() - t0
+    return {"value": round(4.0 * sample_bits.size / dt / 1e9, 3), "unit": "GB/s", "cores": 1,
+            "kind": "port", "checked": bool((status == 0).all()),
+            "sample": f"{sample_bits.size:,} BF16 elements of the bench payload, "
+                      f"{dt:.2f} s, one thread"}
 
 
 def cpu_decode_baseline(seconds: float):
