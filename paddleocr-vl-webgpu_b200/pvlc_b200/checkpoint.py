@@ -630,7 +630,8 @@ class _DevicePayload:
         scratch = None if dst is not None else torch.empty(self.chunk, dtype=torch.uint8,
                                                            device=self.device)
         fd, base = fh.fileno(), fh.tell()
-        with ThreadPoolExecutor(self.readers) as pool:
+        # the library launches on the calling thread's current device
+        with torch.cuda.device(self.device), ThreadPoolExecutor(self.readers) as pool:
             return self._run(pool, fd, base, body_len, dst, scratch, stream, on_chunk, hasher)
 
     def _run(self, pool, fd, base, body_len, dst, scratch, stream, on_chunk, hasher):
