@@ -300,7 +300,7 @@ int pvlc_silu_mul(const pvlc_half* gate_up, uint32_t rows, uint32_t width, pvlc_
  * it in HBM instead of writing an FP16 file on the host.
  *
  * Converts `count` elements of `src` into `dst` (both 16-byte aligned device
- * pointers).  A NaN / infinity source, or a finite one beyond the f16 range,
+ * pointers; src == dst converts in place).  A NaN / infinity source, or a finite one beyond the f16 range,
  * is rejected as the reference rejects it: `*rejected` (an 8-byte aligned
  * device word) is lowered with atomicMin to
  *     (index_base + i) << 1 | out_of_range
