@@ -315,3 +315,26 @@ def test_payload_reader_fills_slices_exactly(tmp_path):
         with pytest.raises(C.Fp16CheckpointError) as e:
             C._pread_exact(f.fileno(), memoryview(buf), len(data) - 10)
     assert e.value.code == "Io"
+
+
+def test_converter_refuses_before_touching_a_device(tmp_path):
+    """fp16.rs:278-305,524-552: aliasing, an existing output, an unreadable catalog and a
+    non-BF16 tensor are refused on the host, before any payload work, leaving no file."""
+    src = write(tmp_path, b'{"w":{"dtype":"BF16","shape":[1],"data_offsets":[0,2]}}', b"\x80\x3f",
+                "source.safetensors")
+    existing = tmp_path / "existing.safetensors"
+    existing.write_bytes(b"keep")
+    cases = [(src, src, "SourceDestinationAlias"),
+             (src, existing, "OutputAlreadyExists"),
+             (write(tmp_path, b'{"w":{"dtype":"BF16","shape":[2],"data_offsets":[0,2]}}',
+                    b"\0\0", "bad.safetensors"), tmp_path / "bad.out", "InvalidSource"),
+             (write(tmp_path, b'{"w":{"dtype":"F16","shape":[1],"data_offsets":[0,2]}}',
+                    b"\0\x3c", "f16.safetensors"), tmp_path / "f16.out",
+              "UnsupportedSourceDtype")]
+    for source, output, code in cases:
+        with pytest.raises(C.Fp16CheckpointError) as e:
+            C.convert_bf16_checkpoint_to_f16(source, output)
+        assert e.value.code == code
+    assert existing.read_bytes() == b"keep"
+    assert not (tmp_path / "bad.out").exists() and not (tmp_path / "f16.out").exists()
+    assert not [p for p in os.listdir(tmp_path) if p.startswith(".pvlc-f16-")]
