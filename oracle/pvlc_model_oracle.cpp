@@ -81,9 +81,13 @@ using Vec = std::vector<float>;
 
 inline float f16_round(float x) { return (float)(_Float16)x; }
 
+// Elementwise passes below are split across threads only by element, so each
+// element sees the same single operation whatever the thread count.
 void store(Vec& v, bool f16) {
   if (!f16) return;
-  for (auto& x : v) x = f16_round(x);
+  const long long n = (long long)v.size();
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < n; ++i) v[i] = f16_round(v[i]);
 }
 
 inline float widen_half(uint16_t h) {
@@ -94,7 +98,8 @@ inline float widen_half(uint16_t h) {
 
 Vec widen(const uint16_t* p, size_t n) {
   Vec out(n);
-  for (size_t i = 0; i < n; ++i) out[i] = widen_half(p[i]);
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; ++i) out[i] = widen_half(p[i]);
   return out;
 }
 
@@ -104,16 +109,70 @@ Vec widen(const uint16_t* p, size_t n) {
 // [out][in].
 void linear(const float* in, size_t rows, size_t iw, const float* w, const float* bias, size_t ow,
             float* out) {
-  const long long total = (long long)rows * (long long)ow;
+  // Every output is the same scalar sequence (start at the bias, then
+  // `acc += x[d] * w[o][d]` for d ascending); only independent outputs are
+  // computed side by side.  Few rows (a decode step, the LM head): 8 outputs
+  // per thread step, weights read in place.  Many rows: the weights are first
+  // transposed to [in][out] so a block of 4 rows x 64 outputs advances in
+  // vector lanes.
+  if (rows < 8) {
+    const long long groups = (long long)((ow + 7) / 8);
 #pragma omp parallel for schedule(static)
-  for (long long i = 0; i < total; ++i) {
-    const size_t r = (size_t)(i / (long long)ow), o = (size_t)(i % (long long)ow);
-    const float* x = in + r * iw;
-    const float* wr = w + o * iw;
-    float acc = bias ? bias[o] : 0.0f;
-    for (size_t d = 0; d < iw; ++d) acc += x[d] * wr[d];
-    out[r * ow + o] = acc;
+    for (long long gi = 0; gi < groups; ++gi) {
+      const size_t o0 = (size_t)gi * 8, no = std::min<size_t>(8, ow - o0);
+      for (size_t r = 0; r < rows; ++r) {
+        const float* x = in + r * iw;
+        float acc[8];
+        for (size_t j = 0; j < no; ++j) acc[j] = bias ? bias[o0 + j] : 0.0f;
+        if (no == 8) {
+          for (size_t d = 0; d < iw; ++d) {
+            const float xd = x[d];
+            for (size_t j = 0; j < 8; ++j) acc[j] += xd * w[(o0 + j) * iw + d];
+          }
+        } else {
+          for (size_t d = 0; d < iw; ++d)
+            for (size_t j = 0; j < no; ++j) acc[j] += x[d] * w[(o0 + j) * iw + d];
+        }
+        for (size_t j = 0; j < no; ++j) out[r * ow + o0 + j] = acc[j];
+      }
+    }
+    return;
   }
+  std::vector<float> wt(iw * ow);
+#pragma omp parallel for schedule(static)
+  for (long long o = 0; o < (long long)ow; ++o)
+    for (size_t d = 0; d < iw; ++d) wt[d * ow + (size_t)o] = w[(size_t)o * iw + d];
+  constexpr size_t RB = 4, OB = 64;
+  const long long rblocks = (long long)((rows + RB - 1) / RB);
+  const long long oblocks = (long long)((ow + OB - 1) / OB);
+#pragma omp parallel for collapse(2) schedule(static)
+  for (long long rb = 0; rb < rblocks; ++rb)
+    for (long long ob = 0; ob < oblocks; ++ob) {
+      const size_t r0 = (size_t)rb * RB, nr = std::min(RB, rows - r0);
+      const size_t o0 = (size_t)ob * OB, no = std::min(OB, ow - o0);
+      float acc[RB][OB];
+      for (size_t r = 0; r < RB; ++r)
+        for (size_t j = 0; j < OB; ++j) acc[r][j] = (bias && j < no) ? bias[o0 + j] : 0.0f;
+      if (nr == RB && no == OB) {
+        for (size_t d = 0; d < iw; ++d) {
+          const float* wr = &wt[d * ow + o0];
+          for (size_t r = 0; r < RB; ++r) {
+            const float xd = in[(r0 + r) * iw + d];
+            for (size_t j = 0; j < OB; ++j) acc[r][j] += xd * wr[j];
+          }
+        }
+      } else {
+        for (size_t d = 0; d < iw; ++d) {
+          const float* wr = &wt[d * ow + o0];
+          for (size_t r = 0; r < nr; ++r) {
+            const float xd = in[(r0 + r) * iw + d];
+            for (size_t j = 0; j < no; ++j) acc[r][j] += xd * wr[j];
+          }
+        }
+      }
+      for (size_t r = 0; r < nr; ++r)
+        for (size_t j = 0; j < no; ++j) out[(r0 + r) * ow + o0 + j] = acc[r][j];
+    }
 }
 
 Vec linear_v(const Vec& in, size_t rows, size_t iw, const float* w, const float* bias, size_t ow,
@@ -169,7 +228,21 @@ inline float gelu_erf(float v) { return 0.5f * v * (1.0f + std::erf(v * 0.707106
 
 void add_into(Vec& acc, const Vec& x) {
   // crates/pvlc-cpu-ref/src/lib.rs:142-154 (add_vectors_f32)
-  for (size_t i = 0; i < acc.size(); ++i) acc[i] = acc[i] + x[i];
+  const long long n = (long long)acc.size();
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < n; ++i) acc[i] = acc[i] + x[i];
+}
+
+void apply(Vec& v, float (*f)(float)) {
+  const long long n = (long long)v.size();
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < n; ++i) v[i] = f(v[i]);
+}
+
+void silu_gate(const Vec& gate, const Vec& up, Vec& act) {
+  const long long n = (long long)act.size();
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < n; ++i) act[i] = silu(gate[i]) * up[i];
 }
 
 // Bilinear source coordinate, crates/pvlc-cpu-ref/src/lib.rs:265-278.
@@ -330,7 +403,7 @@ int decoder_layer_prefill(Vec& h, size_t T, const DecoderGeom& g, const float* c
   Vec gate = linear_v(n2, T, D, w.gate, nullptr, g.inter, f16);
   Vec up = linear_v(n2, T, D, w.up, nullptr, g.inter, f16);
   Vec act(T * g.inter);
-  for (size_t i = 0; i < act.size(); ++i) act[i] = silu(gate[i]) * up[i];
+  silu_gate(gate, up, act);
   store(act, f16);
   Vec down = linear_v(act, T, g.inter, w.down, nullptr, D, f16);
   add_into(h, down);
@@ -385,7 +458,7 @@ int decoder_layer_decode(Vec& h, const DecoderGeom& g, const float* cos_t, const
   Vec gate = linear_v(n2, 1, D, w.gate, nullptr, g.inter, f16);
   Vec up = linear_v(n2, 1, D, w.up, nullptr, g.inter, f16);
   Vec act(g.inter);
-  for (size_t i = 0; i < act.size(); ++i) act[i] = silu(gate[i]) * up[i];
+  silu_gate(gate, up, act);
   store(act, f16);
   Vec down = linear_v(act, 1, g.inter, w.down, nullptr, D, f16);
   add_into(h, down);
@@ -464,7 +537,7 @@ int vision_encoder(const pvlc_oracle_model_dims& d, const uint16_t* const* vw,
       Vec w = widen(lw[12], I * H), b = widen(lw[13], I);
       f1 = linear_v(n2, n, H, w.data(), b.data(), I, false);
     }
-    for (auto& e : f1) e = gelu_tanh(e);
+    apply(f1, gelu_tanh);
     store(f1, f16);
     {
       Vec w = widen(lw[14], H * I), b = widen(lw[15], H);
@@ -495,7 +568,7 @@ int projector(const pvlc_oracle_model_dims& d, const uint16_t* const* pw, const 
     Vec w = widen(pw[2], M * M), b = widen(pw[3], M);
     l1 = linear_v(merged, m, M, w.data(), b.data(), M, f16);
   }
-  for (auto& e : l1) e = gelu_erf(e);
+  apply(l1, gelu_erf);
   store(l1, f16);
   Vec w2 = widen(pw[4], D * M), b2 = widen(pw[5], D);
   out = linear_v(l1, m, M, w2.data(), b2.data(), D, f16);

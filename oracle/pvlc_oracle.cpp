@@ -101,6 +101,55 @@ inline float dot_rows(const float* a, const float* b, size_t n) {
   return s;
 }
 
+// The same dot as dot_rows (left to right over dims, then `* scale`) for one
+// query row against n keys at once.  Keys are stored transposed,
+// kt[d * ld + key], so that 64 keys' independent sums advance side by side in
+// vector lanes; every score still sees exactly dot_rows' sequence of roundings.
+inline void scaled_scores(const float* q, const float* kt, size_t ld, size_t n, size_t hd,
+                          float scale, float* out) {
+  constexpr size_t B = 64;
+  for (size_t k0 = 0; k0 < n; k0 += B) {
+    float acc[B];
+    for (size_t j = 0; j < B; ++j) acc[j] = 0.0f;
+    if (n - k0 >= B) {
+      for (size_t d = 0; d < hd; ++d) {
+        const float qd = q[d];
+        const float* row = kt + d * ld + k0;
+        for (size_t j = 0; j < B; ++j) acc[j] += qd * row[j];
+      }
+      for (size_t j = 0; j < B; ++j) out[k0 + j] = acc[j] * scale;
+    } else {
+      const size_t nb = n - k0;
+      for (size_t d = 0; d < hd; ++d) {
+        const float qd = q[d];
+        const float* row = kt + d * ld + k0;
+        for (size_t j = 0; j < nb; ++j) acc[j] += qd * row[j];
+      }
+      for (size_t j = 0; j < nb; ++j) out[k0 + j] = acc[j] * scale;
+    }
+  }
+}
+
+// Keys [n][stride] (dims contiguous from `first`) into the transposed form
+// scaled_scores reads: kt[d * n + key].
+inline void transpose_keys(const float* first, size_t stride, size_t n, size_t hd, float* kt) {
+  for (size_t t = 0; t < n; ++t)
+    for (size_t d = 0; d < hd; ++d) kt[d * n + t] = first[t * stride + d];
+}
+
+// out[d] = sum over keys k in ascending order of p[k] * v[k][d], each sum from
+// 0.0 -- the reference's per-dimension weighted-value loop; the dims advance
+// side by side, the order of every sum is unchanged.
+inline void weighted_values(const float* p, const float* v, size_t stride, size_t n, size_t hd,
+                            float* out) {
+  for (size_t d = 0; d < hd; ++d) out[d] = 0.0f;
+  for (size_t k = 0; k < n; ++k) {
+    const float pk = p[k];
+    const float* row = v + k * stride;
+    for (size_t d = 0; d < hd; ++d) out[d] += pk * row[d];
+  }
+}
+
 // One softmax row as the reference computes it: max fold from -inf, exp of
 // (x - max) summed left to right, then divide each by the sum.
 // crates/pvlc-cpu-ref/src/lib.rs:369-422 (softmax_rows_f32, unmasked) and the
@@ -237,8 +286,14 @@ int pvlc_oracle_segmented_attention(const float* query, const float* key, const 
   int st = validate_sequence_boundaries(tokens, cu_seqlens, n_cu);
   if (st) return st;
   const float scale = 1.0f / std::sqrt((float)head_dim);
+  const size_t stride = (size_t)heads * head_dim;
   for (uint32_t seg = 0; seg + 1 < n_cu; ++seg) {
     const size_t start = cu_seqlens[seg], end = cu_seqlens[seg + 1], len = end - start;
+    std::vector<float> kt((size_t)heads * head_dim * len);
+#pragma omp parallel for schedule(static)
+    for (long long h = 0; h < (long long)heads; ++h)
+      transpose_keys(key + attention_index(start, h, 0, heads, head_dim), stride, len, head_dim,
+                     kt.data() + (size_t)h * head_dim * len);
 #pragma omp parallel
     {
       std::vector<float> row(len);
@@ -247,17 +302,12 @@ int pvlc_oracle_segmented_attention(const float* query, const float* key, const 
         for (long long qo = 0; qo < (long long)len; ++qo) {
           const size_t qt = start + qo;
           const float* qrow = query + attention_index(qt, h, 0, heads, head_dim);
-          for (size_t ko = 0; ko < len; ++ko)
-            row[ko] = dot_rows(qrow, key + attention_index(start + ko, h, 0, heads, head_dim),
-                               head_dim) * scale;
+          scaled_scores(qrow, kt.data() + (size_t)h * head_dim * len, len, len, head_dim, scale,
+                        row.data());
           softmax_row(row.data(), len);
-          float* orow = out + attention_index(qt, h, 0, heads, head_dim);
-          for (size_t d = 0; d < head_dim; ++d) {
-            float acc = 0.0f;
-            for (size_t ko = 0; ko < len; ++ko)
-              acc += row[ko] * value[attention_index(start + ko, h, d, heads, head_dim)];
-            orow[d] = acc;
-          }
+          weighted_values(row.data(), value + attention_index(start, h, 0, heads, head_dim),
+                          stride, len, head_dim,
+                          out + attention_index(qt, h, 0, heads, head_dim));
         }
     }
   }
@@ -427,6 +477,11 @@ int pvlc_oracle_causal_gqa(const float* query, const float* key, const float* va
     return ORC_NON_FINITE_INPUT;
   const size_t group = query_heads / kv_heads;
   const float scale = 1.0f / std::sqrt((float)head_dim);
+  const size_t kstride = (size_t)kv_heads * head_dim;
+  std::vector<float> kt((size_t)kv_heads * head_dim * tokens);
+  for (size_t g = 0; g < kv_heads; ++g)
+    transpose_keys(key + g * head_dim, kstride, tokens, head_dim,
+                   kt.data() + g * head_dim * tokens);
 #pragma omp parallel
   {
     std::vector<float> p(tokens);
@@ -436,17 +491,11 @@ int pvlc_oracle_causal_gqa(const float* query, const float* key, const float* va
         const size_t kvh = h / group;
         const float* qrow = query + attention_index(qt, h, 0, query_heads, head_dim);
         const size_t n = qt + 1;
-        for (size_t kt = 0; kt < n; ++kt)
-          p[kt] = dot_rows(qrow, key + attention_index(kt, kvh, 0, kv_heads, head_dim), head_dim) *
-                  scale;
+        scaled_scores(qrow, kt.data() + kvh * head_dim * tokens, tokens, n, head_dim, scale,
+                      p.data());
         softmax_row(p.data(), n);
-        float* orow = out + attention_index(qt, h, 0, query_heads, head_dim);
-        for (size_t d = 0; d < head_dim; ++d) {
-          float w = 0.0f;
-          for (size_t kt = 0; kt < n; ++kt)
-            w += p[kt] * value[attention_index(kt, kvh, d, kv_heads, head_dim)];
-          orow[d] = w;
-        }
+        weighted_values(p.data(), value + kvh * head_dim, kstride, n, head_dim,
+                        out + attention_index(qt, h, 0, query_heads, head_dim));
       }
   }
   return ORC_OK;
@@ -466,6 +515,11 @@ int pvlc_oracle_decode_gqa(const float* query, const float* key, const float* va
     return ORC_NON_FINITE_INPUT;
   const size_t group = query_heads / kv_heads;
   const float scale = 1.0f / std::sqrt((float)head_dim);
+  const size_t kstride = (size_t)kv_heads * head_dim;
+  std::vector<float> kt((size_t)kv_heads * head_dim * cache_tokens);
+  for (size_t g = 0; g < kv_heads; ++g)
+    transpose_keys(key + g * head_dim, kstride, cache_tokens, head_dim,
+                   kt.data() + g * head_dim * cache_tokens);
 #pragma omp parallel
   {
     std::vector<float> p(cache_tokens);
@@ -473,16 +527,11 @@ int pvlc_oracle_decode_gqa(const float* query, const float* key, const float* va
     for (long long h = 0; h < (long long)query_heads; ++h) {
       const size_t kvh = h / group;
       const float* qrow = query + (size_t)h * head_dim;
-      for (size_t kt = 0; kt < cache_tokens; ++kt)
-        p[kt] = dot_rows(qrow, key + attention_index(kt, kvh, 0, kv_heads, head_dim), head_dim) *
-                scale;
+      scaled_scores(qrow, kt.data() + kvh * head_dim * cache_tokens, cache_tokens, cache_tokens,
+                    head_dim, scale, p.data());
       softmax_row(p.data(), cache_tokens);
-      for (size_t d = 0; d < head_dim; ++d) {
-        float w = 0.0f;
-        for (size_t kt = 0; kt < cache_tokens; ++kt)
-          w += p[kt] * value[attention_index(kt, kvh, d, kv_heads, head_dim)];
-        out[(size_t)h * head_dim + d] = w;
-      }
+      weighted_values(p.data(), value + kvh * head_dim, kstride, cache_tokens, head_dim,
+                      out + (size_t)h * head_dim);
     }
   }
   return ORC_OK;
