@@ -228,8 +228,10 @@ int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
  *   - batch may not exceed PVLC_DECODE_NOALLOC_MAX_BATCH; a larger batch (or a
  *     device whose SM count needs more scratch) returns
  *     PVLC_WORKSPACE_TOO_SMALL before any device effect.
- *   - The first call on each device looks up the array's device address (with
- *     that device current); make that first call before any stream capture.
+ *   - Every call looks up the array's device address on the current device
+ *     (a host-only query); the first call on a device may also load the
+ *     library's device code there, so make that first call before any stream
+ *     capture.
  *   - The call makes no cudaMalloc/cudaFree or other allocation; it clears the
  *     array's flag and ticket words on `stream` before the kernel.
  *   - All calls share the one array: calls that may overlap on the GPU (other

@@ -862,15 +862,8 @@ size_t decode_workspace_bytes(uint32_t batch, int num_sms) {
 }
 
 int decode_launch(const DecodeArgs& a, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(decode::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             decode::SMEM_BYTES) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
-    attr_set[dev] = true;
-  }
+  if (set_smem_attribute_once(reinterpret_cast<const void*>(decode::decode_kernel), decode::SMEM_BYTES) != PVLC_OK)
+    return PVLC_CUDA_ERROR;
   decode::Params p;
   p.q = reinterpret_cast<const __half*>(a.q);
   p.k_new = reinterpret_cast<const __half*>(a.k_new);
@@ -918,25 +911,16 @@ namespace {
 
 __device__ __align__(256) uint8_t g_decode_noalloc_scratch[PVLC_DECODE_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mutex;
-void* g_noalloc_scratch_ptr[kMaxDevices] = {};
-
 // Device address of the scratch array on the current device.  In host code
 // `g_decode_noalloc_scratch` names a host-side stand-in, never the device
-// memory, so the address is looked up once per device (with that device
-// current) and cached.
+// memory, so the address is asked for on every call, with the device current:
+// a host-only lookup that stays right if the context is ever re-created
+// (cudaDeviceReset reloads the module, possibly elsewhere).
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return PVLC_CUDA_ERROR;
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_scratch_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch) != cudaSuccess || ptr == nullptr)
-      return PVLC_CUDA_ERROR;
-    g_noalloc_scratch_ptr[dev] = ptr;
-  }
-  *out = g_noalloc_scratch_ptr[dev];
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+    return PVLC_CUDA_ERROR;
+  *out = ptr;
   return PVLC_OK;
 }
 

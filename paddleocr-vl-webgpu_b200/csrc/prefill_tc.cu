@@ -766,15 +766,8 @@ bool make_cache_map(CUtensorMap* m, const void* base, uint32_t capacity, uint32_
 template <int MAXB>
 int launch(const void* q, const void* k, const void* v, uint32_t rows, const Prompts<MAXB>& pr,
            Params p, uint32_t capacity, uint32_t grid_y, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(prefill_attn_kernel<MAXB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             SMEM_BYTES) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
-    attr_set[dev] = true;
-  }
+  if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_attn_kernel<MAXB>), SMEM_BYTES) != PVLC_OK)
+    return PVLC_CUDA_ERROR;
   if (grid_y == 0 || grid_y > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
   Maps maps;
   // keys come from the caches (rotated by kv_rope_kernel): rows past a

@@ -17,6 +17,49 @@
 
 namespace pvlc {
 
+// The current CUDA context (the driver's cuCtxGetCurrent, looked up once
+// through the runtime), or nullptr when it cannot be read.
+static void* current_context() {
+  using GetCurrent = int (*)(void**);
+  static GetCurrent fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetCurrent>(ptr);
+  });
+  void* ctx = nullptr;
+  if (!fn || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
+int set_smem_attribute_once(const void* kernel, int smem_bytes) {
+  // One entry per (kernel, device) holding the context the attribute was set
+  // in: an attribute belongs to its context, so the context that follows a
+  // cudaDeviceReset gets it again.  The mutex covers concurrent first calls
+  // from several threads.
+  struct Entry { const void* kernel; int dev; void* ctx; };
+  static std::mutex mu;
+  static Entry done[256];
+  static int n_done = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
+  void* ctx = current_context();
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* e = nullptr;
+  for (int i = 0; i < n_done; ++i)
+    if (done[i].kernel == kernel && done[i].dev == dev) e = &done[i];
+  if (e && ctx && e->ctx == ctx) return PVLC_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) !=
+      cudaSuccess)
+    return PVLC_CUDA_ERROR;
+  if (!e && n_done < 256) e = &done[n_done++];
+  if (e) *e = Entry{kernel, dev, ctx};
+  return PVLC_OK;
+}
+
 int device_sm_count() {
   static int cached[64] = {};
   int dev = 0;

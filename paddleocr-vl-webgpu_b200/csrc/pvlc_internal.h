@@ -88,5 +88,8 @@ int prefill_block_threads();
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream);
 
 int device_sm_count();
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, smem_bytes) once per
+// kernel, device and context (thread-safe); a PVLC_* status.
+int set_smem_attribute_once(const void* kernel, int smem_bytes);
 
 }  // namespace pvlc

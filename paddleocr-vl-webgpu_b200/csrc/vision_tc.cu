@@ -526,15 +526,8 @@ size_t vision_workspace_bytes(uint32_t tokens, uint32_t heads) {
 
 int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, void* workspace,
                   cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return PVLC_CUDA_ERROR;
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(vtc::vision_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             vtc::SMEM_BYTES) != cudaSuccess)
-      return PVLC_CUDA_ERROR;
-    attr_set[dev] = true;
-  }
+  if (set_smem_attribute_once(reinterpret_cast<const void*>(vtc::vision_tc_kernel), vtc::SMEM_BYTES) != PVLC_OK)
+    return PVLC_CUDA_ERROR;
   // rotated q and k (the scratch) or the inputs themselves when there is no RoPE
   const void* qa = a.q;
   const void* ka = a.k;

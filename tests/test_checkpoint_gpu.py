@@ -170,6 +170,25 @@ def test_load_weights_is_bit_exact_and_drives_the_engine(cuda_lib, tmp_path):
     assert ta == tb and len(ta[0]) >= 1
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible GPUs")
+def test_load_onto_a_device_that_is_not_current(cuda_lib, tmp_path):
+    """cuda:0 stays current while the weights go to cuda:1: the conversion kernels
+    must run on cuda:1 (the loader makes it current around its launches), the
+    result must live there and be bit-exact."""
+    path = tmp_path / "small.safetensors"
+    src = _write_checkpoint(path, SMALL, seed=3)
+    torch.cuda.set_device(0)
+    w = C.load_weights(path, SMALL, device="cuda:1", chunk_bytes=8 << 20)
+    assert torch.cuda.current_device() == 0
+    names = sum(C.engine_tensor_names(SMALL), [])
+    for name, got in zip(names, w.vision + w.projector + w.decoder):
+        assert got.device == torch.device("cuda:1"), name
+        ref = src[name].to(torch.float16).reshape(got.shape).to("cuda:1")
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), name
+    blob = C.load_payload_f16(C.SafetensorsCatalog.open(path), "cuda:1")
+    assert blob.device == torch.device("cuda:1")
+
+
 def test_load_weights_names_the_first_rejected_element(cuda_lib, tmp_path):
     path = tmp_path / "poisoned.safetensors"
     _write_checkpoint(path, SMALL, seed=2,
