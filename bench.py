@@ -610,11 +610,7 @@ def run_e2e(args, dev, rank, world, dist):
     weights = M.init_weights(cfg, seed=0, device=dev)
     eng = M.OcrEngine(cfg, weights, dev)
     mine = pdist.shard(args.e2e_requests, rank, world)
-    pages = []
-    for i in mine:
-        rng = np.random.default_rng(10_000 + i)
-        pages.append(torch.from_numpy(
-            rng.integers(0, 256, (1024, 1024, 3), dtype=np.uint8)).pin_memory())
+    pages = [request_page(i, pin=True) for i in mine]
 
     def barrier():
         if dist is not None:
@@ -651,6 +647,13 @@ def run_e2e(args, dev, rank, world, dist):
         dist.all_reduce(n, op=dist.ReduceOp.SUM)
     ms_max = float(t.item())
     tokens_all, reqs_all, eos_all = (int(x) for x in n.tolist())
+    # after the timed region: every request's token ids and every rank's phase times
+    # to rank 0 (NCCL all-gather of a fixed-size id block per rank, then a small object
+    # gather), the only cross-GPU traffic of the run
+    gathered = pdist.gather_token_ids(res["tokens"], args.e2e_requests, args.e2e_tokens, dev)
+    phases = dict(rank=rank, ms=round(ms, 2), requests=len(mine),
+                  **{k: (round(v, 2) if isinstance(v, float) else v) for k, v in timings.items()})
+    per_rank = pdist.gather_to_rank0(phases) if dist is not None else [phases]
     out = {"workload": "configs[4] e2e greedy OCR, random-init fp16 PaddleOCR-VL, 1024x1024 "
                        "noise pages -> 980x980 (1225 image tokens), OCR prompt",
            "requests": reqs_all, "max_new_tokens": args.e2e_tokens, "n_gpus": world,
@@ -661,13 +664,38 @@ def run_e2e(args, dev, rank, world, dist):
            "rank0_breakdown_ms": {k: (round(v, 2) if isinstance(v, float) else v)
                                   for k, v in timings.items()},
            "h2d_bytes_per_request": 1024 * 1024 * 3,
+           "decode_batch_per_gpu": len(mine),
+           "per_rank": per_rank,
            "clocks": clocks,
            "path": "pvlc_b200.model.OcrEngine.recognize (host pages in, token ids out)"}
+    if rank == 0:
+        out["tokens_digest"] = pdist.tokens_digest(gathered)
+        # the gathered ids of a sample of requests -- the first one of every rank's shard
+        # (at one GPU the first eight) -- against the same requests run again on rank 0
+        # as one batch of their own
+        sample = list(range(min(args.e2e_requests, max(world, 8))))
+        again = eng.recognize([request_page(i, pin=True) for i in sample], args.e2e_tokens)
+        same = [i for i, toks in zip(sample, again["tokens"])
+                if [int(x) for x in toks] == gathered[i]]
+        out["rerun_check"] = {"requests": sample, "identical": len(same),
+                              "rerun_batch": len(sample),
+                              "mismatched": [i for i in sample if i not in same]}
+    if dist is not None:
+        dist.barrier()
     if rank == 0 and not args.skip_cpu:
         out["cpu_baseline"] = cpu_e2e_baseline(cfg, weights)
     del eng, weights
     torch.cuda.empty_cache()
     return out
+
+
+def request_page(i, pin=False):
+    """configs[4] request i: a seeded uniform-noise 1024x1024 RGB page (host memory)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(10_000 + i)
+    t = torch.from_numpy(rng.integers(0, 256, (1024, 1024, 3), dtype=np.uint8))
+    return t.pin_memory() if pin else t
 
 
 # --------------------------------------------------------------- CPU (oracle)

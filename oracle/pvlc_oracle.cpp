@@ -131,10 +131,16 @@ inline void scaled_scores(const float* q, const float* kt, size_t ld, size_t n, 
 }
 
 // Keys [n][stride] (dims contiguous from `first`) into the transposed form
-// scaled_scores reads: kt[d * n + key].
+// scaled_scores reads: kt[d * n + key].  Called outside parallel regions; the
+// copy itself is split across threads by key blocks.
 inline void transpose_keys(const float* first, size_t stride, size_t n, size_t hd, float* kt) {
-  for (size_t t = 0; t < n; ++t)
-    for (size_t d = 0; d < hd; ++d) kt[d * n + t] = first[t * stride + d];
+  const long long blocks = (long long)((n + 255) / 256);
+#pragma omp parallel for schedule(static) if (n >= 2048)
+  for (long long b = 0; b < blocks; ++b) {
+    const size_t t1 = std::min(n, (size_t)(b + 1) * 256);
+    for (size_t t = (size_t)b * 256; t < t1; ++t)
+      for (size_t d = 0; d < hd; ++d) kt[d * n + t] = first[t * stride + d];
+  }
 }
 
 // out[d] = sum over keys k in ascending order of p[k] * v[k][d], each sum from
@@ -290,7 +296,6 @@ int pvlc_oracle_segmented_attention(const float* query, const float* key, const 
   for (uint32_t seg = 0; seg + 1 < n_cu; ++seg) {
     const size_t start = cu_seqlens[seg], end = cu_seqlens[seg + 1], len = end - start;
     std::vector<float> kt((size_t)heads * head_dim * len);
-#pragma omp parallel for schedule(static)
     for (long long h = 0; h < (long long)heads; ++h)
       transpose_keys(key + attention_index(start, h, 0, heads, head_dim), stride, len, head_dim,
                      kt.data() + (size_t)h * head_dim * len);

@@ -91,3 +91,48 @@ def run_sharded(n_requests: int, work, rank: int, world: int):
     if sorted(merged) != list(range(n_requests)):
         raise RuntimeError("gathered results do not cover every request exactly once")
     return merged
+
+
+def gather_token_ids(tokens, n_requests: int, max_new: int, device=None):
+    """Every rank's generated ids (this rank's shard, in shard order) on rank 0 as
+    {request index: [ids]}; None on the other ranks.  One all-gather of a fixed-size
+    [ceil(n / world), 1 + max_new] int32 block per rank (length, ids, -1 padding), so the
+    collective has the same shape on every rank."""
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    rows = (n_requests + world - 1) // world
+    block = torch.full((rows, 1 + max_new), -1, dtype=torch.int32)
+    for j, toks in enumerate(tokens):
+        ids = [int(x) for x in toks]
+        if len(ids) > max_new or j >= rows:
+            raise ValueError("more tokens or requests than the gather block holds")
+        block[j, 0] = len(ids)
+        block[j, 1:1 + len(ids)] = torch.tensor(ids, dtype=torch.int32)
+    block = block.to(device) if device is not None else block
+    if world == 1:
+        parts = [block]
+    else:
+        parts = [torch.empty_like(block) for _ in range(world)]
+        dist.all_gather(parts, block)
+    if rank != 0:
+        return None
+    out = {}
+    for r, part in enumerate(parts):
+        part = part.cpu()
+        for j, i in enumerate(shard(n_requests, r, world)):
+            n = int(part[j, 0])
+            out[i] = [int(x) for x in part[j, 1:1 + n]]
+    return out
+
+
+def tokens_digest(by_request) -> str:
+    """sha256 (first 16 hex digits) over every request's ids in request order: equal for
+    any GPU count as long as a request's tokens do not depend on how requests are
+    batched."""
+    import hashlib
+    h = hashlib.sha256()
+    for i in sorted(by_request):
+        h.update(int(i).to_bytes(4, "little") + len(by_request[i]).to_bytes(4, "little"))
+        for t in by_request[i]:
+            h.update(int(t).to_bytes(4, "little", signed=True))
+    return h.hexdigest()[:16]

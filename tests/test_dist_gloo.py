@@ -49,6 +49,13 @@ def _worker(rank, world, port, mode, result_q):
     try:
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure on rank 1")
+        if mode == "tokens":
+            # 5 requests over 2 ranks (shards of 3 and 2); request i emits i + 1 ids
+            mine = pd.shard(5, rank, world)
+            toks = [[100 * i + j for j in range(i + 1)] for i in mine]
+            merged = pd.gather_token_ids(toks, 5, 8)
+            result_q.put((rank, "ok", merged, None))
+            return
         merged = pd.run_sharded(6, _request, rank, world)
         t = pd.max_over_ranks(float(rank + 1))
         result_q.put((rank, "ok", merged, t))
@@ -100,3 +107,17 @@ def test_failed_rank_ends_the_peer_collective_with_an_error():
     assert res[1][0] == "error" and "injected failure" in res[1][1]
     # rank 0 must not hang: its gather fails once rank 1 is gone
     assert res[0][0] == "error"
+
+
+def test_token_ids_gather_to_rank0_by_request_index():
+    sys.path.insert(0, os.path.join(ROOT, "paddleocr-vl-webgpu_b200"))
+    from pvlc_b200 import dist as pd
+    res = _run("tokens")
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    expected = {i: [100 * i + j for j in range(i + 1)] for i in range(5)}
+    assert res[0][1] == expected and res[1][1] is None
+    # one process gives the same gather and digest
+    single = pd.gather_token_ids([expected[i] for i in range(5)], 5, 8)
+    assert single == expected
+    assert pd.tokens_digest(single) == pd.tokens_digest(res[0][1])
+    assert pd.tokens_digest({0: [1]}) != pd.tokens_digest({0: [1, 2]})

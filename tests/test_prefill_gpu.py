@@ -25,7 +25,7 @@ def image_prompt(prefix_text, grid_hw_merged, suffix_text):
     return ids, [(1, 2 * h, 2 * w)]
 
 
-def _run_case(ids, grids, capacity, seed):
+def _run_case(ids, grids, capacity, seed, plant=None, fp16_rotated=False):
     from pvlc_b200 import ops, positions
     T = len(ids)
     pos, delta = positions.mrope_position_ids(ids, grids)
@@ -34,13 +34,25 @@ def _run_case(ids, grids, capacity, seed):
     assert delta == odelta
     cos, sin = positions.mrope_tables(pos, delta, capacity)
     rng = np.random.default_rng(seed)
-    q = rng.standard_normal((T, QH, HD)).astype(np.float16)
-    k = rng.standard_normal((T, KVH, HD)).astype(np.float16)
+    q = rng.standard_normal((T, QH, HD)).astype(np.float32)
+    k = rng.standard_normal((T, KVH, HD)).astype(np.float32)
     v = rng.standard_normal((T, KVH, HD)).astype(np.float16)
+    if plant is not None:
+        plant(q, k)
+    q, k = q.astype(np.float16), k.astype(np.float16)
     kc_o = np.zeros((capacity, KVH, HD), np.float32)
     vc_o = np.zeros((capacity, KVH, HD), np.float32)
     ref = O.decoder_prefill(q.astype(np.float32), k.astype(np.float32), v.astype(np.float32), cos,
                             sin, T, kc_o, vc_o)
+    if fp16_rotated:
+        # attention over the rotated q and k rounded to fp16, as the fp16 KV cache (and the
+        # staged Q tile) hold them: the reference composition with that storage point
+        kc_o[:T] = kc_o[:T].astype(np.float16).astype(np.float32)
+        qr, _ = O.apply_multimodal_rope(q.astype(np.float32), k.astype(np.float32), T, QH, KVH,
+                                        HD, np.ascontiguousarray(cos[:, :T]),
+                                        np.ascontiguousarray(sin[:, :T]))
+        qr = qr.astype(np.float16).astype(np.float32)
+        ref = O.causal_gqa(qr, kc_o[:T].copy(), v.astype(np.float32), T, QH, KVH, HD)
     dev = torch.device("cuda")
     kc = torch.full((capacity, KVH, HD), float("nan"), dtype=torch.float16, device=dev)
     vc = torch.full((capacity, KVH, HD), float("nan"), dtype=torch.float16, device=dev)
@@ -83,6 +95,32 @@ def test_long_prefill_schedules(cuda_lib, T):
     that keep one wave (1600, 52 light tiles), and split CTAs only, in several waves
     heaviest first, where pairing would outlast the heaviest CTA (1800, 2500, 4100)."""
     _run_case(list(range(3, 3 + T)), [], T + 5, seed=T)
+
+
+def test_lazy_rescale_branch(cuda_lib):
+    """Scores that rise along the keys and jump by more than the kernel's lazy rescale
+    threshold (8 log2 units) twice, at 45 % and 85 % of the prompt, so queries past
+    each jump rescale O in the middle of their key range; query heads alternate the
+    sign of the planted component, so half of them meet their max in the first K
+    tile.  The planted component is dim 63 (partner 127), the M-RoPE's lowest
+    frequency (500000^(-126/128) ~ 2.5e-6 rad a position), so it survives rotation.
+    Planted scores of ~14 nats make the fp16 rounding of the rotated q and k (the fp16
+    cache's storage point) worth ~1e-2 nats a score, so the reference here attends over
+    the rotated operands rounded to fp16: the test isolates the rescale logic."""
+    T = 1800
+    sign = np.where(np.arange(QH) % 2 == 0, 1.0, -1.0).astype(np.float32)
+
+    def plant(q, k):
+        q *= 0.25
+        k *= 0.25
+        q[:, :, 63] = (8.0 * sign)[None, :]
+        k[:, :, 63] = np.linspace(-2.0, 6.0, T, dtype=np.float32)[:, None]
+        k[int(0.45 * T):int(0.45 * T) + 32, :, 63] = 10.0
+        k[int(0.85 * T):int(0.85 * T) + 64, :, 63] = 20.0
+
+    per_unit = 8.0 / np.sqrt(128.0) * np.log2(np.e)
+    assert (10.0 - (-2.0)) * per_unit > 8.0 and (20.0 - 10.0) * per_unit > 8.0
+    _run_case(list(range(3, 3 + T)), [], T + 4, seed=17, plant=plant, fp16_rotated=True)
 
 
 def test_packed_prompts_match_single_calls(cuda_lib):

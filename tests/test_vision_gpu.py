@@ -89,26 +89,76 @@ def test_packed_images_with_rope(cuda_lib, grids):
     assert err <= ATOL, f"max abs err {err}"
 
 
-def test_config2_shape_sampled(cuda_lib):
-    """BASELINE config 2 geometry (8000 tokens, segments 1024/2304/576/4096) with RoPE;
-    the oracle checks every row of the two shorter images and a strided row sample."""
+def _rope_case(grids, seed):
     from pvlc_b200 import positions
-    grids = [(1, 32, 32), (1, 48, 48), (1, 24, 24), (1, 64, 64)]
-    cu = [0, 1024, 3328, 3904, 8000]
-    T = 8000
-    rng = np.random.default_rng(2)
+    lens = [t * h * w for t, h, w in grids]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32).tolist()
+    T = cu[-1]
+    rng = np.random.default_rng(seed)
     q = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
     k = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
     v = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
     cos, sin = positions.vision_rope_tables(grids)
+    return cu, T, q, k, v, cos, sin
+
+
+def _check_every_segment(got, q, k, v, cu, cos, sin):
+    T = cu[-1]
+    qr, kr = O.vision_rope_apply_tables(q, k, T, H, D, cos, sin)
+    ref = O.segmented_attention(qr, kr, v, T, H, D, cu).reshape(T, H, D)
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        err = float(np.abs(got[a:b] - ref[a:b]).max())
+        assert err <= ATOL, f"segment {s} ({b - a} tokens) err {err}"
+
+
+def test_config2_shape_every_segment(cuda_lib):
+    """BASELINE config 2 geometry (8000 tokens, segments 1024/2304/576/4096, 2-D RoPE):
+    every row of every segment against the oracle."""
+    grids = [(1, 32, 32), (1, 48, 48), (1, 24, 24), (1, 64, 64)]
+    cu, T, q, k, v, cos, sin = _rope_case(grids, 2)
+    assert cu == [0, 1024, 3328, 3904, 8000]
     got = _gpu(q, k, v, cu, cos, sin)
     assert np.isfinite(got).all()
-    qr, kr = O.vision_rope_apply_tables(q, k, T, H, D, cos, sin)
-    for s in (0, 2):
-        a, b = cu[s], cu[s + 1]
-        ref = O.segmented_attention(qr[a:b], kr[a:b], v[a:b], b - a, H, D, [0, b - a])
-        err = np.abs(got[a:b] - ref.reshape(b - a, H, D)).max()
-        assert err <= ATOL, f"segment {s} err {err}"
+    _check_every_segment(got, q, k, v, cu, cos, sin)
+
+
+def test_e2e_page_segment(cuda_lib):
+    """The end-to-end engine's page: a 1024x1024 image resized to 980x980 is one
+    70x70 = 4900-patch segment (39 K tiles), packed after a short one; every row."""
+    grids = [(1, 70, 70), (1, 5, 7)]
+    cu, T, q, k, v, cos, sin = _rope_case(grids, 44)
+    got = _gpu(q, k, v, cu, cos, sin)
+    _check_every_segment(got, q, k, v, cu, cos, sin)
+
+
+def test_lazy_rescale_branch(cuda_lib):
+    """Scores that rise along the keys and jump by more than the kernel's lazy rescale
+    threshold (8 log2 units) twice, in the middle and late in a segment, so the
+    running max moves and O is rescaled mid-segment; heads alternate the sign of the
+    query's planted component, so half of them meet their max in the first K tile and
+    only see P far below 1 afterwards.  The planted component is dim 35 of head_dim 72:
+    a column-position pair at the 2-D RoPE's lowest frequency (~1.7e-4 rad a patch).
+    The 3000-patch image is one column wide, so dim 35 is not rotated there at all; in
+    the 40x50 image it turns by at most 49 patches' worth."""
+    grids = [(1, 3000, 1), (1, 40, 50)]
+    cu, T, q, k, v, cos, sin = _rope_case(grids, 9)
+    q *= 0.25
+    k *= 0.25
+    sign = np.where(np.arange(H) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    q[:, :, 35] = (6.0 * sign)[None, :]
+    for a, b in ((cu[0], cu[1]), (cu[1], cu[2])):
+        n = b - a
+        k[a:b, :, 35] = np.linspace(-2.0, 6.0, n, dtype=np.float32)[:, None]
+        k[a + int(0.45 * n):a + int(0.45 * n) + 32, :, 35] = 10.0
+        k[a + int(0.85 * n):a + int(0.85 * n) + 64, :, 35] = 20.0
+    q, k = (x.astype(np.float16).astype(np.float32) for x in (q, k))
+    # a planted key value x gives a score of about 6 x / sqrt(72) nats = 1.02 x log2 units
+    per_unit = 6.0 / np.sqrt(72.0) * np.log2(np.e)
+    assert (10.0 - (-2.0)) * per_unit > 8.0 and (20.0 - 10.0) * per_unit > 8.0
+    got = _gpu(q, k, v, cu, cos, sin)
+    assert np.isfinite(got).all()
+    _check_every_segment(got, q, k, v, cu, cos, sin)
 
 
 def test_vision_validation_errors(cuda_lib):
@@ -146,7 +196,7 @@ def test_workspace_entry_points_agree(cuda_lib):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     need = ops.vision_workspace_bytes(T, H)
-    assert need == 2 * T * H * D * 2
+    assert need == T * H * D * 2
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     f = abi.lib().pvlc_attn_vision_varlen_ws
     args = (P(q), P(k), P(v), cu.ctypes.data_as(ctypes.c_void_p), 2, T, H, D, P(c), P(s))
