@@ -358,8 +358,10 @@ def run_gpu(args, rank, world, local_rank, dist):
 
 
 def run_components(args, dev, tf_peak, peak_src,
-                   which=("vision", "prefill", "prefill_batch", "checkpoint"), iters=20, warm=3):
+                   which=("decode_b1", "vision", "prefill", "prefill_batch", "checkpoint"),
+                   iters=20, warm=3):
     import torch
+    cpu = not args.skip_cpu
 
     res = {}
     stream = torch.cuda.current_stream()
@@ -378,10 +380,12 @@ def run_components(args, dev, tf_peak, peak_src,
         torch.cuda.synchronize()
         return a.elapsed_time(b) / iters
 
+    if "decode_b1" in which:
+        res["decode_b1"] = bench_decode_b1(dev, timeit)
     if "vision" in which:
-        res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src)
+        res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src, cpu)
     if "prefill" in which:
-        res["decoder_prefill"] = bench_prefill(dev, timeit, tf_peak, peak_src)
+        res["decoder_prefill"] = bench_prefill(dev, timeit, tf_peak, peak_src, cpu)
     if "prefill_batch" in which:
         res["decoder_prefill_batch"] = bench_prefill_batch(dev, timeit, tf_peak, peak_src)
     if "checkpoint" in which:
@@ -472,7 +476,111 @@ def bench_checkpoint(dev, timeit):
     return res
 
 
-def bench_vision(dev, timeit, tf_peak, peak_src):
+def bench_decode_b1(dev, timeit):
+    """one decode call at batch 1 -- q [16,128], 1023 cached K/V rows + the
+    appended one (1024 rows after the append), 1,056,768 algorithmic bytes per call.
+    Calls rotate over 256 independent caches (272 MB, more than L2), so every call reads
+    its cache from HBM."""
+    import torch
+
+    from pvlc_b200 import ops, positions
+    hbm_peak, _, peak_src = peaks()
+    n_sets, L, cap = 256, 1023, 1040
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    kc = torch.randn((n_sets, cap, KVH, HD), generator=g, device=dev).half()
+    vc = torch.randn((n_sets, cap, KVH, HD), generator=g, device=dev).half()
+    q = torch.randn((n_sets, 1, QH, HD), generator=g, device=dev).half()
+    kn = torch.randn((n_sets, 1, KVH, HD), generator=g, device=dev).half()
+    vn = torch.randn((n_sets, 1, KVH, HD), generator=g, device=dev).half()
+    kp = [torch.tensor([kc[i].data_ptr()], dtype=torch.int64, device=dev) for i in range(n_sets)]
+    vp = [torch.tensor([vc[i].data_ptr()], dtype=torch.int64, device=dev) for i in range(n_sets)]
+    cos_np, sin_np = positions.linear_rope_tables(cap)
+    cos, sin = torch.from_numpy(cos_np).to(dev), torch.from_numpy(sin_np).to(dev)
+    ct = torch.tensor([L], dtype=torch.int32, device=dev)
+    ws = ops.DecodeWorkspace(1, dev)
+    out = torch.empty((1, QH, HD), dtype=torch.float16, device=dev)
+    it = [0]
+
+    def call():
+        i = it[0] % n_sets
+        it[0] += 1
+        # the same row is appended again each time the set comes round: same bytes
+        ops.decode(q[i], kn[i], vn[i], cos, sin, kp[i], vp[i], ct, cap, L, ws, out=out)
+
+    ms = timeit(call)
+    if ws.errors():
+        raise RuntimeError("decode fault flags in the batch-1 component")
+    nbytes = 2 * (L + 1) * KVH * HD * 2 + 2 * QH * HD * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": "configs[0] decode, batch 1, Q16/KV2/D128, 1024 K/V rows after the "
+                        "append, 256 rotating caches (> L2)",
+            "ms": round(ms, 5), "value": round(gbs, 1), "unit": "GB/s",
+            "algorithmic_bytes": nbytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                         "peak_source": peak_src},
+            "note": "1 MB per call: launch and pipeline latency, not bandwidth, set the time",
+            "kernel": "pvlc::decode::decode_kernel"}
+
+
+def cpu_attention_baseline(kind, args_np, flops):
+    """The oracle (C++ restatement of pvlc-cpu-ref) on the full component workload, on the
+    host cores; returns the cpu_baseline record in TFLOP/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    t0 = time.perf_counter()
+    if kind == "vision":
+        q, k, v, T, cu, c, s_ = args_np
+        qr, kr = O.vision_rope_apply_tables(q, k, T, 16, 72, c, s_)
+        O.segmented_attention(qr, kr, v, T, 16, 72, cu)
+        what = "vision_rope_2d (tables) + materialized_segmented_attention_f32, all 8000 tokens"
+    else:
+        q, k, v, T, c, s_, cap = args_np
+        import numpy as np
+        kc = np.zeros((cap, 2, 128), np.float32)
+        vc = np.zeros_like(kc)
+        O.decoder_prefill(q, k, v, c, s_, T, kc, vc)
+        what = "apply_multimodal_rope_f32 + KV write + causal_gqa_f32, all 1564 tokens"
+    el = time.perf_counter() - t0
+    return {"value": round(flops / el / 1e12, 5), "unit": "TFLOP/s", "cores": O.threads(),
+            "kind": "port", "sample": f"the full workload once ({what}), {el:.2f} s"}
+
+
+def library_sdpa(dev, q, k, v, causal, gqa, segments=None):
+    """Context only: the same attention through torch's scaled_dot_product_attention
+    (cuDNN's fused attention where torch picks it), on pre-rotated inputs; not this
+    library's code.  Returns ms per call or an error string."""
+    import torch
+    import torch.nn.functional as F
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        segs = segments or [(0, q.shape[0])]
+        qs = [q[a:b].transpose(0, 1).unsqueeze(0) for a, b in segs]
+        ks = [k[a:b].transpose(0, 1).unsqueeze(0) for a, b in segs]
+        vs = [v[a:b].transpose(0, 1).unsqueeze(0) for a, b in segs]
+
+        def run():
+            for x, y, z in zip(qs, ks, vs):
+                F.scaled_dot_product_attention(x, y, z, is_causal=causal, enable_gqa=gqa)
+
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                          SDPBackend.EFFICIENT_ATTENTION]):
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(20):
+                run()
+            b.record()
+            torch.cuda.synchronize()
+        return a.elapsed_time(b) / 20
+    except Exception as e:   # noqa: BLE001 - context figure only
+        return f"{type(e).__name__}: {e}"[:160]
+
+
+def bench_vision(dev, timeit, tf_peak, peak_src, cpu=True):
     """Vision varlen prefill, configs[1]."""
     import torch
 
@@ -500,16 +608,27 @@ def bench_vision(dev, timeit, tf_peak, peak_src):
     ms = timeit(vis)
     flops = 4.0 * 72 * 16 * sum((cu[i + 1] - cu[i]) ** 2 for i in range(4))
     tf = flops / (ms * 1e-3) / 1e12
-    return {"workload": "configs[1] 8000 tokens, segments 1024/2304/576/4096, H16 D72, 2-D RoPE",
-            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
-            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
-                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
-                         "peak_source": peak_src, "traffic": VISION_TC_TRAFFIC_BYTES,
-                         "traffic_kernel": "pvlc::vtc::vision_tc_kernel (ncu, one launch)"},
-            "kernel": "pvlc::vtc::vision_rope_kernel + pvlc::vtc::vision_tc_kernel"}
+    res = {"workload": "configs[1] 8000 tokens, segments 1024/2304/576/4096, H16 D72, 2-D RoPE",
+           "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                        "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                        "peak_source": peak_src, "traffic": VISION_TC_TRAFFIC_BYTES,
+                        "traffic_kernel": "pvlc::vtc::vision_tc_kernel (ncu, one launch)"},
+           "kernel": "pvlc::vtc::vision_rope_kernel + pvlc::vtc::vision_tc_kernel"}
+    lib_ms = library_sdpa(dev, qs[0], ks[0], vs[0], False, False,
+                          [(cu[i], cu[i + 1]) for i in range(4)])
+    res["library_reference"] = {
+        "what": "torch scaled_dot_product_attention per image (4 calls), q/k not rotated",
+        "ms": round(lib_ms, 4) if isinstance(lib_ms, float) else lib_ms,
+        "tflops": round(flops / (lib_ms * 1e-3) / 1e12, 1) if isinstance(lib_ms, float) else None}
+    if cpu:
+        f = lambda t: t.float().cpu().numpy()   # noqa: E731
+        res["cpu_baseline"] = cpu_attention_baseline(
+            "vision", (f(qs[0]), f(ks[0]), f(vs[0]), T, cu, c_np, s_np), flops)
+    return res
 
 
-def bench_prefill(dev, timeit, tf_peak, peak_src):
+def bench_prefill(dev, timeit, tf_peak, peak_src, cpu=True):
     """Decoder causal prefill, configs[2]."""
     import torch
 
@@ -538,13 +657,23 @@ def bench_prefill(dev, timeit, tf_peak, peak_src):
     ms = timeit(pre)
     flops = 4.0 * 128 * 16 * Tp * (Tp + 1) / 2
     tf = flops / (ms * 1e-3) / 1e12
-    return {"workload": "configs[2] T=1564 (20 text + 40x37 image + 64 text), Q16/KV2/D128, M-RoPE",
-            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
-            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
-                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
-                         "peak_source": peak_src, "traffic": PREFILL_ATTN_TRAFFIC_BYTES,
-                         "traffic_kernel": "pvlc::ptc::prefill_attn_kernel (ncu, one launch)"},
-            "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
+    res = {"workload": "configs[2] T=1564 (20 text + 40x37 image + 64 text), Q16/KV2/D128, M-RoPE",
+           "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                        "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                        "peak_source": peak_src, "traffic": PREFILL_ATTN_TRAFFIC_BYTES,
+                        "traffic_kernel": "pvlc::ptc::prefill_attn_kernel (ncu, one launch)"},
+           "kernel": "pvlc::ptc::kv_rope_kernel + pvlc::ptc::prefill_attn_kernel"}
+    lib_ms = library_sdpa(dev, pq[0], pk[0], pv[0], True, True)
+    res["library_reference"] = {
+        "what": "torch scaled_dot_product_attention, causal GQA, q/k not rotated, no cache write",
+        "ms": round(lib_ms, 4) if isinstance(lib_ms, float) else lib_ms,
+        "tflops": round(flops / (lib_ms * 1e-3) / 1e12, 1) if isinstance(lib_ms, float) else None}
+    if cpu:
+        f = lambda t: t.float().cpu().numpy()   # noqa: E731
+        res["cpu_baseline"] = cpu_attention_baseline(
+            "prefill", (f(pq[0]), f(pk[0]), f(pv[0]), Tp, pc, ps, Tp + 256), flops)
+    return res
 
 
 def bench_prefill_batch(dev, timeit, tf_peak, peak_src):
@@ -833,7 +962,8 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true", help="skip configs[4] e2e greedy OCR")
     ap.add_argument("--e2e-requests", type=int, default=256)
     ap.add_argument("--e2e-tokens", type=int, default=512)
-    ap.add_argument("--only", choices=["vision", "prefill", "prefill_batch", "checkpoint", "e2e"],
+    ap.add_argument("--only", choices=["decode_b1", "vision", "prefill", "prefill_batch",
+                                       "checkpoint", "e2e"],
                     default=None,
                     help="time one prefill component alone (profiling runs); prints its line")
     args = ap.parse_args()

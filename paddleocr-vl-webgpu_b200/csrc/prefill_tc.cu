@@ -588,7 +588,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // MUFU operation per two values.  The row sum adds the fp16 P the PV
       // product consumes, in f32, over two accumulator chains.
       const uint64_t negm2 = f2_pack(-mm, -mm);
-      const uint64_t negmh2 = f2_pack(-mm - 0.5f, -mm - 0.5f);
+      const uint64_t negmh2 = f2_pack(6.5f - mm, 6.5f - mm);   // exp2_h2_poly takes x + 6.5
       uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {

@@ -225,21 +225,25 @@ __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
 // 2^x for a pair of f32 exponents, returned as fp16x2 bits, computed on the
 // FMA and integer pipes only (no MUFU, no f32 -> f16 conversion), so that a
 // kernel can split its exponentials between this and ex2_h2.  The argument is
-// xh = x - 0.5 (callers fold the 0.5 into their shift).
-//   j = round-to-nearest(xh) = floor(x), via the 1.5 * 2^23 rounding constant;
-//   g = xh - j in [-0.5, 0.5];
+// xs = x + 6.5 (callers fold the 6.5 into their shift): the fp16 bits of
+// 2^(x + 7) are built first, where x + 7 >= -14 stays in the normal fp16
+// range, and one f16x2 multiply by 2^-7 brings them down, rounding into the
+// subnormal range where 2^x < 2^-14 (gradual underflow, as ex2_h2 gives).
+//   j = round-to-nearest(xs) = floor(x + 7), via the 1.5 * 2^23 rounding constant;
+//   g = xs - j in [-0.5, 0.5];
 //   2^(g + 0.5) by a degree-3 minimax polynomial (relative error 7.5e-5 on
 //   [-0.5, 0.5], Remez exchange), evaluated scaled by 1024 with
 //   2^23 + 15 * 1024 - 1024 added, so the last fused multiply-add rounds the
 //   10-bit fp16 mantissa (plus the exponent bias 15 << 10) into the low bits
 //   of its f32 result; a carry out of the mantissa bumps the exponent, as it
 //   should.  The fp16 exponent j is then added as an integer (j << 10).
-// Results are within one fp16 ulp of 2^x for x >= -14; x <= -15 (and -inf)
-// gives exactly 0 and x in (-15, -14) a value below 2^-14.
-__device__ __forceinline__ uint32_t exp2_h2_poly(uint64_t xh2) {
+// Results are within one fp16 ulp of 2^x for x >= -21 (subnormal ulps below
+// 2^-14); x <= -22 gives exactly 0.  Valid for x <= 8 (2^(x + 7) <= 2^15).
+__device__ __forceinline__ uint32_t exp2_h2_poly(uint64_t xs2) {
   constexpr float kRound = 12582912.f;  // 1.5 * 2^23
   constexpr float kA3 = 79.89711f, kA2 = 351.33844f, kA1 = 1003.94916f, kA0 = 8404392.f;
-  float2 xh = f2_unpack(xh2);
+  constexpr uint32_t kPow2m7x2 = 0x20002000u;   // fp16x2 {2^-7, 2^-7}
+  float2 xh = f2_unpack(xs2);
   xh.x = fmaxf(xh.x, -15.5f);
   xh.y = fmaxf(xh.y, -15.5f);
   const uint64_t x2 = f2_pack(xh.x, xh.y);
@@ -253,7 +257,10 @@ __device__ __forceinline__ uint32_t exp2_h2_poly(uint64_t xh2) {
   asm("mov.b64 {%0, %1}, %2;" : "=r"(t0), "=r"(t1) : "l"(t2));
   asm("mov.b64 {%0, %1}, %2;" : "=r"(q0), "=r"(q1) : "l"(q2));
   // low 16 bits: (j << 10) + (15 << 10) + mantissa; the high halves are dropped
-  return __byte_perm(t0 * 1024u + q0, t1 * 1024u + q1, 0x5410);
+  const uint32_t up = __byte_perm(t0 * 1024u + q0, t1 * 1024u + q1, 0x5410);
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(up), "r"(kPow2m7x2));
+  return r;
 }
 
 // Programmatic dependent launch.  A kernel launched with the programmatic

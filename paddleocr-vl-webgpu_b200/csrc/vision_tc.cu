@@ -423,7 +423,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         // others by scaling in f32, rounding the exponent to fp16 and one
         // MUFU operation per two values
         const uint64_t negm2 = f2_pack(-m_run, -m_run);
-        const uint64_t negmh2 = f2_pack(-m_run - 0.5f, -m_run - 0.5f);
+        const uint64_t negmh2 = f2_pack(6.5f - m_run, 6.5f - m_run);   // exp2_h2_poly takes x + 6.5
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t pk[16];

@@ -196,7 +196,7 @@ def test_workspace_entry_points_agree(cuda_lib):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     need = ops.vision_workspace_bytes(T, H)
-    assert need == T * H * D * 2
+    assert need == 2 * T * H * D * 2
     ws = torch.empty(need, dtype=torch.uint8, device="cuda")
     f = abi.lib().pvlc_attn_vision_varlen_ws
     args = (P(q), P(k), P(v), cu.ctypes.data_as(ctypes.c_void_p), 2, T, H, D, P(c), P(s))
