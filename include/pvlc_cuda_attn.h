@@ -185,6 +185,14 @@ int pvlc_attn_decoder_prefill_batch(const pvlc_half* q, const pvlc_half* k, cons
  *   zeroed once with pvlc_attn_decode_workspace_init before first use; it
  *   is reusable across calls on the same stream without re-initialisation.
  * out: device [batch, 16, 128] fp16.
+ * Ordering: the kernel is launched with programmatic dependent launch, so it
+ *   may start while the kernel ahead of it on `stream` is still finishing; it
+ *   waits for that kernel before touching q, k_new, v_new, the tables, the
+ *   caches, the workspace or out, but it reads cache_tokens, rope_row and the
+ *   two pointer arrays (to plan its split) before that wait.  Those four may
+ *   be written by any earlier stream operation, but not by a kernel launched
+ *   directly ahead of this call that itself allows programmatic dependent
+ *   launch (triggers early); the same holds for the two variants below.
  */
 size_t pvlc_attn_decode_workspace_bytes(uint32_t batch);
 int pvlc_attn_decode_workspace_init(void* workspace, size_t workspace_bytes, void* stream);

@@ -80,6 +80,10 @@ constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]
 #define PVLC_DECODE_END_WEIGHT 4
 #endif
 constexpr uint32_t END_WEIGHT = PVLC_DECODE_END_WEIGHT;
+#ifndef PVLC_DECODE_MIN_TILES_PER_CTA
+#define PVLC_DECODE_MIN_TILES_PER_CTA 4
+#endif
+constexpr uint64_t MIN_TILES_PER_CTA = PVLC_DECODE_MIN_TILES_PER_CTA;
 
 // shared memory map (bytes)
 constexpr int SM_K = 0;
@@ -257,16 +261,20 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const uint32_t B = p.batch;
-  // Programmatic dependent launch: this grid may have been launched before
-  // the preceding kernel of the stream finished; nothing is read before it
-  // has (pdl_wait).  The next launch may then be scheduled early: its CTAs
-  // take an SM as soon as one of this grid's CTAs leaves it.
-  pdl_wait();
+  // Programmatic dependent launch: this grid may start while the kernel ahead
+  // of it on the stream still runs (its CTAs take an SM as soon as one of that
+  // grid's CTAs leaves it), and lets the next launch do the same.  Until
+  // pdl_wait it reads only cache_tokens, rope_row and the two cache-pointer
+  // arrays -- which the kernel ahead does not produce (a documented
+  // condition of the call) -- to build the schedule, and it prefetches into
+  // L2 the first cache tiles of its range and its first sequence's q, table
+  // and new rows: prefetches only warm the cache, so they are harmless even
+  // if that data is still being written.  Everything else waits.
   pdl_launch_dependents();
 
   // ---- schedule: per-sequence tile counts (every thread), then an in-place
   // exclusive prefix sum over them (warp 0)
-  for (uint32_t bb = tid; bb < B; bb += THREADS) tile_off[bb + 1] = seq_tiles(p, bb, blockIdx.x == 0);
+  for (uint32_t bb = tid; bb < B; bb += THREADS) tile_off[bb + 1] = seq_tiles(p, bb, false);
   if (tid == 0) {
     tile_off[0] = 0;
     cost_off[0] = 0;
@@ -321,24 +329,16 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   __syncthreads();
 
   const uint64_t NT = tile_off[B];
-  // Block 0 zero-fills the outputs of sequences that were rejected.
-  if (blockIdx.x == 0) {
-    for (uint32_t b = warp; b < B; b += THREADS / 32) {
-      if (tile_off[b] == tile_off[b + 1]) {
-        uint2* o = reinterpret_cast<uint2*>(p.out + (size_t)b * QH * HD);
-        for (int i = lane; i < QH * HD / 4; i += 32) o[i] = make_uint2(0, 0);
-      }
-    }
-  }
-  if (NT == 0) return;
   // Stream-K split of the cost line: sequence b covers [cost_off[b],
   // cost_off[b+1]) = its tiles, then END_WEIGHT units for its end-merge.  CTA
   // c takes the tiles whose cost positions fall in [c C / G, (c+1) C / G):
   // contiguous, monotone tile ranges that give the CTAs holding sequence ends
   // fewer tiles.  A range inside one allowance is empty.
   const uint64_t C = cost_off[B];
-  const uint64_t G = umin64(gridDim.x, NT);
-  if (blockIdx.x >= G) return;
+  // a small batch (few tiles) uses fewer CTAs, each streaming at least
+  // MIN_TILES_PER_CTA tiles: a one-tile CTA is all latency, and every split
+  // adds a partial record to the sequence's combine
+  const uint64_t G = umax64(1, umin64(gridDim.x, (NT + MIN_TILES_PER_CTA - 1) / MIN_TILES_PER_CTA));
   auto tile_at = [&](uint64_t y) -> uint64_t {   // first tile at cost position >= y
     if (y >= C) return NT;
     uint32_t lo = 0, hi = B;  // invariant: cost_off[lo] <= y < cost_off[hi]
@@ -350,11 +350,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     const uint64_t n = tile_off[lo + 1] - tile_off[lo];
     return u < n ? tile_off[lo] + u : tile_off[lo + 1];
   };
-  const uint64_t t0 = tile_at(blockIdx.x * C / G);
-  const uint64_t t1 = tile_at((blockIdx.x + 1) * C / G);
-  if (t0 == t1) return;
-
-  // first sequence touching t0: last b with tile_off[b] <= t0 < tile_off[b+1]
+  // first sequence touching t: last b with tile_off[b] <= t < tile_off[b+1]
   auto seq_of = [&](uint64_t t) -> uint32_t {
     uint32_t lo = 0, hi = B;  // invariant: tile_off[lo] <= t < tile_off[hi]
     while (hi - lo > 1) {
@@ -363,6 +359,52 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     }
     return lo;
   };
+  const bool active = NT > 0 && blockIdx.x < G;
+  const uint64_t t0 = active ? tile_at(blockIdx.x * C / G) : 0;
+  const uint64_t t1 = active ? tile_at((blockIdx.x + 1) * C / G) : 0;
+  if (t0 < t1 && warp == CONSUMER_WARPS + 1) {
+    // sequence warp: the first sequence's q row (32 lines), table rows (3
+    // planes x cos/sin x 4 lines) and new K/V rows (2 x 4 lines) toward L2;
+    // they are on the consumers' critical path at the start
+    const uint32_t b = seq_of(t0);
+    const uint32_t ct0 = __ldg(p.cache_tokens + b);
+    const uint32_t rr0 = p.rope_row ? __ldg(p.rope_row + b) : ct0;
+    prefetch_l2(reinterpret_cast<const uint8_t*>(p.q + (size_t)b * p.q_stride) + lane * 128);
+    if (lane < 24 && rr0 < p.rope_rows) {
+      const float* tab = (lane & 4) ? p.rope_sin : p.rope_cos;
+      prefetch_l2(reinterpret_cast<const uint8_t*>(tab + ((size_t)(lane >> 3) * p.rope_rows + rr0) * HD) +
+                  (lane & 3) * 128);
+    } else if (lane >= 24) {
+      const __half* nr = (lane & 4) ? p.v_new : p.k_new;
+      prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * p.kv_stride) + (lane & 3) * 128);
+    }
+  } else if (t0 < t1 && warp == CONSUMER_WARPS && lane == 0) {
+    // copy warp: the range's first STAGES tiles (K and V rows) toward L2 with
+    // one bulk prefetch per tile and plane
+    uint32_t b = seq_of(t0);
+    for (uint64_t gt = t0; gt < t1 && gt < t0 + STAGES; ++gt) {
+      while (gt >= tile_off[b + 1]) ++b;
+      const uint32_t L = __ldg(p.cache_tokens + b) + 1;
+      const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
+      const uint32_t n = umin32(TILE, L - row0);
+      const size_t off = (size_t)row0 * ROW_BYTES;
+      prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(p.k_cache[b]) + off, n * ROW_BYTES);
+      prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(p.v_cache[b]) + off, n * ROW_BYTES);
+    }
+  }
+  pdl_wait();
+
+  // Block 0 flags the sequences that were rejected and zero-fills their outputs.
+  if (blockIdx.x == 0) {
+    for (uint32_t b = warp; b < B; b += THREADS / 32) {
+      if (tile_off[b] == tile_off[b + 1]) {
+        if (lane == 0) seq_tiles(p, b, true);
+        uint2* o = reinterpret_cast<uint2*>(p.out + (size_t)b * QH * HD);
+        for (int i = lane; i < QH * HD / 4; i += 32) o[i] = make_uint2(0, 0);
+      }
+    }
+  }
+  if (t0 >= t1) return;
 
   if (warp >= CONSUMER_WARPS) {
     // ======================= producer warps =======================
@@ -432,26 +474,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     } else if (warp == CONSUMER_WARPS + 1) {
       // sequence warp: lane l rotates query head l/2, dims 32(l%2)..+31 and
       // their partners 64 above
-      {
-        // pull the first sequence's q row (32 lines), table rows (3 planes x
-        // cos/sin x 4 lines) and new K/V rows (2 x 4 lines) toward L2, then
-        // release the copy warp
-        const uint32_t ct0 = __ldg(p.cache_tokens + b);
-        const uint32_t rr0 = p.rope_row ? __ldg(p.rope_row + b) : ct0;
-        prefetch_l2(reinterpret_cast<const uint8_t*>(p.q + (size_t)b * p.q_stride) + lane * 128);
-        if (lane < 24 && rr0 < p.rope_rows) {
-          const float* tab = (lane & 4) ? p.rope_sin : p.rope_cos;
-          prefetch_l2(reinterpret_cast<const uint8_t*>(tab + ((size_t)(lane >> 3) * p.rope_rows + rr0) * HD) +
-                      (lane & 3) * 128);
-        } else if (lane >= 24) {
-          const __half* nr = (lane & 4) ? p.v_new : p.k_new;
-          prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * p.kv_stride) + (lane & 3) * 128);
-        }
-        __syncwarp();
-        if (lane == 0) {
-          asm volatile("" ::: "memory");
-          misc[4] = 1;
-        }
+      // the opening prefetches (before the wait) are issued: release the copy warp
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("" ::: "memory");
+        misc[4] = 1;
       }
       uint32_t nseq = 0;
       while (true) {

@@ -91,6 +91,12 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// Bulk L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global
+// address: one instruction for a whole contiguous range.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // ------------------------------------------------------ bulk async copies
 // 1-D bulk copy global -> shared, completion signalled on `bar` (tx bytes).
 // Both addresses 16-byte aligned, bytes a multiple of 16.
