@@ -84,6 +84,14 @@ constexpr uint32_t END_WEIGHT = PVLC_DECODE_END_WEIGHT;
 #define PVLC_DECODE_MIN_TILES_PER_CTA 4
 #endif
 constexpr uint64_t MIN_TILES_PER_CTA = PVLC_DECODE_MIN_TILES_PER_CTA;
+// Tiles of a CTA's range prefetched into L2 before the programmatic-launch wait.
+// Swept on B200 at 64 sequences x 18 layers (0, 2, 3, 5, 10, 16 tiles): 0 is
+// best (0.729 of the copy peak; 5 tiles 0.721, 16 tiles 0.686) -- the early
+// CTAs' prefetches compete with the previous launch's last streaming CTAs.
+#ifndef PVLC_DECODE_PREFETCH_TILES
+#define PVLC_DECODE_PREFETCH_TILES 0
+#endif
+constexpr uint64_t PREFETCH_TILES = PVLC_DECODE_PREFETCH_TILES;
 
 // shared memory map (bytes)
 constexpr int SM_K = 0;
@@ -379,10 +387,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       prefetch_l2(reinterpret_cast<const uint8_t*>(nr + (size_t)b * p.kv_stride) + (lane & 3) * 128);
     }
   } else if (t0 < t1 && warp == CONSUMER_WARPS && lane == 0) {
-    // copy warp: the range's first STAGES tiles (K and V rows) toward L2 with
+    // copy warp: the range's first PREFETCH_TILES tiles (K and V rows) toward L2 with
     // one bulk prefetch per tile and plane
     uint32_t b = seq_of(t0);
-    for (uint64_t gt = t0; gt < t1 && gt < t0 + STAGES; ++gt) {
+    for (uint64_t gt = t0; gt < t1 && gt < t0 + PREFETCH_TILES; ++gt) {
       while (gt >= tile_off[b + 1]) ++b;
       const uint32_t L = __ldg(p.cache_tokens + b) + 1;
       const uint32_t row0 = static_cast<uint32_t>(gt - tile_off[b]) * TILE;
