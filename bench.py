@@ -737,13 +737,32 @@ def bench_prefill_batch(dev, timeit, tf_peak, peak_src):
     ms = timeit(pre)
     flops = B * 4.0 * 128 * 16 * T * (T + 1) / 2
     tf = flops / (ms * 1e-3) / 1e12
-    return {"workload": f"configs[4] decoder prefill, {B} prompts x {T} tokens packed, one "
-                        "launch pair per layer, Q16/KV2/D128, M-RoPE",
-            "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
-            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
-                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
-                         "peak_source": peak_src},
-            "kernel": "pvlc::ptc::kv_rope_kernel<256> + pvlc::ptc::prefill_attn_kernel<256>"}
+    res = {"workload": f"configs[4] decoder prefill, {B} prompts x {T} tokens packed, one "
+                       "launch pair per layer, Q16/KV2/D128, M-RoPE",
+           "ms": round(ms, 4), "value": round(tf, 2), "unit": "TFLOP/s",
+           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
+                        "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
+                        "peak_source": peak_src},
+           "kernel": "pvlc::ptc::kv_rope_kernel<256> + pvlc::ptc::prefill_attn_kernel<256>"}
+    # context: the same causal GQA as one batched torch SDPA call (all prompts have the
+    # same length here, so a [B, heads, T, 128] batch needs no packing)
+    try:
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        qb = q.view(B, T, 16, 128).transpose(1, 2)
+        kb = k.view(B, T, 2, 128).transpose(1, 2)
+        vb = v.view(B, T, 2, 128).transpose(1, 2)
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+                          SDPBackend.EFFICIENT_ATTENTION]):
+            lib_ms = timeit(lambda: F.scaled_dot_product_attention(qb, kb, vb, is_causal=True,
+                                                                   enable_gqa=True))
+        res["library_reference"] = {
+            "what": "torch scaled_dot_product_attention, [256, 16, 1238, 128] causal GQA, q/k "
+                    "not rotated, no cache write",
+            "ms": round(lib_ms, 4), "tflops": round(flops / (lib_ms * 1e-3) / 1e12, 1)}
+    except Exception as e:   # noqa: BLE001 - context figure only
+        res["library_reference"] = {"error": f"{type(e).__name__}: {e}"[:160]}
+    return res
 
 
 def run_e2e(args, dev, rank, world, dist):

@@ -101,6 +101,10 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 #define PVLC_PREFILL_EXP_POLY_MASK 0x4924u
 #endif
 constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
+// 1: the exponent phase as a rolled loop over 32-key chunks (see the softmax)
+#ifndef PVLC_PREFILL_ROLLED
+#define PVLC_PREFILL_ROLLED 1
+#endif
 
 struct Maps {
   // q, v: the packed input rows; k: the KV caches (rotated keys) as
@@ -590,6 +594,38 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t negm2 = f2_pack(-mm, -mm);
       const uint64_t negmh2 = f2_pack(6.5f - mm, 6.5f - mm);   // exp2_h2_poly takes x + 6.5
       uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+#if PVLC_PREFILL_ROLLED
+      // One 32-key chunk per trip of a rolled loop, S reloaded from TMEM (P of
+      // chunk c lands in columns 16c..16c+15, below every chunk still to be
+      // read): a quarter of the code of the unrolled form, which missed in
+      // the instruction cache.
+      const bool diag = j * BN + BN - 1 > warp_tok_lo;
+#pragma unroll 1
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t sc[32];
+        tc::tmem_ld32(tS + 32 * ch, sc);
+        tc::tmem_wait_ld();
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (j * BN + 32 * ch + c > token) sc[c] = __float_as_uint(-CUDART_INF_F);
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const uint64_t s2 = f2_pack(__uint_as_float(sc[2 * c]), __uint_as_float(sc[2 * c + 1]));
+          if ((EXP_POLY_MASK >> c) & 1u) {
+            pk[c] = exp2_h2_poly(f2_fma(s2, scale2, negmh2));
+          } else {
+            const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
+            pk[c] = ex2_h2(pack_half2(x.x, x.y));
+          }
+          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
+          sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
+        }
+        tc::tmem_st16(tS + 16 * ch, pk);
+      }
+#else
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
         uint32_t pk[16];
@@ -608,6 +644,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc::tmem_st16(tS + 16 * ch, pk);
       }
+#endif
       tc::tmem_wait_st();
       const float2 sum = f2_unpack(f2_add(sum2[0], sum2[1]));
       l_run += sum.x + sum.y;

@@ -62,30 +62,51 @@ constexpr int HD = 72;
 constexpr int PAIRS = 36;
 constexpr int QUADS = PAIRS / 4;  // rotation pairs in groups of four (16 bytes of table)
 constexpr int BM = 128;           // rows per Q tile
-constexpr int QT = 2;             // Q tiles per CTA
-constexpr int BN = 128;           // keys per K/V tile
-constexpr int THREADS = 12 * 32;  // 3 warpgroups: softmax 0, softmax 1, producer/MMA/row-sum
-constexpr int CTRL_WARP = 8;      // first warp of the control warpgroup
-// Register split (setmaxnreg) against the registers of the launch: 384
-// threads start with 168 each (65536 / 384 rounded down to the allocation
-// unit of 8).
-constexpr uint32_t REGS_LAUNCH = 168;
-constexpr uint32_t REGS_SOFTMAX = 208, REGS_CTRL = 88;
-static_assert(128 * (2 * REGS_SOFTMAX + REGS_CTRL) <= THREADS * REGS_LAUNCH, "register split");
+// Q tiles per CTA (one softmax warpgroup each) and keys per K/V tile: two
+// tiles of 128 keys (TMEM: 2 x (128 S + 80 O) columns).  Three tiles of 80
+// keys (3 x (80 S + 80 O) = 480 columns, 512 threads) also pass the parity
+// tests but measured slower on configs[1] (174 vs 165 us): the per-step
+// costs (S load, row max, hand-offs, MMA issue) are paid per 80 keys instead
+// of per 128.
+#ifndef PVLC_VISION_QT
+#define PVLC_VISION_QT 2
+#endif
+constexpr int QT = PVLC_VISION_QT;
+static_assert(QT == 2 || QT == 3, "2 or 3 Q tiles per CTA");
+constexpr int BN = QT == 3 ? 80 : 128;
+constexpr int THREADS = (QT + 1) * 128;  // QT softmax warpgroups + producer/MMA/row-sum
+constexpr int CTRL_WARP = 4 * QT;        // first warp of the control warpgroup
+// Register split (setmaxnreg) against the registers of the launch: the
+// launch gives each thread 65536 / THREADS rounded down to the allocation
+// unit of 8 (168 for 384 threads, 128 for 512).
+constexpr uint32_t REGS_LAUNCH = QT == 3 ? 128 : 168;
+constexpr uint32_t REGS_SOFTMAX = QT == 3 ? 144 : 208, REGS_CTRL = QT == 3 ? 80 : 88;
+static_assert(128 * (QT * REGS_SOFTMAX + REGS_CTRL) <= THREADS * REGS_LAUNCH, "register split");
+static_assert(THREADS * REGS_LAUNCH <= 65536, "launch registers");
 constexpr int MAX_SEG = PVLC_VISION_MAX_SEGMENTS;
 
 // shared memory map (offsets from a 1024-aligned base)
-constexpr uint32_t SZ_W = 128 * 128;    // 128 rows x 64 dims fp16, 128B swizzle
-constexpr uint32_t SZ_N = 128 * 32;     // 128 rows x 16 dims fp16, 32B swizzle
-constexpr uint32_t Q_BYTES = SZ_W + SZ_N;
+constexpr uint32_t SZ_QW = BM * 128;    // Q: 128 rows x 64 dims fp16, 128B swizzle
+constexpr uint32_t SZ_QN = BM * 32;     // Q: 128 rows x 16 dims fp16, 32B swizzle
+constexpr uint32_t Q_BYTES = SZ_QW + SZ_QN;
 constexpr uint32_t OFF_Q = 0;           // tile t at OFF_Q + t * Q_BYTES: wide block, narrow block
 constexpr uint32_t OFF_STAGE = QT * Q_BYTES;
-constexpr uint32_t ST_K0 = 0, ST_K1 = SZ_W, ST_V0 = SZ_W + SZ_N, ST_V1 = 2 * SZ_W + SZ_N;
-constexpr uint32_t STAGE_BYTES = 3 * SZ_W + SZ_N;
-constexpr int STAGES = 3;
+// stage: K dims 0..63 (BN rows x 128 B), V dims 0..63, V dims 64..127 (both BN
+// x 128 B), K dims 64..79 (BN x 32 B); every 128B-swizzled block 1 KB aligned
+constexpr uint32_t ST_K0 = 0, ST_V0 = BN * 128, ST_V1 = 2 * BN * 128, ST_K1 = 3 * BN * 128;
+constexpr uint32_t LOAD_BYTES = ST_K1 + BN * 32;   // bytes the four TMA boxes of a stage bring
+constexpr uint32_t STAGE_BYTES = (LOAD_BYTES + 1023) / 1024 * 1024;
+constexpr int STAGES = QT == 3 ? 4 : 3;
 constexpr uint32_t OFF_BARS = OFF_STAGE + STAGES * STAGE_BYTES;
-// q_full, kv_full[3], v_ready[3], kv_empty[3], s_full[2], p_ready[2], o_done[2]
-constexpr int NBARS = 16;
+// q_full, kv_full[STAGES], v_ready[STAGES], kv_empty[STAGES], s_full[QT], p_ready[QT], o_done[QT]
+constexpr int NBARS = 1 + 3 * STAGES + 3 * QT;
+// TMEM columns: S/P of tile t at S_COL(t), O (80 columns) at O_COL(t)
+constexpr uint32_t O_COLS = 80;
+__host__ __device__ constexpr uint32_t S_COL(int t) { return (uint32_t)t * BN; }
+__host__ __device__ constexpr uint32_t O_COL(int t) { return (uint32_t)QT * BN + (uint32_t)t * O_COLS; }
+static_assert(O_COL(QT) <= 512, "TMEM columns");
+static_assert(BN % 16 == 0 && BN % 8 == 0 && ST_V0 % 1024 == 0 && ST_K1 % 1024 == 0,
+              "tile shapes");
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 64 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "vision shared memory exceeds the sm_100 limit");
@@ -179,12 +200,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [3]
-  uint64_t* v_ready = bars + 4;    // [3] K/V landed and the row-sum column written
-  uint64_t* kv_empty = bars + 7;   // [3]
-  uint64_t* s_full = bars + 10;    // [2]
-  uint64_t* p_ready = bars + 12;   // [2]
-  uint64_t* o_done = bars + 14;    // [2]
+  uint64_t* kv_full = bars + 1;                   // [STAGES]
+  uint64_t* v_ready = kv_full + STAGES;           // [STAGES] K/V landed, row-sum column written
+  uint64_t* kv_empty = v_ready + STAGES;          // [STAGES]
+  uint64_t* s_full = kv_empty + STAGES;           // [QT]
+  uint64_t* p_ready = s_full + QT;                // [QT]
+  uint64_t* o_done = p_ready + QT;                // [QT]
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
   // misc[0]: TMEM base, misc[1]: abort
 
@@ -196,7 +217,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t seg0 = sc.seg_start[sg], seglen = sc.seg_len[sg];
   const uint32_t q0 = seg0 + (item - sc.item_prefix[sg]) * (QT * BM);
   const uint32_t seg_end = seg0 + seglen;
-  const bool has1 = q0 + BM < seg_end;       // second Q tile holds rows of this segment
+  // Q tiles of this item that hold rows of the segment
+  const int ntile = static_cast<int>(umin32(QT, (seg_end - q0 + BM - 1) / BM));
   const int nk = static_cast<int>((seglen + BN - 1) / BN);
 
   if (tid == 0) {
@@ -235,10 +257,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tma_prefetch_desc(&maps.v0);
       // q and k come from the rotation pass (the preceding launch, when rotated)
       pdl_wait();
-      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * Q_BYTES);
-      for (int t = 0; t < (has1 ? 2 : 1); ++t) {
+      mbar_arrive_expect_tx(q_full, ntile * Q_BYTES);
+      for (int t = 0; t < ntile; ++t) {
         tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES, &maps.q0, 0, head, q0 + t * BM, q_full);
-        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + SZ_W, &maps.q1, 64, head, q0 + t * BM, q_full);
+        tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + SZ_QW, &maps.q1, 64, head, q0 + t * BM, q_full);
       }
       int issued = 0;
       for (int j = 0; j < nk; ++j) {
@@ -247,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (misc[1] || !mbar_wait(&kv_empty[s], (use & 1) ^ 1)) { misc[1] = 1; break; }
         uint8_t* st = smem + OFF_STAGE + s * STAGE_BYTES;
         const int z = seg0 + j * BN;
-        mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
+        mbar_arrive_expect_tx(&kv_full[s], LOAD_BYTES);
         tc::tma_load_3d(st + ST_K0, &maps.k0, 0, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_K1, &maps.k1, 64, head, z, &kv_full[s]);
         tc::tma_load_3d(st + ST_V0, &maps.v0, 0, head, z, &kv_full[s]);
@@ -264,22 +286,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the commit that tracks it.  Descriptors are built once; each K step
       // only adds a constant to the start-address field (address >> 4 in the
       // low bits).
-      constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
-      constexpr uint32_t idesc_pv = tc::idesc_f16(128, 80, 0, 1);
-      const int ntile = has1 ? 2 : 1;
+      constexpr uint32_t idesc_qk = tc::idesc_f16(128, BN, 0, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(128, O_COLS, 0, 1);
       // Descriptors of tile t / stage s are the tile-0 / stage-0 descriptors
       // plus the byte offset >> 4 in the start-address field (which never
       // carries out of its 14 bits inside 227 KB of shared memory).
       const uint32_t sq = smem_u32(smem + OFF_Q);
       const uint32_t st0 = smem_u32(smem + OFF_STAGE);
       const uint64_t dq_w = tc::smem_desc(sq, 16, 1024, tc::kSw128);
-      const uint64_t dq_n = tc::smem_desc(sq + SZ_W, 16, 256, tc::kSw32);
+      const uint64_t dq_n = tc::smem_desc(sq + SZ_QW, 16, 256, tc::kSw32);
       const uint64_t dk_w = tc::smem_desc(st0 + ST_K0, 16, 1024, tc::kSw128);
       const uint64_t dk_n = tc::smem_desc(st0 + ST_K1, 16, 256, tc::kSw32);
       // MN-major V: 64-column swizzle atoms ST_V1 - ST_V0 apart (LBO), 8-key groups 1 KB apart
       const uint64_t dv = tc::smem_desc(st0 + ST_V0, ST_V1 - ST_V0, 1024, tc::kSw128);
       auto qk = [&](int t, int s) {
-        const uint32_t tS = tmem + 128u * t;
+        const uint32_t tS = tmem + S_COL(t);
         const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4), so = (uint64_t)s * (STAGE_BYTES >> 4);
         if (tc::elect_one()) {
 #pragma unroll
@@ -291,11 +312,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
       };
       auto pv = [&](int t, int s, bool first, bool release) {
-        const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
+        const uint32_t tS = tmem + S_COL(t), tO = tmem + O_COL(t);
         const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
         if (tc::elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks)   // 16 keys = two 1 KB groups per K step -> +128
+          for (int ks = 0; ks < BN / 16; ++ks)   // 16 keys = two 1 KB groups per K step -> +128
             tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
           tc::commit(&o_done[t]);
           if (release) tc::commit(&kv_empty[s]);   // the stage is free once every tile's PV is done
@@ -337,17 +358,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp >= CTRL_WARP + 2) {
       // ---------------------------------------------------- row-sum column
       // V row r, dims 72..79 (chunk 1 of the second 64-dim block) = {1, 0 x 7}
-      const int u = tid - 32 * (CTRL_WARP + 2);   // 0..63: rows u and u + 64
+      const int u = tid - 32 * (CTRL_WARP + 2);   // 0..63: rows u, u + 64, ...
       for (int j = 0; j < nk; ++j) {
         const int s = j % STAGES;
         if (misc[1] || !mbar_wait(&kv_full[s], (j / STAGES) & 1)) { misc[1] = 1; break; }
         uint8_t* v1 = smem + OFF_STAGE + s * STAGE_BYTES + ST_V1;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = u + 64 * h;
+        for (int r = u; r < BN; r += 64)
           *reinterpret_cast<uint4*>(v1 + r * 128 + ((1 ^ (r & 7)) << 4)) =
               make_uint4(0x3C00u, 0u, 0u, 0u);
-        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&v_ready[s]);
@@ -359,10 +377,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int t = wg;                              // Q tile of this warpgroup
     const int i = tid - 128 * t;                   // query row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_base + 128u * t;
-    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+    const uint32_t tS = tmem + lane_base + S_COL(t);
+    const uint32_t tO = tmem + lane_base + O_COL(t);
     const uint32_t row = q0 + t * BM + i;          // token of this query row
-    if (t == 0 || has1) {
+    if (t < ntile) {
       const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
       const uint64_t scale2 = f2_pack(scale, scale);
       float m_run = -CUDART_INF_F;   // running max (the row sum lives in O[:, 72])
@@ -375,28 +393,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         tc::fence_after_sync();
         const int kv = static_cast<int>(umin32(BN, seglen - j * BN));
-        uint32_t sv[128];
-        tc::tmem_ld32(tS + 0, sv);
-        tc::tmem_ld32(tS + 32, sv + 32);
-        tc::tmem_ld32(tS + 64, sv + 64);
-        tc::tmem_ld32(tS + 96, sv + 96);
+        uint32_t sv[BN];
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (c0 + 32 <= BN) tc::tmem_ld32(tS + c0, sv + c0);
+          else tc::tmem_ld16(tS + c0, sv + c0);
+        }
         tc::tmem_wait_ld();
         if (kv < BN) {   // last tile of the segment: keys past its end score -inf
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < BN; ++c)
             if (c >= kv) sv[c] = __float_as_uint(-CUDART_INF_F);
         }
         // row max over four independent chains
         float m4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
                        __uint_as_float(sv[3])};
 #pragma unroll
-        for (int c = 4; c < 124; c += 8) {
+        for (int c = 4; c + 8 <= BN; c += 8) {
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             m4[e] = fmax3(m4[e], __uint_as_float(sv[c + 2 * e]), __uint_as_float(sv[c + 2 * e + 1]));
         }
-        m4[0] = fmax3(m4[0], __uint_as_float(sv[124]), __uint_as_float(sv[125]));
-        m4[1] = fmax3(m4[1], __uint_as_float(sv[126]), __uint_as_float(sv[127]));
+        static_assert(BN % 8 == 0, "the max tail is the last four columns");
+        m4[0] = fmax3(m4[0], __uint_as_float(sv[BN - 4]), __uint_as_float(sv[BN - 3]));
+        m4[1] = fmax3(m4[1], __uint_as_float(sv[BN - 2]), __uint_as_float(sv[BN - 1]));
         const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
         // move the running max only when it grew past the threshold
         const bool need = mx > m_run + RESCALE_THRESHOLD;
@@ -424,11 +444,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         // MUFU operation per two values
         const uint64_t negm2 = f2_pack(-m_run, -m_run);
         const uint64_t negmh2 = f2_pack(6.5f - m_run, 6.5f - m_run);   // exp2_h2_poly takes x + 6.5
+        // chunks of up to 16 pairs (32 keys); P of keys 2c, 2c+1 lands in column c
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < (BN + 31) / 32; ++ch) {
+          constexpr int kPairs = BN / 2;
+          const int np = kPairs - 16 * ch < 16 ? kPairs - 16 * ch : 16;
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
+            if (c >= np) break;
             const int k = 32 * ch + 2 * c;
             if ((EXP_POLY_MASK >> c) & 1u) {
               pk[c] = exp2_h2_poly(f2_fma(u2_pack(sv[k], sv[k + 1]), scale2, negmh2));
@@ -437,8 +461,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               pk[c] = ex2_h2(pack_half2(x.x, x.y));
             }
           }
-          tc::tmem_st16(tS + 16 * ch, pk);
+          if (np == 16) tc::tmem_st16(tS + 16 * ch, pk);
+          else tc::tmem_st8(tS + 16 * ch, pk);
         }
+        static_assert(BN % 32 == 0 || BN % 32 == 16, "a P chunk is 16 or 8 columns");
         tc::tmem_wait_st();
         tc::fence_before_sync();
         __syncwarp();
@@ -501,14 +527,14 @@ EncodeTiled encoder() {
 }
 
 // [tokens, heads, 72] fp16 viewed as a 3-D tensor {72, heads, tokens}; box
-// {inner, 1, 128} rows of one head.
+// {inner, 1, rows} rows of one head.
 bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads, uint32_t inner,
-              CUtensorMapSwizzle sw) {
+              uint32_t rows, CUtensorMapSwizzle sw) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
   const cuuint64_t dims[3] = {HD, heads, tokens};
   const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)heads * HD * 2};
-  const cuuint32_t box[3] = {inner, 1, 128};
+  const cuuint32_t box[3] = {inner, 1, rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -545,11 +571,14 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, vo
     ka = k_rot;
   }
   vtc::Maps maps;
-  const bool ok = vtc::make_map(&maps.q0, qa, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  vtc::make_map(&maps.q1, qa, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
-                  vtc::make_map(&maps.k0, ka, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
-                  vtc::make_map(&maps.k1, ka, a.tokens, a.heads, 16, CU_TENSOR_MAP_SWIZZLE_32B) &&
-                  vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  using vtc::BM;
+  using vtc::BN;
+  const bool ok =
+      vtc::make_map(&maps.q0, qa, a.tokens, a.heads, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      vtc::make_map(&maps.q1, qa, a.tokens, a.heads, 16, BM, CU_TENSOR_MAP_SWIZZLE_32B) &&
+      vtc::make_map(&maps.k0, ka, a.tokens, a.heads, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      vtc::make_map(&maps.k1, ka, a.tokens, a.heads, 16, BN, CU_TENSOR_MAP_SWIZZLE_32B) &&
+      vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return PVLC_CUDA_ERROR;
   vtc::Sched sc;
   std::vector<uint32_t> order(segments);
