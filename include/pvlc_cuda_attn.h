@@ -109,6 +109,20 @@ int pvlc_attn_vision_varlen_ws(const pvlc_half* q, const pvlc_half* k, const pvl
                                uint32_t tokens, uint32_t heads, uint32_t head_dim,
                                const float* rope_cos, const float* rope_sin, void* workspace,
                                size_t workspace_bytes, pvlc_half* out, void* stream);
+/* pvlc_attn_vision_varlen_ws with q, k and v rows qkv_row_stride elements apart
+ * (token t's q row at q + t * qkv_row_stride, each row heads x head_dim
+ * contiguous); out stays packed.  It has no counterpart in the reference.  It
+ * lets the three vision projections come out of one GEMM: with a [tokens,
+ * 3 x 1152] output, q = base, k = base + 1152, v = base + 2304,
+ * qkv_row_stride = 3456.  The stride must be a multiple of 8 and at least
+ * heads x head_dim, otherwise PVLC_LENGTH_MISMATCH. */
+int pvlc_attn_vision_varlen_strided_ws(const pvlc_half* q, const pvlc_half* k,
+                                       const pvlc_half* v, uint32_t qkv_row_stride,
+                                       const uint32_t* cu_seqlens_host, uint32_t segments,
+                                       uint32_t tokens, uint32_t heads, uint32_t head_dim,
+                                       const float* rope_cos, const float* rope_sin,
+                                       void* workspace, size_t workspace_bytes, pvlc_half* out,
+                                       void* stream);
 
 /* ----------------------------------------------------------------------------
  * Path 2: decoder causal GQA prefill with fused 3-section M-RoPE and in-place
@@ -298,6 +312,33 @@ int pvlc_add_norm(float* residual, const pvlc_half* delta, uint32_t rows, uint32
 int pvlc_gelu(pvlc_half* x, uint64_t n, int erf_form, void* stream);
 int pvlc_silu_mul(const pvlc_half* gate_up, uint32_t rows, uint32_t width, pvlc_half* out,
                   void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Greedy top-1 over the LM head (decoder-stack glue beside the attention path).
+ *
+ * Replaces the logits GEMM and the argmax of the reference's greedy step:
+ * chunked_lm_head_top_k_f32 with top_k = 1 and compare_top_k_entries
+ * (crates/pvlc-cpu-ref/src/lib.rs:1511-1568, 2051-2056), run in the WebGPU
+ * session as an LM-head pass and an argmax pass
+ * (crates/pvlc-runtime-web/src/web/decoder_stack_session.rs:308-350).
+ *
+ * tokens[r] = the id v maximising logit(r, v) = sum_d hidden[r, d] *
+ * lm_head[v, d] (fp16 operands, f32 accumulation), larger logits first in
+ * f32::total_cmp order and equal logits to the smaller id; logits[r] (when
+ * not NULL) receives that logit.  The [rows, vocab] logits are never written.
+ * hidden: device [rows, hidden_dim] fp16 (the final-norm output), rows <=
+ * PVLC_LM_HEAD_MAX_ROWS; lm_head: device [vocab, hidden_dim] fp16; hidden_dim
+ * a multiple of 64 (1024 in the pinned decoder).  workspace: device scratch of
+ * pvlc_lm_head_top1_workspace_bytes(rows) bytes, 16-byte aligned; the call
+ * clears it on `stream` first.  pvlc_lm_head_top1_errors reads the fault word
+ * (bit 3: a pipeline wait timed out) and waits for the stream.
+ */
+#define PVLC_LM_HEAD_MAX_ROWS 256u
+size_t pvlc_lm_head_top1_workspace_bytes(uint32_t rows);
+int pvlc_lm_head_top1(const pvlc_half* hidden, uint32_t rows, const pvlc_half* lm_head,
+                      uint32_t vocab, uint32_t hidden_dim, void* workspace,
+                      size_t workspace_bytes, int32_t* tokens, float* logits, void* stream);
+int pvlc_lm_head_top1_errors(void* workspace, uint32_t rows, uint32_t* flags_out, void* stream);
 
 /* ----------------------------------------------------------------------------
  * Checkpoint import on the device: BF16 -> IEEE binary16, round to nearest,

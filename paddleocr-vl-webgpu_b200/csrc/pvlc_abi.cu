@@ -268,7 +268,26 @@ int pvlc_attn_vision_varlen_ws(const pvlc_half* q, const pvlc_half* k, const pvl
     if (!aligned16(workspace)) return PVLC_MISALIGNED_POINTER;
     if (workspace_bytes < vision_workspace_bytes(tokens, heads)) return PVLC_WORKSPACE_TOO_SMALL;
   }
-  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out};
+  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out, heads * head_dim};
+  return vision_launch(a, cu, segments, workspace, static_cast<cudaStream_t>(stream));
+}
+
+int pvlc_attn_vision_varlen_strided_ws(const pvlc_half* q, const pvlc_half* k,
+                                       const pvlc_half* v, uint32_t qkv_row_stride,
+                                       const uint32_t* cu, uint32_t segments, uint32_t tokens,
+                                       uint32_t heads, uint32_t head_dim, const float* rope_cos,
+                                       const float* rope_sin, void* workspace,
+                                       size_t workspace_bytes, pvlc_half* out, void* stream) {
+  const int st = vision_checks(q, k, v, cu, segments, tokens, heads, head_dim, rope_cos, rope_sin,
+                               out);
+  if (st) return st;
+  if (qkv_row_stride < heads * head_dim || qkv_row_stride % 8 != 0) return PVLC_LENGTH_MISMATCH;
+  if (rope_cos) {
+    if (!workspace) return PVLC_NULL_POINTER;
+    if (!aligned16(workspace)) return PVLC_MISALIGNED_POINTER;
+    if (workspace_bytes < vision_workspace_bytes(tokens, heads)) return PVLC_WORKSPACE_TOO_SMALL;
+  }
+  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out, qkv_row_stride};
   return vision_launch(a, cu, segments, workspace, static_cast<cudaStream_t>(stream));
 }
 
@@ -290,7 +309,7 @@ int pvlc_attn_vision_varlen(const pvlc_half* q, const pvlc_half* k, const pvlc_h
       return PVLC_CUDA_ERROR;
     }
   }
-  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out};
+  VisionArgs a{q, k, v, rope_cos, rope_sin, tokens, heads, out, heads * head_dim};
   const int rc = vision_launch(a, cu, segments, ws, s);
   if (ws && cudaFreeAsync(ws, s) != cudaSuccess && rc == PVLC_OK) return PVLC_CUDA_ERROR;
   return rc;

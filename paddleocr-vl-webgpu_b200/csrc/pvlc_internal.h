@@ -43,6 +43,7 @@ struct VisionArgs {
   uint32_t tokens;
   uint32_t heads;
   pvlc_half* out;
+  uint32_t qkv_stride;   // elements between consecutive tokens' q / k / v rows (heads x 72 packed)
 };
 int vision_query_tile();
 int vision_block_threads();
@@ -86,6 +87,19 @@ int prefill_query_tile();
 void prefill_schedule(uint32_t tokens, int sms, uint32_t* n_split, uint32_t* n_light);
 int prefill_block_threads();
 int prefill_launch(const PrefillArgs& a, cudaStream_t stream);
+
+// Greedy top-1 over the LM head (lm_head.cu).
+struct LmHeadArgs {
+  const pvlc_half* hidden;    // [rows, hidden_dim]
+  const pvlc_half* lm_head;   // [vocab, hidden_dim]
+  uint32_t rows, vocab, hidden_dim;
+  void* workspace;            // lm_head_workspace_bytes(rows)
+  int32_t* tokens;            // [rows]
+  float* logits;              // [rows] winning logit, or null
+};
+size_t lm_head_workspace_bytes(uint32_t rows);
+size_t lm_head_flags_offset(uint32_t rows);
+int lm_head_top1_launch(const LmHeadArgs& a, cudaStream_t stream);
 
 int device_sm_count();
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, smem_bytes) once per

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(256)
     vision_rope_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
                        const float* __restrict__ cs, const float* __restrict__ sn,
                        __half* __restrict__ q_rot, __half* __restrict__ k_rot, uint32_t heads,
-                       uint64_t quads) {
+                       uint32_t in_stride, uint64_t quads) {
   // the attention launch may start its prologue (barriers, TMEM) now; it
   // waits for this kernel before loading the rotated q and k
   pdl_launch_dependents();
@@ -173,10 +173,12 @@ __global__ void __launch_bounds__(256)
   const uint64_t token = row / heads;
   const float4 c = __ldg(reinterpret_cast<const float4*>(cs + token * PAIRS) + quad);
   const float4 s = __ldg(reinterpret_cast<const float4*>(sn + token * PAIRS) + quad);
+  // inputs at a token stride of in_stride elements; the rotated copies packed
   const size_t lo = row * HD + 4 * quad, hi = lo + PAIRS;
+  const size_t ilo = token * in_stride + (row - token * heads) * HD + 4 * quad, ihi = ilo + PAIRS;
   auto rot = [&](const __half* src, __half* dst) {
-    const uint2 a = __ldg(reinterpret_cast<const uint2*>(src + lo));
-    const uint2 b = __ldg(reinterpret_cast<const uint2*>(src + hi));
+    const uint2 a = __ldg(reinterpret_cast<const uint2*>(src + ilo));
+    const uint2 b = __ldg(reinterpret_cast<const uint2*>(src + ihi));
     const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&a.x));
     const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&a.y));
     const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&b.x));
@@ -526,14 +528,14 @@ EncodeTiled encoder() {
   return fn;
 }
 
-// [tokens, heads, 72] fp16 viewed as a 3-D tensor {72, heads, tokens}; box
-// {inner, 1, rows} rows of one head.
-bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads, uint32_t inner,
-              uint32_t rows, CUtensorMapSwizzle sw) {
+// [tokens, heads, 72] fp16 rows `stride` elements apart, viewed as a 3-D tensor
+// {72, heads, tokens}; box {inner, 1, rows} rows of one head.
+bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads, uint32_t stride,
+              uint32_t inner, uint32_t rows, CUtensorMapSwizzle sw) {
   EncodeTiled enc = encoder();
   if (!enc) return false;
   const cuuint64_t dims[3] = {HD, heads, tokens};
-  const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)heads * HD * 2};
+  const cuuint64_t strides[2] = {HD * 2, (cuuint64_t)stride * 2};
   const cuuint32_t box[3] = {inner, 1, rows};
   const cuuint32_t estr[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
@@ -557,6 +559,7 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, vo
   // rotated q and k (the scratch) or the inputs themselves when there is no RoPE
   const void* qa = a.q;
   const void* ka = a.k;
+  uint32_t qk_stride = a.qkv_stride;   // the rotated copies are packed
   if (a.rope_cos != nullptr) {
     __half* q_rot = static_cast<__half*>(workspace);
     __half* k_rot = q_rot + (size_t)a.tokens * a.heads * vtc::HD;
@@ -565,20 +568,22 @@ int vision_launch(const VisionArgs& a, const uint32_t* cu, uint32_t segments, vo
     if (blocks > 0x7fffffffull) return PVLC_ARITHMETIC_OVERFLOW;
     vtc::vision_rope_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
         reinterpret_cast<const __half*>(a.q), reinterpret_cast<const __half*>(a.k), a.rope_cos,
-        a.rope_sin, q_rot, k_rot, a.heads, quads);
+        a.rope_sin, q_rot, k_rot, a.heads, a.qkv_stride, quads);
     if (cudaPeekAtLastError() != cudaSuccess) return PVLC_CUDA_ERROR;
     qa = q_rot;
     ka = k_rot;
+    qk_stride = a.heads * vtc::HD;
   }
   vtc::Maps maps;
   using vtc::BM;
   using vtc::BN;
   const bool ok =
-      vtc::make_map(&maps.q0, qa, a.tokens, a.heads, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
-      vtc::make_map(&maps.q1, qa, a.tokens, a.heads, 16, BM, CU_TENSOR_MAP_SWIZZLE_32B) &&
-      vtc::make_map(&maps.k0, ka, a.tokens, a.heads, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B) &&
-      vtc::make_map(&maps.k1, ka, a.tokens, a.heads, 16, BN, CU_TENSOR_MAP_SWIZZLE_32B) &&
-      vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+      vtc::make_map(&maps.q0, qa, a.tokens, a.heads, qk_stride, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      vtc::make_map(&maps.q1, qa, a.tokens, a.heads, qk_stride, 16, BM, CU_TENSOR_MAP_SWIZZLE_32B) &&
+      vtc::make_map(&maps.k0, ka, a.tokens, a.heads, qk_stride, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B) &&
+      vtc::make_map(&maps.k1, ka, a.tokens, a.heads, qk_stride, 16, BN, CU_TENSOR_MAP_SWIZZLE_32B) &&
+      vtc::make_map(&maps.v0, a.v, a.tokens, a.heads, a.qkv_stride, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok) return PVLC_CUDA_ERROR;
   vtc::Sched sc;
   std::vector<uint32_t> order(segments);

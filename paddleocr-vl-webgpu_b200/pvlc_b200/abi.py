@@ -69,6 +69,9 @@ _SIGNATURES = {
     "pvlc_attn_vision_workspace_bytes": (ctypes.c_size_t, [_U32, _U32, _U32]),
     "pvlc_attn_vision_varlen_ws": (ctypes.c_int, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _P, _P,
                                                   _P, ctypes.c_size_t, _P, _P]),
+    "pvlc_attn_vision_varlen_strided_ws": (ctypes.c_int, [_P, _P, _P, _U32, _P, _U32, _U32, _U32,
+                                                          _U32, _P, _P, _P, ctypes.c_size_t, _P,
+                                                          _P]),
     "pvlc_attn_decoder_prefill": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _P,
                                                  _P, _P]),
     "pvlc_attn_decoder_prefill_batch": (ctypes.c_int, [_P, _P, _P, _P, _U32, _P, _P, _P, _P, _P,
@@ -90,6 +93,10 @@ _SIGNATURES = {
     "pvlc_gelu": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int, _P]),
     "pvlc_silu_mul": (ctypes.c_int, [_P, _U32, _U32, _P, _P]),
     "pvlc_bf16_to_f16": (ctypes.c_int, [_P, _P, ctypes.c_uint64, ctypes.c_uint64, _P, _P]),
+    "pvlc_lm_head_top1_workspace_bytes": (ctypes.c_size_t, [_U32]),
+    "pvlc_lm_head_top1": (ctypes.c_int, [_P, _U32, _P, _U32, _U32, _P, ctypes.c_size_t, _P, _P,
+                                         _P]),
+    "pvlc_lm_head_top1_errors": (ctypes.c_int, [_P, _U32, ctypes.POINTER(ctypes.c_uint32), _P]),
     "pvlc_plan_vision_varlen": (ctypes.c_int, [_P, _U32, _U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_prefill": (ctypes.c_int, [_U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_kv_session": (ctypes.c_int, [_U32, _U32, _U32, _U32, _U32,

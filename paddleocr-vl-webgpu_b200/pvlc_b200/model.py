@@ -163,9 +163,13 @@ class OcrEngine:
         self.vlayers = []
         for l in range(c.vision_layers):
             lw = vw[3 + 16 * l: 3 + 16 * (l + 1)]
+            # q, k and v as one [3 x 1152, 1152] projection (one GEMM per layer); the
+            # attention reads the three column blocks of its output in place
             self.vlayers.append(dict(
-                ln1=(f32(lw[0]), f32(lw[1])), q=(lw[2], lw[3]), k=(lw[4], lw[5]),
-                v=(lw[6], lw[7]), o=(lw[8], lw[9]), ln2=(f32(lw[10]), f32(lw[11])),
+                ln1=(f32(lw[0]), f32(lw[1])),
+                qkv=(torch.cat([lw[2], lw[4], lw[6]], 0).contiguous(),
+                     torch.cat([lw[3], lw[5], lw[7]], 0).contiguous()),
+                o=(lw[8], lw[9]), ln2=(f32(lw[10]), f32(lw[11])),
                 fc1=(lw[12], lw[13]), fc2=(lw[14], lw[15])))
         post = vw[3 + 16 * c.vision_layers:]
         self.post_ln = (f32(post[0]), f32(post[1]))
@@ -181,7 +185,7 @@ class OcrEngine:
         self.final_norm = f32(dw[1 + 9 * c.decoder_layers])
         self.lm_head = dw[2 + 9 * c.decoder_layers]
         self._grid_cache = {}
-        self._graph = None
+        self._decode = None
 
     @classmethod
     def from_checkpoint(cls, path, cfg: ModelConfig | None = None, device=None, **kw):
@@ -252,9 +256,8 @@ class OcrEngine:
         pending = None
         for L in self.vlayers:
             n1 = ops.add_norm(h32, L["ln1"][0], c.vision_eps, bias=L["ln1"][1], delta=pending)
-            q = F.linear(n1, *L["q"]).view(N, heads, hd)
-            k = F.linear(n1, *L["k"]).view(N, heads, hd)
-            v = F.linear(n1, *L["v"]).view(N, heads, hd)
+            qkv = F.linear(n1, *L["qkv"])                 # [N, 3 x 1152]
+            q, k, v = (qkv[:, j * H:(j + 1) * H].view(N, heads, hd) for j in range(3))
             ops.vision_varlen_attention(q, k, v, cu, rcos, rsin, out=ctx, workspace=ws)
             o = F.linear(ctx.view(N, H), *L["o"])
             n2 = ops.add_norm(h32, L["ln2"][0], c.vision_eps, bias=L["ln2"][1], delta=o)
@@ -314,6 +317,17 @@ class OcrEngine:
                    delta)
             self._grid_cache[key] = hit
         return hit
+
+    def _decode_buffers(self, B: int, cap: int) -> "_DecodeGraph":
+        """The decode buffers of the last batch shape when (B, cap) matches; otherwise the
+        old ones are released first and new ones made."""
+        d = self._decode
+        if d is None or d.B != B or d.cap != cap:
+            self._decode = None
+            del d
+            torch.cuda.empty_cache()
+            self._decode = _DecodeGraph(self, B, cap)
+        return self._decode
 
     def _layer_mlp(self, L, h32, o):
         """h32 += o; SwiGLU MLP of RMSNorm(h32); returns the MLP output (added to h32 by the
@@ -414,9 +428,10 @@ class OcrEngine:
         if ev:
             ev[1].record()
         QW = c.query_heads * c.head_dim
-        Lyr = c.decoder_layers
-        kc = torch.empty((Lyr, B, cap, c.kv_heads, c.head_dim), dtype=torch.float16, device=dev)
-        vc = torch.empty_like(kc)
+        # the KV caches and the decode step's graph belong to the batch shape (B, cap) and
+        # are reused by the next call of the same shape
+        dec = self._decode_buffers(B, cap)
+        kc, vc = dec.kc, dec.vc
         # ---- prefill: GEMMs over all prompts, attention per prompt
         emb = self.embed.index_select(0, ids_t)
         emb.index_copy_(0, img_idx, torch.cat(img, 0))
@@ -431,15 +446,18 @@ class OcrEngine:
             ops.decoder_prefill_packed(q, k, v, offs, tables, kc[l], vc[l], ctx)
             pending = self._layer_mlp(L, h32, F.linear(ctx.view(NT, QW), L["o"]))
         fn = ops.add_norm(h32, self.final_norm, c.rms_eps, delta=pending)
-        logits0 = self._logits(fn.index_select(0, last))
-        first = torch.argmax(logits0, dim=-1)
+        if record_logits:
+            logits0 = self._logits(fn.index_select(0, last))
+            first = torch.argmax(logits0, dim=-1)
+        else:
+            first = ops.lm_head_top1(fn.index_select(0, last), self.lm_head).long()
         if ev:
             ev[2].record()
         first_host = _download(first)
         rec = [_download(logits0)] if record_logits else None
         # ---- batched decode, one CUDA graph per step shape; one chunk always queued
         # ahead of the chunk whose tokens are being applied
-        dec = _DecodeGraph(self, kc, vc, cap, first, np.asarray(Ts), np.asarray(deltas))
+        dec.reset(first, np.asarray(Ts), np.asarray(deltas))
         inflight = []
         budget = max_new_tokens - 1        # decode steps a request can still need
 
@@ -517,24 +535,24 @@ class _DecodeGraph:
     """One batched decode step (embedding -> 18 layers with the fused decode attention ->
     LM head -> argmax), captured in a CUDA graph over static buffers."""
 
-    def __init__(self, eng: OcrEngine, kc, vc, cap, first_tokens, prompt_lens, deltas):
-        """prompt_lens, deltas: host integer arrays [B] (prompt rows, M-RoPE decode delta)."""
+    def __init__(self, eng: OcrEngine, B: int, cap: int):
+        """Static buffers of a B-request batch with KV caches of `cap` rows: the caches
+        (filled by the prefill), the decode scratch and, once run() first captures it,
+        the step graph.  reset() loads a new batch into them."""
         c, dev = eng.cfg, eng.device
-        self.eng, self.cap = eng, cap
-        B = first_tokens.shape[0]
-        self.B = B
-        pl = np.asarray(prompt_lens, dtype=np.int64)
-        pos = pl + np.asarray(deltas, dtype=np.int64)
-        if pos.min() < 0:
-            raise positions.PositionError("decode position is negative")
-        self.tok = first_tokens.clone().to(torch.int64)
-        self.rows = _upload(np.concatenate([pl, pos]).astype(np.int32), dev)
+        self.eng, self.cap, self.B = eng, cap, B
+        Lyr = c.decoder_layers
+        self.kc = torch.empty((Lyr, B, cap, c.kv_heads, c.head_dim), dtype=torch.float16,
+                              device=dev)
+        self.vc = torch.empty_like(self.kc)
+        kc, vc = self.kc, self.vc
+        self.tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.rows = torch.zeros(2 * B, dtype=torch.int32, device=dev)
         self.ct = self.rows[:B]                 # rows before the append
         self.rope_row = self.rows[B:]           # decode position ct + delta
-        self.ct_max = int(pl.max())             # host copy of ct.max() (all rows step together)
-        rows = int(pos.max()) + cap + 1
-        rc, rs = positions.linear_rope_tables(rows, c.decoder_theta, c.head_dim)
-        self.rcos, self.rsin = _upload(rc, dev), _upload(rs, dev)
+        self.ct_max = 0
+        self.rope_rows = 0
+        self.rcos = self.rsin = None
         # per-layer device tables of the B cache bases (kc[l, b], vc[l, b])
         Lyr = c.decoder_layers
         lb = np.arange(Lyr * B, dtype=np.int64).reshape(Lyr, B) * (kc.stride(1) * kc.element_size())
@@ -550,10 +568,38 @@ class _DecodeGraph:
         self.k = self.qkv[:, QW:QW + KW].view(B, c.kv_heads, c.head_dim)
         self.v = self.qkv[:, QW + KW:].view(B, c.kv_heads, c.head_dim)
         self.ctx = torch.empty((B, c.query_heads, c.head_dim), dtype=torch.float16, device=dev)
+        # greedy top-1 straight from the LM head GEMM (pvlc_lm_head_top1) unless the
+        # caller wants the logits themselves
+        self.top1 = torch.empty(B, dtype=torch.int32, device=dev)
+        self.top1_ws = torch.empty(
+            int(abi.lib().pvlc_lm_head_top1_workspace_bytes(min(B, ops.LM_HEAD_MAX_ROWS))),
+            dtype=torch.uint8, device=dev)
         self.graph = None
+        self.graph_logits = None
         self.logits = None
 
-    def _step(self):
+    def reset(self, first_tokens, prompt_lens, deltas):
+        """A new batch: first tokens (device [B]), host prompt lengths and M-RoPE decode
+        deltas [B].  The prefill has written rows [0, prompt_lens[b]) of every cache."""
+        c, dev = self.eng.cfg, self.eng.device
+        pl = np.asarray(prompt_lens, dtype=np.int64)
+        pos = pl + np.asarray(deltas, dtype=np.int64)
+        if pos.min() < 0:
+            raise positions.PositionError("decode position is negative")
+        if len(pl) != self.B or pl.max() >= self.cap:
+            raise ValueError("batch does not fit the decode buffers")
+        need = int(pos.max()) + self.cap + 1
+        if need > self.rope_rows:
+            # decode M-RoPE tables (linear positions); the step graph reads them in place
+            rc, rs = positions.linear_rope_tables(need, c.decoder_theta, c.head_dim)
+            self.rcos, self.rsin = _upload(rc, dev), _upload(rs, dev)
+            self.rope_rows = need
+            self.graph = None
+        self.tok.copy_(first_tokens.to(torch.int64))
+        self.rows.copy_(_upload(np.concatenate([pl, pos]).astype(np.int32), dev))
+        self.ct_max = int(pl.max())             # host copy of ct.max() (all rows step together)
+
+    def _step(self, with_logits: bool):
         eng, c = self.eng, self.eng.cfg
         B = self.B
         h32 = eng.embed.index_select(0, self.tok).float()
@@ -565,31 +611,37 @@ class _DecodeGraph:
                        self.ct, self.cap, self.cap - 1, self.ws[l], rope_row=self.rope_row,
                        out=self.ctx)
             pending = eng._layer_mlp(L, h32, F.linear(self.ctx.view(B, -1), L["o"]))
-        self.logits = eng._logits(ops.add_norm(h32, eng.final_norm, c.rms_eps, delta=pending))
-        self.tok.copy_(torch.argmax(self.logits, dim=-1))
+        fn = ops.add_norm(h32, eng.final_norm, c.rms_eps, delta=pending)
+        if with_logits:
+            self.logits = eng._logits(fn)
+            self.tok.copy_(torch.argmax(self.logits, dim=-1))
+        else:
+            ops.lm_head_top1(fn, eng.lm_head, tokens=self.top1, workspace=self.top1_ws)
+            self.tok.copy_(self.top1)
         self.rows += 1                          # ct and rope_row advance together
 
-    def _capture(self):
+    def _capture(self, with_logits: bool):
         saved = (self.tok.clone(), self.rows.clone())
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
-            self._step()           # warm-up: cuBLAS handles and workspaces
+            self._step(with_logits)   # warm-up: cuBLAS handles and workspaces
         torch.cuda.current_stream().wait_stream(s)
         # the warm-up wrote cache rows at ct, which the first real step rewrites
         self.tok.copy_(saved[0])
         self.rows.copy_(saved[1])
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self._step()
+            self._step(with_logits)
+        self.graph_logits = with_logits
 
     def run(self, steps: int, record_logits: bool = False):
         """Queue `steps` decode steps; returns their [steps, B] tokens (device) and, with
         record_logits, their [steps, B, vocab] logits (device).  Does not wait."""
         if self.ct_max + steps >= self.cap:
             raise abi.PvlcError(abi.CAPACITY_EXHAUSTED, "decode past the cache capacity")
-        if self.graph is None:
-            self._capture()
+        if self.graph is None or self.graph_logits != record_logits:
+            self._capture(record_logits)
         hist = torch.empty((steps, self.B), dtype=torch.int64, device=self.eng.device)
         lg = [] if record_logits else None
         for i in range(steps):

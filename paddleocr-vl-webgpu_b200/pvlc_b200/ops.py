@@ -45,20 +45,33 @@ def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, o
                             workspace=None):
     """Bidirectional block-diagonal attention over packed images with the 2-D RoPE.
 
-    q, k, v: [T, H, 72] fp16 CUDA; cu_seqlens: host sequence of segment boundaries;
-    rope_cos/rope_sin: [T, 36] f32 CUDA tables or None; workspace: optional uint8
-    CUDA tensor of at least vision_workspace_bytes (taken from torch's allocator
-    when omitted).  Returns [T, H, 72] fp16.
+    q, k, v: [T, H, 72] fp16 CUDA, each either contiguous or all three views whose
+    token rows sit the same number of elements apart (e.g. column blocks of one
+    [T, 3 * H * 72] QKV projection: pvlc_attn_vision_varlen_strided_ws);
+    cu_seqlens: host sequence of segment boundaries; rope_cos/rope_sin: [T, 36] f32
+    CUDA tables or None; workspace: optional uint8 CUDA tensor of at least
+    vision_workspace_bytes (taken from torch's allocator when omitted).  Returns
+    [T, H, 72] fp16 (contiguous).
     """
     T, H, D = q.shape
-    for name, t in (("q", q), ("k", k), ("v", v)):
-        _need(t, torch.float16, (T, H, D), name)
+    row_stride = H * D
+    strided = any(not t.is_contiguous() for t in (q, k, v))
+    if strided:
+        row_stride = q.stride(0)
+        for name, t in (("q", q), ("k", k), ("v", v)):
+            if (t.dtype != torch.float16 or tuple(t.shape) != (T, H, D) or not t.is_cuda or
+                    t.stride() != (row_stride, D, 1)):
+                raise ValueError(f"{name}: expected [T, H, {D}] fp16 CUDA rows {row_stride} "
+                                 f"elements apart, got {tuple(t.shape)} strides {t.stride()}")
+    else:
+        for name, t in (("q", q), ("k", k), ("v", v)):
+            _need(t, torch.float16, (T, H, D), name)
     if rope_cos is not None:
         _need(rope_cos, torch.float32, (T, D // 2), "rope_cos")
         _need(rope_sin, torch.float32, (T, D // 2), "rope_sin")
     cu = np.ascontiguousarray(np.asarray(cu_seqlens, dtype=np.uint32))
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty((T, H, D), dtype=torch.float16, device=q.device)
     ws_bytes = 0
     if rope_cos is not None:
         ws_bytes = vision_workspace_bytes(T, H, D)
@@ -66,10 +79,17 @@ def vision_varlen_attention(q, k, v, cu_seqlens, rope_cos=None, rope_sin=None, o
             workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
         _need(workspace, torch.uint8, None, "workspace")
         ws_bytes = workspace.numel()
+    wsp = _ptr(workspace if rope_cos is not None else None)
+    if strided:
+        st = abi.lib().pvlc_attn_vision_varlen_strided_ws(
+            _ptr(q), _ptr(k), _ptr(v), row_stride, cu.ctypes.data_as(ctypes.c_void_p),
+            max(len(cu) - 1, 0), T, H, D, _ptr(rope_cos), _ptr(rope_sin), wsp, ws_bytes,
+            _ptr(out), _stream())
+        abi.check(st, "pvlc_attn_vision_varlen_strided_ws")
+        return out
     st = abi.lib().pvlc_attn_vision_varlen_ws(
         _ptr(q), _ptr(k), _ptr(v), cu.ctypes.data_as(ctypes.c_void_p), max(len(cu) - 1, 0), T, H,
-        D, _ptr(rope_cos), _ptr(rope_sin), _ptr(workspace if rope_cos is not None else None),
-        ws_bytes, _ptr(out), _stream())
+        D, _ptr(rope_cos), _ptr(rope_sin), wsp, ws_bytes, _ptr(out), _stream())
     abi.check(st, "pvlc_attn_vision_varlen_ws")
     return out
 
@@ -281,3 +301,35 @@ def silu_mul(gate_up, out=None):
     abi.check(abi.lib().pvlc_silu_mul(_ptr(gate_up), rows, w2 // 2, _ptr(out), _stream()),
               "pvlc_silu_mul")
     return out
+
+
+LM_HEAD_MAX_ROWS = 256          # PVLC_LM_HEAD_MAX_ROWS
+
+
+def lm_head_top1(hidden, lm_head, tokens=None, logits=None, workspace=None):
+    """Greedy top-1 over the LM head without materialising the logits
+    (pvlc_lm_head_top1): hidden [rows, K] fp16 (the final-norm output), lm_head
+    [vocab, K] fp16 -> int32 token ids [rows] (the largest f32 logit; equal logits go to
+    the smaller id).  logits, when given, is a [rows] f32 tensor that receives the
+    winning logit.  Rows beyond 256 are taken in groups of 256."""
+    rows, K = hidden.shape
+    V = lm_head.shape[0]
+    _need(hidden, torch.float16, (rows, K), "hidden")
+    _need(lm_head, torch.float16, (V, K), "lm_head")
+    if tokens is None:
+        tokens = torch.empty(rows, dtype=torch.int32, device=hidden.device)
+    _need(tokens, torch.int32, (rows,), "tokens")
+    if logits is not None:
+        _need(logits, torch.float32, (rows,), "logits")
+    need = int(abi.lib().pvlc_lm_head_top1_workspace_bytes(min(rows, LM_HEAD_MAX_ROWS)))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=hidden.device)
+    _need(workspace, torch.uint8, None, "workspace")
+    for r0 in range(0, rows, LM_HEAD_MAX_ROWS):
+        r1 = min(rows, r0 + LM_HEAD_MAX_ROWS)
+        st = abi.lib().pvlc_lm_head_top1(
+            _ptr(hidden[r0:r1]), r1 - r0, _ptr(lm_head), V, K, _ptr(workspace),
+            workspace.numel(), _ptr(tokens[r0:r1]),
+            _ptr(logits[r0:r1] if logits is not None else None), _stream())
+        abi.check(st, "pvlc_lm_head_top1")
+    return tokens

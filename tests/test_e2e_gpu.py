@@ -86,6 +86,8 @@ def test_e2e_greedy_matches_oracle(engine_and_weights):
         patches.append(ops.image_patches(dev, pre.resized_height, pre.resized_width))
         grids.append(pre.image_grid_thw)
     res = eng.generate(patches, grids, MAX_NEW, chunk=8, record_logits=True)
+    # the serving path: greedy top-1 straight from the LM head (pvlc_lm_head_top1)
+    fused = eng.generate(patches, grids, MAX_NEW, chunk=8, record_logits=False)
     dims = cfg.oracle_dims()
     report = []
     for b, (rgb, pre) in enumerate(reqs):
@@ -110,6 +112,7 @@ def test_e2e_greedy_matches_oracle(engine_and_weights):
         assert err0 <= 1e-2, err0
         # the north star's rule: the same tokens as the plain f32 reference, every step
         assert res["tokens"][b] == f32["tokens"], (b, res["tokens"][b], f32["tokens"])
+        assert list(fused["tokens"][b]) == f32["tokens"], (b, fused["tokens"][b])
         same = len(f32["tokens"])
         report.append(dict(request=b, tokens=len(ref["tokens"]), max_rel_logit_err=max(errs),
                            min_margin=min(margins), f32_prefill_rel_err=err0,
@@ -133,6 +136,7 @@ def test_e2e_config4_page_matches_f32_oracle(engine_and_weights):
     patches = ops.image_patches(torch.from_numpy(rgb).cuda(), pre.resized_height,
                                 pre.resized_width)
     res = eng.generate([patches], [g], steps, chunk=steps, record_logits=True)
+    fused = eng.generate([patches], [g], steps, chunk=steps, record_logits=False)
     ids = M.ocr_prompt_ids(g[0] * g[1] * g[2] // 4, cfg)
     assert len(ids) == 1238
     f32 = O.generate(cfg.oracle_dims(), vw, pw, dw, pre.values, [g], ids, steps,
@@ -144,3 +148,4 @@ def test_e2e_config4_page_matches_f32_oracle(engine_and_weights):
                                    prefill_rel_err=rel0, top1_margin=float(top2[1] - top2[0])))
     assert rel0 <= 1e-2, rel0
     assert res["tokens"][0] == f32["tokens"], (res["tokens"][0], f32["tokens"])
+    assert list(fused["tokens"][0]) == f32["tokens"], (fused["tokens"][0], f32["tokens"])

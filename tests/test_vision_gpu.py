@@ -247,3 +247,37 @@ def test_many_ragged_segments_persistent_schedule(cuda_lib, rope):
     err = float(np.abs(out.float().cpu().numpy().reshape(-1) - ref.reshape(-1)).max())
     assert err <= 2e-3, err
     assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_strided_qkv_matches_packed(cuda_lib, rope):
+    """q, k, v as the three column blocks of one [T, 3 x 1152] projection output
+    (pvlc_attn_vision_varlen_strided_ws) give the packed call's outputs bit for bit;
+    a stride below heads x 72 or not a multiple of 8 is refused before any launch."""
+    import ctypes
+    from pvlc_b200 import abi, ops, positions
+    grids = [(1, 12, 16), (1, 9, 7), (1, 20, 20)]
+    lens = [t * h * w for t, h, w in grids]
+    cu = np.concatenate([[0], np.cumsum(lens)]).tolist()
+    T = cu[-1]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(12)
+    qkv = torch.randn((T, 3 * H * D), generator=g, device="cuda").half()
+    q, k, v = (qkv[:, j * H * D:(j + 1) * H * D].view(T, H, D) for j in range(3))
+    tabs = (None, None)
+    if rope:
+        tabs = tuple(torch.from_numpy(x).cuda() for x in positions.vision_rope_tables(grids))
+    got = ops.vision_varlen_attention(q, k, v, cu, *tabs)
+    ref = ops.vision_varlen_attention(q.contiguous(), k.contiguous(), v.contiguous(), cu, *tabs)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+    cuh = np.asarray(cu, np.uint32)
+    ws = torch.empty(ops.vision_workspace_bytes(T, H), dtype=torch.uint8, device="cuda")
+    out = torch.empty((T, H, D), dtype=torch.float16, device="cuda")
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    f = abi.lib().pvlc_attn_vision_varlen_strided_ws
+    for bad in (H * D - 8, H * D + 4):
+        st = f(P(q), P(k), P(v), bad, cuh.ctypes.data_as(ctypes.c_void_p), 3, T, H, D,
+               P(tabs[0]), P(tabs[1]), P(ws), ws.numel(), P(out), stream)
+        assert st == abi.LENGTH_MISMATCH
