@@ -310,8 +310,6 @@ def run_gpu(args, rank, world, local_rank, dist):
     kernel_achieved = (algorithmic_decode_bytes(k_lengths) / len(kernel_ms)) / (avg_kernel_ms * 1e-3) / 1e9
 
     components = {}
-    if rank == 0 and not args.skip_components:
-        components = run_components(args, dev, tf_peak, peak_src)
     del kc, vc, kp, vp, q, kn, vn, out, ws, qh, knh, vnh, outh, sets
     torch.cuda.empty_cache()
     if not args.skip_e2e:
@@ -1054,6 +1052,14 @@ def main():
         if dist is not None:
             dist.barrier()
             dist.destroy_process_group()
+        # the single-GPU components run on rank 0 after the last collective, so no
+        # rank waits in one while they run
+        if line is not None and not args.skip_components:
+            import torch
+            _, tf_peak, peak_src = peaks()
+            comps = run_components(args, torch.device("cuda", local_rank), tf_peak, peak_src)
+            comps.update(line["components"])
+            line["components"] = comps
     if line is not None:
         emit(line)
 

@@ -101,10 +101,15 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 #define PVLC_PREFILL_EXP_POLY_MASK 0x4924u
 #endif
 constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
-// 1: the exponent phase as a rolled loop over 32-key chunks (see the softmax)
-#ifndef PVLC_PREFILL_ROLLED
-#define PVLC_PREFILL_ROLLED 1
+// 1: batched launches run the persistent kernel (prefill_persist_kernel)
+#ifndef PVLC_PREFILL_PERSIST
+#define PVLC_PREFILL_PERSIST 1
 #endif
+// 1: a persistent CTA rotates the next item's Q before writing the current output
+#ifndef PVLC_PREFILL_EARLY_ROT
+#define PVLC_PREFILL_EARLY_ROT 1
+#endif
+
 
 struct Maps {
   // q, v: the packed input rows; k: the KV caches (rotated keys) as
@@ -128,6 +133,7 @@ struct Params {
 template <int MAXB>
 struct Prompts {
   uint32_t count;
+  uint32_t ranks_max;              // largest CTA count of a prompt (persistent item slots)
   uint32_t cta_prefix[MAXB + 1];   // CTAs (per KV head) of the prompts before b
   uint32_t row0[MAXB + 1];         // first packed row of prompt b; row0[count] = rows
   uint32_t rope_rows[MAXB];
@@ -203,15 +209,17 @@ __device__ __forceinline__ uint8_t* chunk_addr(uint8_t* blk, int r, int c) {
 // M-RoPE table entries of one Q row's chunks c0..c0+3 (dims 8c..8c+7 and
 // their partners 64 above): [chunk][cos lo 2, cos hi 2, sin lo 2, sin hi 2].
 // Loaded before the Q tile lands, so the table latency overlaps the TMA load.
+template <int NC = 4>
 struct RowTables {
-  float4 v[4][8];
+  float4 v[NC][8];
 };
 
-__device__ __forceinline__ void mrope_tables(RowTables& t, const float* rope_cos,
+template <int NC>
+__device__ __forceinline__ void mrope_tables(RowTables<NC>& t, const float* rope_cos,
                                              const float* rope_sin, uint32_t rope_rows,
                                              uint32_t token, int c0) {
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
+  for (int u = 0; u < NC; ++u) {
     const int c = c0 + u;
     const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
     const size_t tb = ((size_t)axis * rope_rows + token) * HD + 8 * c;
@@ -230,10 +238,11 @@ __device__ __forceinline__ void mrope_tables(RowTables& t, const float* rope_cos
 
 // M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in
 // place: chunks c0..c0+3 of 8 dims (dims 8c..8c+7 and their partners 64 above).
-__device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const RowTables& t,
+template <int NC>
+__device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const RowTables<NC>& t,
                                           int c0) {
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
+  for (int u = 0; u < NC; ++u) {
     const int c = c0 + u;
     const float4 cl0 = t.v[u][0], cl1 = t.v[u][1], ch0 = t.v[u][2], ch1 = t.v[u][3];
     const float4 sl0 = t.v[u][4], sl1 = t.v[u][5], sh0 = t.v[u][6], sh1 = t.v[u][7];
@@ -262,6 +271,111 @@ __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
   uint64_t r;
   asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
   return r;
+}
+
+// One online-softmax step of stream tile row i (TMEM lane i) over K tile j:
+// S from TMEM columns [tS, tS + 128), causal mask past `token` (also removing
+// cache rows past the prompt), lazy running max (O rescaled in TMEM, after
+// waiting for the previous PV through o_done at parity o_prev_parity, only
+// when a row max grows by more than RESCALE_THRESHOLD), then P = 2^(x - m)
+// as fp16 written over S (P of keys 2c, 2c + 1 in column c) and the row sum
+// of that fp16 P added to l_run.  Returns false when a wait timed out.
+__device__ __forceinline__ bool softmax_step(uint32_t tS, uint32_t tO, int j, uint32_t token,
+                                         uint32_t warp_tok_lo, bool has_prev,
+                                         uint64_t* o_done, uint32_t o_prev_parity,
+                                         float scale, uint64_t scale2, float& m_run,
+                                         float& l_run) {
+  tc::fence_after_sync();
+  uint32_t sv[128];
+  tc::tmem_ld32(tS + 0, sv);
+  tc::tmem_ld32(tS + 32, sv + 32);
+  tc::tmem_ld32(tS + 64, sv + 64);
+  tc::tmem_ld32(tS + 96, sv + 96);
+  tc::tmem_wait_ld();
+  // causal mask where this tile reaches past the warp's first token;
+  // it also removes cache rows past the prompt (unwritten, any bits)
+  if (j * BN + BN - 1 > warp_tok_lo) {
+#pragma unroll
+    for (int c = 0; c < 128; ++c)
+      if (j * BN + c > token) sv[c] = __float_as_uint(-CUDART_INF_F);
+  }
+  // row max over four independent chains
+  float m4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
+                 __uint_as_float(sv[3])};
+#pragma unroll
+  for (int c = 4; c < 124; c += 8) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      m4[e] = fmax3(m4[e], __uint_as_float(sv[c + 2 * e]), __uint_as_float(sv[c + 2 * e + 1]));
+  }
+  m4[0] = fmax3(m4[0], __uint_as_float(sv[124]), __uint_as_float(sv[125]));
+  m4[1] = fmax3(m4[1], __uint_as_float(sv[126]), __uint_as_float(sv[127]));
+  const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
+  const bool need = mx > m_run + RESCALE_THRESHOLD;
+  float alpha = 1.f;
+  if (need) {
+    alpha = fast_exp2(m_run - mx);
+    m_run = mx;
+    l_run *= alpha;
+  }
+  if (has_prev && __any_sync(0xffffffffu, need)) {
+    if (!__all_sync(0xffffffffu, mbar_wait(o_done, o_prev_parity))) return false;
+    tc::fence_after_sync();
+#pragma unroll
+    for (int cc = 0; cc < 128; cc += 16) {
+      uint32_t ov[16];
+      tc::tmem_ld16(tO + cc, ov);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+      tc::tmem_st16(tO + cc, ov);
+    }
+  }
+  // a row whose keys in this stream are all masked keeps m = -inf: its
+  // P is 0 (guard the subtraction)
+  const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
+  // P = 2^(x - m) as fp16 pairs, split between two pipes as in the
+  // vision kernel: the pairs of EXP_POLY_MASK by the polynomial on the
+  // FMA / integer pipes, the others by one f32 -> f16x2 rounding and one
+  // MUFU operation per two values.  The row sum adds the fp16 P the PV
+  // product consumes, in f32, over two accumulator chains.
+  const uint64_t negm2 = f2_pack(-mm, -mm);
+  const uint64_t negmh2 = f2_pack(6.5f - mm, 6.5f - mm);   // exp2_h2_poly takes x + 6.5
+  uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  // One 32-key chunk per trip of a rolled loop, S reloaded from TMEM (P of
+  // chunk c lands in columns 16c..16c+15, below every chunk still to be
+  // read): a quarter of the code of the unrolled form, which missed in
+  // the instruction cache.
+  const bool diag = j * BN + BN - 1 > warp_tok_lo;
+#pragma unroll 1
+  for (int ch = 0; ch < 4; ++ch) {
+    uint32_t sc[32];
+    tc::tmem_ld32(tS + 32 * ch, sc);
+    tc::tmem_wait_ld();
+    if (diag) {
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        if (j * BN + 32 * ch + c > token) sc[c] = __float_as_uint(-CUDART_INF_F);
+    }
+    uint32_t pk[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      const uint64_t s2 = f2_pack(__uint_as_float(sc[2 * c]), __uint_as_float(sc[2 * c + 1]));
+      if ((EXP_POLY_MASK >> c) & 1u) {
+        pk[c] = exp2_h2_poly(f2_fma(s2, scale2, negmh2));
+      } else {
+        const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
+        pk[c] = ex2_h2(pack_half2(x.x, x.y));
+      }
+      const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
+      sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
+    }
+    tc::tmem_st16(tS + 16 * ch, pk);
+  }
+  tc::tmem_wait_st();
+  const float2 sum = f2_unpack(f2_add(sum2[0], sum2[1]));
+  l_run += sum.x + sum.y;
+  return true;
 }
 
 template <int MAXB>
@@ -502,7 +616,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* qb0 = smem + OFF_Q + (pair ? t * Q_BYTES : 0);
     bool ok = true;
     {
-      RowTables rt;
+      RowTables<4> rt;
       const int c0 = pair ? 0 : 4 * t;
       const float* rcos = pr.rope_cos[pi];
       const float* rsin = pr.rope_sin[pi];
@@ -537,117 +651,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         good = false;
         break;
       }
-      tc::fence_after_sync();
-      uint32_t sv[128];
-      tc::tmem_ld32(tS + 0, sv);
-      tc::tmem_ld32(tS + 32, sv + 32);
-      tc::tmem_ld32(tS + 64, sv + 64);
-      tc::tmem_ld32(tS + 96, sv + 96);
-      tc::tmem_wait_ld();
-      // causal mask where this tile reaches past the warp's first token;
-      // it also removes cache rows past the prompt (unwritten, any bits)
-      if (j * BN + BN - 1 > warp_tok_lo) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (j * BN + c > token) sv[c] = __float_as_uint(-CUDART_INF_F);
+      if (!softmax_step(tS, tO, j, token, warp_tok_lo, step > 0, &o_done[t], (step - 1) & 1,
+                        scale, scale2, m_run, l_run)) {
+        good = false;
+        break;
       }
-      // row max over four independent chains
-      float m4[4] = {__uint_as_float(sv[0]), __uint_as_float(sv[1]), __uint_as_float(sv[2]),
-                     __uint_as_float(sv[3])};
-#pragma unroll
-      for (int c = 4; c < 124; c += 8) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          m4[e] = fmax3(m4[e], __uint_as_float(sv[c + 2 * e]), __uint_as_float(sv[c + 2 * e + 1]));
-      }
-      m4[0] = fmax3(m4[0], __uint_as_float(sv[124]), __uint_as_float(sv[125]));
-      m4[1] = fmax3(m4[1], __uint_as_float(sv[126]), __uint_as_float(sv[127]));
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * scale;
-      const bool need = mx > m_run + RESCALE_THRESHOLD;
-      float alpha = 1.f;
-      if (need) {
-        alpha = fast_exp2(m_run - mx);
-        m_run = mx;
-        l_run *= alpha;
-      }
-      if (step > 0 && __any_sync(0xffffffffu, need)) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (step - 1) & 1))) { good = false; break; }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int cc = 0; cc < 128; cc += 16) {
-          uint32_t ov[16];
-          tc::tmem_ld16(tO + cc, ov);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tc::tmem_st16(tO + cc, ov);
-        }
-      }
-      // a row whose keys in this stream are all masked keeps m = -inf: its
-      // P is 0 (guard the subtraction)
-      const float mm = m_run == -CUDART_INF_F ? 0.f : m_run;
-      // P = 2^(x - m) as fp16 pairs, split between two pipes as in the
-      // vision kernel: the pairs of EXP_POLY_MASK by the polynomial on the
-      // FMA / integer pipes, the others by one f32 -> f16x2 rounding and one
-      // MUFU operation per two values.  The row sum adds the fp16 P the PV
-      // product consumes, in f32, over two accumulator chains.
-      const uint64_t negm2 = f2_pack(-mm, -mm);
-      const uint64_t negmh2 = f2_pack(6.5f - mm, 6.5f - mm);   // exp2_h2_poly takes x + 6.5
-      uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-#if PVLC_PREFILL_ROLLED
-      // One 32-key chunk per trip of a rolled loop, S reloaded from TMEM (P of
-      // chunk c lands in columns 16c..16c+15, below every chunk still to be
-      // read): a quarter of the code of the unrolled form, which missed in
-      // the instruction cache.
-      const bool diag = j * BN + BN - 1 > warp_tok_lo;
-#pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t sc[32];
-        tc::tmem_ld32(tS + 32 * ch, sc);
-        tc::tmem_wait_ld();
-        if (diag) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (j * BN + 32 * ch + c > token) sc[c] = __float_as_uint(-CUDART_INF_F);
-        }
-        uint32_t pk[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint64_t s2 = f2_pack(__uint_as_float(sc[2 * c]), __uint_as_float(sc[2 * c + 1]));
-          if ((EXP_POLY_MASK >> c) & 1u) {
-            pk[c] = exp2_h2_poly(f2_fma(s2, scale2, negmh2));
-          } else {
-            const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
-            pk[c] = ex2_h2(pack_half2(x.x, x.y));
-          }
-          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
-          sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
-        }
-        tc::tmem_st16(tS + 16 * ch, pk);
-      }
-#else
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int k = 32 * ch + 2 * c;
-          const uint64_t s2 = f2_pack(__uint_as_float(sv[k]), __uint_as_float(sv[k + 1]));
-          if ((EXP_POLY_MASK >> c) & 1u) {
-            pk[c] = exp2_h2_poly(f2_fma(s2, scale2, negmh2));
-          } else {
-            const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
-            pk[c] = ex2_h2(pack_half2(x.x, x.y));
-          }
-          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
-          sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
-        }
-        tc::tmem_st16(tS + 16 * ch, pk);
-      }
-#endif
-      tc::tmem_wait_st();
-      const float2 sum = f2_unpack(f2_add(sum2[0], sum2[1]));
-      l_run += sum.x + sum.y;
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[t]);
@@ -748,6 +756,381 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+inline uint32_t umin_host(uint32_t a, uint32_t b) { return a < b ? a : b; }
+
+// ------------------------------------------------------------------------
+// 3. Persistent attention for a batched launch.  One CTA per SM walks the
+// work items (a prompt's adjacent Q tiles n-1-2r and n-2-2r, one per stream,
+// sharing every K/V tile; an odd prompt's tile 0 alone on stream 0) in a
+// static round-robin over an order that lists every prompt's heaviest items
+// first.  Barrier phases run on across items: the producer loads item n+1's
+// Q tiles as soon as the last QK of item n has been issued for each stream
+// (q_free), each softmax warpgroup rotates its row of the next item's Q tile
+// right after its last P of item n and only then writes item n's output, so
+// the next item's first S is computed while the current epilogue runs.
+//
+// Items: index x of [0, prompts * ranks_max * 2): prompt b = x / (2 ranks_max),
+// rank r = (x / 2) mod ranks_max (the prompt's heaviest first), KV head
+// g = x mod 2; a rank past the prompt's CTA count is empty and skipped.
+// Prompt-major, so the CTAs working at one time share a few prompts' keys and
+// values in L2: a rank-major order (every prompt's heaviest items first)
+// spread them over the whole launch and measured 13 % slower (3.14 against
+// 2.77 ms for 256 x 1238 tokens).  Against one CTA per item (the same tiles,
+// prefill_attn_kernel) the persistent form gains ~1 % (2.77 against 2.80 ms);
+// rotating the next Q after the epilogue instead of before it loses ~3 %.
+constexpr uint32_t OFF_BARS_P = OFF_STAGE_PAIR + PAIR_STAGES * STAGE_BYTES;
+// q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2], q_free[2]
+constexpr int NBARS_P = 14;
+constexpr uint32_t OFF_MISC_P = OFF_BARS_P + NBARS_P * 8;
+constexpr uint32_t SMEM_BYTES_P = OFF_MISC_P + 64 + 1024;
+static_assert(SMEM_BYTES_P <= 227 * 1024, "persistent prefill shared memory exceeds the limit");
+
+struct Item {
+  uint32_t pi, g, row0, tokens;
+  uint32_t tile0[STREAMS];
+  int nks[STREAMS];   // K tiles of each stream (0: stream idle)
+  bool valid;
+};
+
+template <int MAXB>
+__device__ __forceinline__ Item item_at(uint32_t x, const Prompts<MAXB>& pr) {
+  Item it;
+  const uint32_t R = pr.ranks_max;
+  it.pi = x / (2 * R);
+  const uint32_t rem = x - it.pi * 2 * R;
+  const uint32_t r = rem >> 1;
+  it.g = rem & 1;
+  it.row0 = pr.row0[it.pi];
+  it.tokens = pr.row0[it.pi + 1] - it.row0;
+  const uint32_t n_qt = (it.tokens + TOK - 1) / TOK;
+  it.valid = r < pr.cta_prefix[it.pi + 1] - pr.cta_prefix[it.pi];
+  it.tile0[0] = it.tile0[1] = 0;
+  it.nks[0] = it.nks[1] = 0;
+  if (!it.valid) return it;
+  const uint32_t qa = n_qt - 1 - 2 * r;
+  it.tile0[0] = qa * TOK;
+  it.nks[0] = static_cast<int>((umin32(qa * TOK + TOK, it.tokens) - 1) / BN) + 1;
+  if (qa >= 1) {
+    const uint32_t qb = qa - 1;
+    it.tile0[1] = qb * TOK;
+    it.nks[1] = static_cast<int>((umin32(qb * TOK + TOK, it.tokens) - 1) / BN) + 1;
+  }
+  return it;
+}
+
+template <int MAXB>
+__global__ void __launch_bounds__(THREADS, 1)
+    prefill_persist_kernel(const __grid_constant__ Maps maps, const Params p,
+                           const __grid_constant__ Prompts<MAXB> pr, uint32_t n_items) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BARS_P);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_ready = bars + 1;
+  uint64_t* kv_full = bars + 2;    // [2]
+  uint64_t* kv_empty = bars + 4;   // [2]
+  uint64_t* s_full = bars + 6;     // [2] per stream
+  uint64_t* p_ready = bars + 8;    // [2]
+  uint64_t* o_done = bars + 10;    // [2]
+  uint64_t* q_free = bars + 12;    // [2] the item's last QK of the stream is complete
+  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC_P);
+  // misc[0]: TMEM base, misc[1]: abort
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t first_x = blockIdx.x, step_x = gridDim.x;
+  // the next valid item index at or after x (n_items when none)
+  auto next_item = [&](uint32_t x) -> uint32_t {
+    while (x < n_items && !item_at<MAXB>(x, pr).valid) x += step_x;
+    return x < n_items ? x : n_items;
+  };
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 8);
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < STREAMS; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&o_done[t], 1);
+      mbar_init(&q_free[t], 1);
+    }
+    misc[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tc::tmem_alloc(const_cast<uint32_t*>(misc), TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = misc[0];
+
+  const int wg = warp >> 2;
+  if (wg == 2) {
+    tc::regs_dec<REGS_CTRL>();
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------- TMA producer
+      tc::tma_prefetch_desc(&maps.q);
+      tc::tma_prefetch_desc(&maps.k);
+      tc::tma_prefetch_desc(&maps.v);
+      bool waited = false;     // pdl_wait done (keys come from the preceding kv_rope_kernel)
+      uint32_t G = 0;          // K/V tiles loaded so far (ring position)
+      uint32_t n = 0;          // items so far
+      for (uint32_t x = next_item(first_x); x < n_items && !misc[1];
+           x = next_item(x + step_x), ++n) {
+        const Item it = item_at<MAXB>(x, pr);
+        if (n > 0 && (!mbar_wait(&q_free[0], (n - 1) & 1) || !mbar_wait(&q_free[1], (n - 1) & 1))) {
+          misc[1] = 1;
+          break;
+        }
+        const int nq = it.nks[1] > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(q_full, nq * Q_BYTES);
+        for (int t = 0; t < nq; ++t)
+          for (int b = 0; b < 2; ++b)
+            tc::tma_load_3d(smem + OFF_Q + t * Q_BYTES + b * SZ_W, &maps.q, 64 * b,
+                            GROUP * it.g, it.row0 + it.tile0[t], q_full);
+        if (!waited) {
+          pdl_wait();
+          waited = true;
+        }
+        for (int j = 0; j < it.nks[0]; ++j, ++G) {
+          const int s = G % PAIR_STAGES;
+          if (misc[1] || !mbar_wait(&kv_empty[s], ((G / PAIR_STAGES) & 1) ^ 1)) {
+            misc[1] = 1;
+            break;
+          }
+          uint8_t* st = smem + OFF_STAGE_PAIR + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
+          for (int b = 0; b < 2; ++b) {
+            tc::tma_load_4d(st + ST_K + b * SZ_W, &maps.k, 64 * b, it.g, j * BN, it.pi,
+                            &kv_full[s]);
+            tc::tma_load_3d(st + ST_V + b * SZ_W, &maps.v, 64 * b, it.g, it.row0 + j * BN,
+                            &kv_full[s]);
+          }
+        }
+      }
+      // the last loads must land before the CTA may exit
+      for (uint32_t g2 = (G > PAIR_STAGES ? G - PAIR_STAGES : 0); g2 < G; ++g2)
+        mbar_wait(&kv_full[g2 % PAIR_STAGES], (g2 / PAIR_STAGES) & 1);
+      if (n > 0) mbar_wait(q_full, (n - 1) & 1);
+    } else if (warp == 9) {
+      // ---------------------------------------------------- MMA issuer
+      // per item: both streams' first QK, then per K tile j and stream the PV of
+      // tile j and the QK of tile j + 1; q_free[t] is committed right after the
+      // stream's last QK of the item (its Q buffer may then be refilled)
+      constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
+      const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + OFF_STAGE_PAIR);
+      const uint64_t dq = tc::smem_desc(sq, 16, 1024, tc::kSw128);
+      const uint64_t dk = tc::smem_desc(st0 + ST_K, 16, 1024, tc::kSw128);
+      const uint64_t dv = tc::smem_desc(st0 + ST_V, SZ_W, 1024, tc::kSw128);
+      auto qk = [&](int t, int s) {
+        const uint32_t tS = tmem + 128u * t;
+        const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        const uint64_t qo = (uint64_t)t * (Q_BYTES >> 4);
+        if (tc::elect_one()) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t off = (uint64_t)(ks >> 2) * (SZ_W >> 4) + 2 * (ks & 3);
+            tc::mma_ss(tS, dq + qo + off, dk + so + off, idesc_qk, ks > 0);
+          }
+          tc::commit(&s_full[t]);
+        }
+        __syncwarp();
+      };
+      auto pv = [&](int t, int s, bool first, bool release) {
+        const uint32_t tS = tmem + 128u * t, tO = tmem + 256u + 128u * t;
+        const uint64_t so = (uint64_t)s * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            tc::mma_ts(tO, tS + ks * 8, dv + so + 128 * ks, idesc_pv, (!first || ks > 0) ? 1u : 0u);
+          tc::commit(&o_done[t]);
+          if (release) tc::commit(&kv_empty[s]);
+        }
+        __syncwarp();
+      };
+      auto commit_free = [&](int t) {
+        if (tc::elect_one()) tc::commit(&q_free[t]);
+        __syncwarp();
+      };
+      constexpr uint32_t kAll = 0xffffffffu;
+      uint32_t G = 0;                        // K/V tiles consumed so far
+      uint32_t steps[STREAMS] = {0, 0};      // P hand-offs (= PVs issued) per stream so far
+      uint32_t n = 0;
+      bool ok = true;
+      for (uint32_t x = next_item(first_x); x < n_items && ok; x = next_item(x + step_x), ++n) {
+        const Item it = item_at<MAXB>(x, pr);
+        const int nk = it.nks[0];
+        ok = __all_sync(kAll, misc[1] == 0 && mbar_wait(q_ready, n & 1) &&
+                                  mbar_wait(&kv_full[G % PAIR_STAGES], (G / PAIR_STAGES) & 1));
+        if (!ok) break;
+        tc::fence_after_sync();
+        const int s0 = G % PAIR_STAGES;
+        qk(0, s0);
+        if (nk == 1) commit_free(0);
+        if (it.nks[1] > 0) {
+          qk(1, s0);
+          if (it.nks[1] == 1) commit_free(1);
+        } else {
+          commit_free(1);   // stream 1 idle in this item
+        }
+        for (int j = 0; j < nk && ok; ++j) {
+          const int s = (G + j) % PAIR_STAGES, s1 = (G + j + 1) % PAIR_STAGES;
+          const uint32_t gn = G + j + 1;
+          if (j + 1 < nk &&
+              !__all_sync(kAll, misc[1] == 0 &&
+                                    mbar_wait(&kv_full[s1], (gn / PAIR_STAGES) & 1))) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int t = 0; t < STREAMS; ++t) {
+            if (j >= it.nks[t]) continue;
+            if (!__all_sync(kAll, mbar_wait(&p_ready[t], steps[t] & 1))) { ok = false; break; }
+            ++steps[t];
+            tc::fence_after_sync();
+            // stream 1's tiles are a prefix of stream 0's: the last reader of
+            // tile j is stream 1 while it still has tiles
+            pv(t, s, j == 0, t == 1 || j >= it.nks[1]);
+            if (j + 1 < it.nks[t]) {
+              qk(t, s1);
+              if (j + 2 == it.nks[t]) commit_free(t);
+            }
+          }
+        }
+        if (ok) G += nk;
+      }
+      if (!ok && lane == 0) misc[1] = 1;
+      // never exit with MMAs in flight or commit arrivals still pending
+#pragma unroll
+      for (int t = 0; t < STREAMS; ++t)
+        if (steps[t] > 0) mbar_wait(&o_done[t], (steps[t] - 1) & 1);
+      if (n > 0) {
+        mbar_wait(&q_free[0], (n - 1) & 1);
+        mbar_wait(&q_free[1], (n - 1) & 1);
+      }
+    }
+  } else {
+    tc::regs_inc<REGS_SOFTMAX>();
+    // ------------------------------------------------------ softmax
+    const int t = wg;                                // stream of this warpgroup
+    const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + 128u * t;
+    const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+    const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
+    const uint64_t scale2 = f2_pack(scale, scale);
+    uint8_t* qb0 = smem + OFF_Q + t * Q_BYTES;
+    // M-RoPE of this thread's row of stream t's Q tile of item `it` (q_full
+    // phase `ph`), then the q_ready arrival (also for an idle stream)
+    auto rotate = [&](const Item& it, uint32_t ph) -> bool {
+      const uint32_t token = it.tile0[t] + (i >> 3);
+      const bool mine = it.nks[t] > 0 && token < it.tokens;
+      const float* rc = pr.rope_cos[it.pi];
+      const float* rs = pr.rope_sin[it.pi];
+      const uint32_t rr = pr.rope_rows[it.pi];
+      // two chunks (16 dims and their partners) of tables at a time: live state
+      // is high here (the current item's epilogue follows)
+      RowTables<2> rt;
+      if (mine) mrope_tables(rt, rc, rs, rr, token, 0);
+      const bool landed = mbar_wait(q_full, ph);
+      if (landed && mine) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < 8; c0 += 2) {
+          if (c0 > 0) mrope_tables(rt, rc, rs, rr, token, c0);
+          mrope_row(qb0, qb0 + SZ_W, i, rt, c0);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      return landed;
+    };
+    uint32_t step_g = 0;     // this stream's steps so far (s_full / p_ready / o_done phases)
+    uint32_t n = 0;
+    uint32_t x = next_item(first_x);
+    bool good = x >= n_items || __all_sync(0xffffffffu, rotate(item_at<MAXB>(x, pr), 0));
+    for (; x < n_items && good; ++n) {
+      const Item it = item_at<MAXB>(x, pr);
+      const int my_nk = it.nks[t];
+      const uint32_t token = it.tile0[t] + (i >> 3);
+      const uint32_t warp_tok_lo = it.tile0[t] + ((warp & 3) * 32 >> 3);
+      float m_run = -CUDART_INF_F, l_run = 0.f;
+      for (int step = 0; step < my_nk && good; ++step, ++step_g) {
+        if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&s_full[t], step_g & 1))) {
+          good = false;
+          break;
+        }
+        if (!softmax_step(tS, tO, step, token, warp_tok_lo, step > 0, &o_done[t],
+                          (step_g - 1) & 1, scale, scale2, m_run, l_run)) {
+          good = false;
+          break;
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
+      }
+      if (!good) break;
+      // the next item's Q row first (its QK then runs during this epilogue)
+      const uint32_t xn = next_item(x + step_x);
+#if PVLC_PREFILL_EARLY_ROT
+      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
+        good = false;
+        break;
+      }
+#endif
+      if (my_nk > 0) {
+        // epilogue: this stream's O / l -> all 128 columns of the row
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (step_g - 1) & 1))) {
+          good = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const bool store = token < it.tokens;
+        __half* orow = p.out + ((size_t)(it.row0 + token) * QH + GROUP * it.g + (i & 7)) * HD;
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int cc = 0; cc < 128; cc += 16) {
+          uint32_t ov[16];
+          tc::tmem_ld16(tO + cc, ov);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
+            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
+          }
+        }
+        tc::fence_before_sync();   // the next item's PV may overwrite O after our arrival
+      }
+#if !PVLC_PREFILL_EARLY_ROT
+      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
+        good = false;
+        break;
+      }
+#endif
+      x = xn;
+    }
+    if (!good) misc[1] = 1;
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 8) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -798,13 +1181,21 @@ bool make_cache_map(CUtensorMap* m, const void* base, uint32_t capacity, uint32_
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// kv_rope_kernel then prefill_attn_kernel (programmatic dependent launch) for
-// the prompts of `pr`; grid_y CTAs per KV head.
+// kv_rope_kernel then the attention: prefill_attn_kernel (grid_y CTAs per KV
+// head) or, when `persist_items` is nonzero, prefill_persist_kernel over that
+// many item slots with one CTA per SM (programmatic dependent launch either way).
 template <int MAXB>
 int launch(const void* q, const void* k, const void* v, uint32_t rows, const Prompts<MAXB>& pr,
-           Params p, uint32_t capacity, uint32_t grid_y, cudaStream_t stream) {
-  if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_attn_kernel<MAXB>), SMEM_BYTES) != PVLC_OK)
+           Params p, uint32_t capacity, uint32_t grid_y, cudaStream_t stream,
+           uint32_t persist_items = 0) {
+  if (persist_items) {
+    if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_persist_kernel<MAXB>),
+                                SMEM_BYTES_P) != PVLC_OK)
+      return PVLC_CUDA_ERROR;
+  } else if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_attn_kernel<MAXB>),
+                                     SMEM_BYTES) != PVLC_OK) {
     return PVLC_CUDA_ERROR;
+  }
   if (grid_y == 0 || grid_y > 65535u) return PVLC_INVALID_DECODER_GEOMETRY;
   Maps maps;
   // keys come from the caches (rotated by kv_rope_kernel): rows past a
@@ -830,8 +1221,18 @@ int launch(const void* q, const void* k, const void* v, uint32_t rows, const Pro
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel<MAXB>, maps, p, pr) != cudaSuccess)
+  if (persist_items) {
+    const int sms = device_sm_count();
+    if (sms <= 0) return PVLC_CUDA_ERROR;
+    const uint32_t ctas = umin_host(static_cast<uint32_t>(sms), 2 * grid_y);
+    cfg.gridDim = dim3(ctas);
+    cfg.dynamicSmemBytes = SMEM_BYTES_P;
+    if (cudaLaunchKernelEx(&cfg, prefill_persist_kernel<MAXB>, maps, p, pr, persist_items) !=
+        cudaSuccess)
+      return PVLC_CUDA_ERROR;
+  } else if (cudaLaunchKernelEx(&cfg, prefill_attn_kernel<MAXB>, maps, p, pr) != cudaSuccess) {
     return PVLC_CUDA_ERROR;
+  }
   return cudaPeekAtLastError() == cudaSuccess ? PVLC_OK : PVLC_CUDA_ERROR;
 }
 
@@ -906,8 +1307,21 @@ int prefill_batch_launch(const PrefillBatchArgs& a, cudaStream_t stream) {
   p.k_cache = reinterpret_cast<__half*>(a.k_cache);
   p.v_cache = reinterpret_cast<__half*>(a.v_cache);
   p.out = reinterpret_cast<__half*>(a.out);
+#if PVLC_PREFILL_PERSIST
+  // item slots of the persistent kernel: ranks (CTA count of the longest prompt) x
+  // prompts x KV heads
+  uint32_t ranks = 0;
+  for (uint32_t b = 0; b < a.prompts; ++b)
+    ranks = ranks > pr.cta_prefix[b + 1] - pr.cta_prefix[b] ? ranks
+                                                            : pr.cta_prefix[b + 1] - pr.cta_prefix[b];
+  const uint32_t items = ranks * a.prompts * ptc::KVH;
+  pr.ranks_max = ranks;
+  return ptc::launch<PVLC_PREFILL_MAX_PROMPTS>(a.q, a.k, a.v, a.offsets[a.prompts], pr, p,
+                                               a.capacity, ctas, stream, items);
+#else
   return ptc::launch<PVLC_PREFILL_MAX_PROMPTS>(a.q, a.k, a.v, a.offsets[a.prompts], pr, p,
                                                a.capacity, ctas, stream);
+#endif
 }
 
 }  // namespace pvlc
