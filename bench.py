@@ -741,7 +741,7 @@ def bench_prefill_batch(dev, timeit, tf_peak, peak_src):
            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tf_peak,
                         "unit": "TFLOP/s", "frac": round(tf / tf_peak, 4),
                         "peak_source": peak_src},
-           "kernel": "pvlc::ptc::kv_rope_kernel<256> + pvlc::ptc::prefill_attn_kernel<256>"}
+           "kernel": "pvlc::ptc::kv_rope_kernel<256> + pvlc::ptc::prefill_persist_kernel<256>"}
     # context: the same causal GQA as one batched torch SDPA call (all prompts have the
     # same length here, so a [B, heads, T, 128] batch needs no packing)
     try:
