@@ -105,10 +105,6 @@ constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
 #ifndef PVLC_PREFILL_PERSIST
 #define PVLC_PREFILL_PERSIST 1
 #endif
-// 1: a persistent CTA rotates the next item's Q before writing the current output
-#ifndef PVLC_PREFILL_EARLY_ROT
-#define PVLC_PREFILL_EARLY_ROT 1
-#endif
 
 
 struct Maps {
@@ -236,35 +232,39 @@ __device__ __forceinline__ void mrope_tables(RowTables<NC>& t, const float* rope
   }
 }
 
-// M-RoPE of one 128-dim Q row held in two 128B-swizzled 64-dim blocks, in
-// place: chunks c0..c0+3 of 8 dims (dims 8c..8c+7 and their partners 64 above).
+// M-RoPE of chunk c of one 128-dim Q row r held in two 128B-swizzled 64-dim
+// blocks, in place: dims 8c..8c+7 and their partners 64 above, with that
+// chunk's table entries tv = {cos lo 2, cos hi 2, sin lo 2, sin hi 2}.
+__device__ __forceinline__ void rope_chunk(uint8_t* b0, uint8_t* b1, int r, int c,
+                                           const float4* tv) {
+  const float4 cl0 = tv[0], cl1 = tv[1], ch0 = tv[2], ch1 = tv[3];
+  const float4 sl0 = tv[4], sl1 = tv[5], sh0 = tv[6], sh1 = tv[7];
+  uint4* pa = reinterpret_cast<uint4*>(chunk_addr(b0, r, c));
+  uint4* pb = reinterpret_cast<uint4*>(chunk_addr(b1, r, c));
+  const uint4 a = *pa, b = *pb;
+  const float cl[8] = {cl0.x, cl0.y, cl0.z, cl0.w, cl1.x, cl1.y, cl1.z, cl1.w};
+  const float chh[8] = {ch0.x, ch0.y, ch0.z, ch0.w, ch1.x, ch1.y, ch1.z, ch1.w};
+  const float sl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
+  const float shh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+  uint32_t ra[4], rb[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&aw[e]));
+    const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&bw[e]));
+    ra[e] = pack_half2(x.x * cl[2 * e] + (-y.x) * sl[2 * e], x.y * cl[2 * e + 1] + (-y.y) * sl[2 * e + 1]);
+    rb[e] = pack_half2(y.x * chh[2 * e] + x.x * shh[2 * e], y.y * chh[2 * e + 1] + x.y * shh[2 * e + 1]);
+  }
+  *pa = make_uint4(ra[0], ra[1], ra[2], ra[3]);
+  *pb = make_uint4(rb[0], rb[1], rb[2], rb[3]);
+}
+
+// M-RoPE of one Q row, chunks c0..c0+NC-1, in place.
 template <int NC>
 __device__ __forceinline__ void mrope_row(uint8_t* b0, uint8_t* b1, int r, const RowTables<NC>& t,
                                           int c0) {
 #pragma unroll
-  for (int u = 0; u < NC; ++u) {
-    const int c = c0 + u;
-    const float4 cl0 = t.v[u][0], cl1 = t.v[u][1], ch0 = t.v[u][2], ch1 = t.v[u][3];
-    const float4 sl0 = t.v[u][4], sl1 = t.v[u][5], sh0 = t.v[u][6], sh1 = t.v[u][7];
-    uint4* pa = reinterpret_cast<uint4*>(chunk_addr(b0, r, c));
-    uint4* pb = reinterpret_cast<uint4*>(chunk_addr(b1, r, c));
-    const uint4 a = *pa, b = *pb;
-    const float cl[8] = {cl0.x, cl0.y, cl0.z, cl0.w, cl1.x, cl1.y, cl1.z, cl1.w};
-    const float chh[8] = {ch0.x, ch0.y, ch0.z, ch0.w, ch1.x, ch1.y, ch1.z, ch1.w};
-    const float sl[8] = {sl0.x, sl0.y, sl0.z, sl0.w, sl1.x, sl1.y, sl1.z, sl1.w};
-    const float shh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
-    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-    uint32_t ra[4], rb[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&aw[e]));
-      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&bw[e]));
-      ra[e] = pack_half2(x.x * cl[2 * e] + (-y.x) * sl[2 * e], x.y * cl[2 * e + 1] + (-y.y) * sl[2 * e + 1]);
-      rb[e] = pack_half2(y.x * chh[2 * e] + x.x * shh[2 * e], y.y * chh[2 * e + 1] + x.y * shh[2 * e + 1]);
-    }
-    *pa = make_uint4(ra[0], ra[1], ra[2], ra[3]);
-    *pb = make_uint4(rb[0], rb[1], rb[2], rb[3]);
-  }
+  for (int u = 0; u < NC; ++u) rope_chunk(b0, b1, r, c0 + u, t.v[u]);
 }
 
 __device__ __forceinline__ uint64_t u2_pack(uint32_t lo, uint32_t hi) {
@@ -338,10 +338,11 @@ __device__ __forceinline__ bool softmax_step(uint32_t tS, uint32_t tO, int j, ui
   // vision kernel: the pairs of EXP_POLY_MASK by the polynomial on the
   // FMA / integer pipes, the others by one f32 -> f16x2 rounding and one
   // MUFU operation per two values.  The row sum adds the fp16 P the PV
-  // product consumes, in f32, over two accumulator chains.
+  // product consumes, in f32 (one mixed-precision add per value), over four
+  // accumulator chains.
   const uint64_t negm2 = f2_pack(-mm, -mm);
   const uint64_t negmh2 = f2_pack(6.5f - mm, 6.5f - mm);   // exp2_h2_poly takes x + 6.5
-  uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};   // four row-sum chains
   // One 32-key chunk per trip of a rolled loop, S reloaded from TMEM (P of
   // chunk c lands in columns 16c..16c+15, below every chunk still to be
   // read): a quarter of the code of the unrolled form, which missed in
@@ -367,14 +368,12 @@ __device__ __forceinline__ bool softmax_step(uint32_t tS, uint32_t tO, int j, ui
         const float2 x = f2_unpack(f2_fma(s2, scale2, negm2));
         pk[c] = ex2_h2(pack_half2(x.x, x.y));
       }
-      const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pk[c]));
-      sum2[c & 1] = f2_add(sum2[c & 1], f2_pack(pf.x, pf.y));
+      add_f16x2_to_f32(pk[c], acc[2 * (c & 1)], acc[2 * (c & 1) + 1]);
     }
     tc::tmem_st16(tS + 16 * ch, pk);
   }
   tc::tmem_wait_st();
-  const float2 sum = f2_unpack(f2_add(sum2[0], sum2[1]));
-  l_run += sum.x + sum.y;
+  l_run += (acc[0] + acc[2]) + (acc[1] + acc[3]);
   return true;
 }
 
@@ -763,11 +762,18 @@ inline uint32_t umin_host(uint32_t a, uint32_t b) { return a < b ? a : b; }
 // work items (a prompt's adjacent Q tiles n-1-2r and n-2-2r, one per stream,
 // sharing every K/V tile; an odd prompt's tile 0 alone on stream 0) in a
 // static round-robin over an order that lists every prompt's heaviest items
-// first.  Barrier phases run on across items: the producer loads item n+1's
-// Q tiles as soon as the last QK of item n has been issued for each stream
-// (q_free), each softmax warpgroup rotates its row of the next item's Q tile
-// right after its last P of item n and only then writes item n's output, so
-// the next item's first S is computed while the current epilogue runs.
+// first.  Four warpgroups: the softmax of stream 0 and of stream 1; control
+// (TMA producer warp, MMA warp); and a boundary warpgroup that takes the
+// per-item work off the softmax warpgroups' chain: it applies M-RoPE to the
+// next item's Q tiles as soon as they land, and writes each item's output
+// (O from TMEM, divided by the row sums the softmax warpgroups leave in
+// shared memory) while the softmax warpgroups already work on the next item.
+// Barrier phases run on across items: the producer loads item n+1's Q tiles
+// once the last QK of item n has completed for each stream (q_free); the
+// first PV of item n+1 waits until the boundary warpgroup has read item n's
+// O (o_free).  (With the rotation and the epilogue in the softmax
+// warpgroups, removing either of them from the kernel had cut the batched
+// launch by ~17 %.)
 //
 // Items: index x of [0, prompts * ranks_max * 2): prompt b = x / (2 ranks_max),
 // rank r = (x / 2) mod ranks_max (the prompt's heaviest first), KV head
@@ -775,14 +781,19 @@ inline uint32_t umin_host(uint32_t a, uint32_t b) { return a < b ? a : b; }
 // Prompt-major, so the CTAs working at one time share a few prompts' keys and
 // values in L2: a rank-major order (every prompt's heaviest items first)
 // spread them over the whole launch and measured 13 % slower (3.14 against
-// 2.77 ms for 256 x 1238 tokens).  Against one CTA per item (the same tiles,
-// prefill_attn_kernel) the persistent form gains ~1 % (2.77 against 2.80 ms);
-// rotating the next Q after the epilogue instead of before it loses ~3 %.
+// 2.77 ms for 256 x 1238 tokens).
 constexpr uint32_t OFF_BARS_P = OFF_STAGE_PAIR + PAIR_STAGES * STAGE_BYTES;
-// q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2], q_free[2]
-constexpr int NBARS_P = 14;
-constexpr uint32_t OFF_MISC_P = OFF_BARS_P + NBARS_P * 8;
+// q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2], q_free[2],
+// o_last, o_free, l_ready[2][2]
+constexpr int NBARS_P = 20;
+constexpr uint32_t OFF_L_P = OFF_BARS_P + NBARS_P * 8;       // row sums [2][2][128] f32
+constexpr uint32_t OFF_MISC_P = OFF_L_P + 2 * STREAMS * 128 * 4;
 constexpr uint32_t SMEM_BYTES_P = OFF_MISC_P + 64 + 1024;
+// launch 512 x 128 registers: softmax 152, control 88, boundary 120
+constexpr int THREADS_P = 16 * 32;
+constexpr uint32_t REGS_SOFTMAX_P = 152, REGS_CTRL_P = 88, REGS_BOUND_P = 120;
+static_assert(256 * REGS_SOFTMAX_P + 128 * (REGS_CTRL_P + REGS_BOUND_P) <= THREADS_P * 128,
+              "persistent register split");
 static_assert(SMEM_BYTES_P <= 227 * 1024, "persistent prefill shared memory exceeds the limit");
 
 struct Item {
@@ -819,7 +830,7 @@ __device__ __forceinline__ Item item_at(uint32_t x, const Prompts<MAXB>& pr) {
 }
 
 template <int MAXB>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS_P, 1)
     prefill_persist_kernel(const __grid_constant__ Maps maps, const Params p,
                            const __grid_constant__ Prompts<MAXB> pr, uint32_t n_items) {
   extern __shared__ uint8_t smem_raw[];
@@ -834,6 +845,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* p_ready = bars + 8;    // [2]
   uint64_t* o_done = bars + 10;    // [2]
   uint64_t* q_free = bars + 12;    // [2] the item's last QK of the stream is complete
+  uint64_t* o_last = bars + 14;    // every PV of the item is complete
+  uint64_t* o_free = bars + 15;    // the boundary warpgroup has read the item's O
+  // [stream][parity of the stream's active-item count]: that item's row sums are in l_sm
+  uint64_t* l_ready = bars + 16;
+  float* l_sm = reinterpret_cast<float*>(smem + OFF_L_P);   // [stream][parity][row]
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC_P);
   // misc[0]: TMEM base, misc[1]: abort
 
@@ -847,7 +863,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (tid == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, 4);
     for (int s = 0; s < PAIR_STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -857,7 +873,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&p_ready[t], 4);
       mbar_init(&o_done[t], 1);
       mbar_init(&q_free[t], 1);
+      mbar_init(&l_ready[2 * t], 4);
+      mbar_init(&l_ready[2 * t + 1], 4);
     }
+    mbar_init(o_last, 1);
+    mbar_init(o_free, 4);
     misc[1] = 0;
     fence_mbar_init();
   }
@@ -872,7 +892,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int wg = warp >> 2;
   if (wg == 2) {
-    tc::regs_dec<REGS_CTRL>();
+    tc::regs_dec<REGS_CTRL_P>();
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------- TMA producer
       tc::tma_prefetch_desc(&maps.q);
@@ -922,7 +942,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---------------------------------------------------- MMA issuer
       // per item: both streams' first QK, then per K tile j and stream the PV of
       // tile j and the QK of tile j + 1; q_free[t] is committed right after the
-      // stream's last QK of the item (its Q buffer may then be refilled)
+      // stream's last QK of the item (its Q buffer may then be refilled), o_last
+      // after the item's last PV; the item's first PV waits until the boundary
+      // warpgroup has read the previous item's O (o_free)
       constexpr uint32_t idesc_qk = tc::idesc_f16(128, 128, 0, 0);
       constexpr uint32_t idesc_pv = tc::idesc_f16(128, 128, 0, 1);
       const uint32_t sq = smem_u32(smem + OFF_Q), st0 = smem_u32(smem + OFF_STAGE_PAIR);
@@ -955,8 +977,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         __syncwarp();
       };
-      auto commit_free = [&](int t) {
-        if (tc::elect_one()) tc::commit(&q_free[t]);
+      auto commit_to = [&](uint64_t* bar) {
+        if (tc::elect_one()) tc::commit(bar);
         __syncwarp();
       };
       constexpr uint32_t kAll = 0xffffffffu;
@@ -973,12 +995,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_after_sync();
         const int s0 = G % PAIR_STAGES;
         qk(0, s0);
-        if (nk == 1) commit_free(0);
+        if (nk == 1) commit_to(&q_free[0]);
         if (it.nks[1] > 0) {
           qk(1, s0);
-          if (it.nks[1] == 1) commit_free(1);
+          if (it.nks[1] == 1) commit_to(&q_free[1]);
         } else {
-          commit_free(1);   // stream 1 idle in this item
+          commit_to(&q_free[1]);   // stream 1 idle in this item
         }
         for (int j = 0; j < nk && ok; ++j) {
           const int s = (G + j) % PAIR_STAGES, s1 = (G + j + 1) % PAIR_STAGES;
@@ -993,6 +1015,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int t = 0; t < STREAMS; ++t) {
             if (j >= it.nks[t]) continue;
             if (!__all_sync(kAll, mbar_wait(&p_ready[t], steps[t] & 1))) { ok = false; break; }
+            if (j == 0 && t == 0 && n > 0 &&
+                !__all_sync(kAll, mbar_wait(o_free, (n - 1) & 1))) {
+              ok = false;
+              break;
+            }
             ++steps[t];
             tc::fence_after_sync();
             // stream 1's tiles are a prefix of stream 0's: the last reader of
@@ -1000,11 +1027,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             pv(t, s, j == 0, t == 1 || j >= it.nks[1]);
             if (j + 1 < it.nks[t]) {
               qk(t, s1);
-              if (j + 2 == it.nks[t]) commit_free(t);
+              if (j + 2 == it.nks[t]) commit_to(&q_free[t]);
             }
           }
         }
-        if (ok) G += nk;
+        if (ok) {
+          commit_to(o_last);
+          G += nk;
+        }
       }
       if (!ok && lane == 0) misc[1] = 1;
       // never exit with MMAs in flight or commit arrivals still pending
@@ -1014,10 +1044,121 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (n > 0) {
         mbar_wait(&q_free[0], (n - 1) & 1);
         mbar_wait(&q_free[1], (n - 1) & 1);
+        if (ok) mbar_wait(o_last, (n - 1) & 1);
       }
     }
+  } else if (wg == 3) {
+    tc::regs_dec<REGS_BOUND_P>();
+    // ------------------------------------------------------ boundary
+    const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    // M-RoPE by (token, chunk): thread i takes token slot i / 8 and chunk
+    // i % 8 (dims 8c..8c+7 and their partners 64 above) of both streams'
+    // tiles, so one set of table entries serves the 8 heads' rows of the
+    // token; the entries are loaded before waiting for the tiles to land.
+    auto rotate = [&](const Item& it, uint32_t ph) -> bool {
+      const int u = i >> 3, c = i & 7;
+      const uint32_t axis = mrope_axis(8 * c);   // section edges are multiples of 8
+      const uint32_t rr = pr.rope_rows[it.pi];
+      float4 tv[STREAMS][8];
+      bool mine[STREAMS];
+#pragma unroll
+      for (int t = 0; t < STREAMS; ++t) {
+        const uint32_t token = it.tile0[t] + u;
+        mine[t] = it.nks[t] > 0 && token < it.tokens;
+        if (mine[t]) {
+          const size_t tb = ((size_t)axis * rr + token) * HD + 8 * c;
+          const float4* cs = reinterpret_cast<const float4*>(pr.rope_cos[it.pi] + tb);
+          const float4* sn = reinterpret_cast<const float4*>(pr.rope_sin[it.pi] + tb);
+          tv[t][0] = __ldg(cs);
+          tv[t][1] = __ldg(cs + 1);
+          tv[t][2] = __ldg(cs + 16);
+          tv[t][3] = __ldg(cs + 17);
+          tv[t][4] = __ldg(sn);
+          tv[t][5] = __ldg(sn + 1);
+          tv[t][6] = __ldg(sn + 16);
+          tv[t][7] = __ldg(sn + 17);
+        }
+      }
+      const bool landed = mbar_wait(q_full, ph);
+      if (landed) {
+#pragma unroll
+        for (int t = 0; t < STREAMS; ++t) {
+          if (!mine[t]) continue;
+          uint8_t* qb = smem + OFF_Q + t * Q_BYTES;
+#pragma unroll
+          for (int h = 0; h < GROUP; ++h) rope_chunk(qb, qb + SZ_W, u * GROUP + h, c, tv[t]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+      return landed;
+    };
+    uint32_t n = 0;
+    uint32_t na[STREAMS] = {0, 0};   // active items per stream so far (l_ready slots)
+    uint32_t x = next_item(first_x);
+    bool good = x >= n_items || __all_sync(0xffffffffu, rotate(item_at<MAXB>(x, pr), 0));
+    for (; x < n_items && good; ++n) {
+      const Item it = item_at<MAXB>(x, pr);
+      const uint32_t xn = next_item(x + step_x);
+      // the next item's Q first: its first QKs then run during this epilogue
+      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
+        good = false;
+        break;
+      }
+      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(o_last, n & 1))) {
+        good = false;
+        break;
+      }
+      tc::fence_after_sync();
+      // O of each active stream, 32 columns at a time; the accumulators are
+      // released (o_free) once the last chunk is in registers.  Row sums are
+      // counted per active item of a stream: the warpgroup of a stream that
+      // is idle in an item passes it without waiting for anything, so it may
+      // run one active item ahead.
+      const int last_t = it.nks[1] > 0 ? 1 : 0;
+#pragma unroll 1
+      for (int t = 0; t <= last_t && good; ++t) {
+        const uint32_t slot = 2 * t + (na[t] & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&l_ready[slot], (na[t] >> 1) & 1))) {
+          good = false;
+          break;
+        }
+        ++na[t];
+        const uint32_t token = it.tile0[t] + (i >> 3);
+        const bool store = token < it.tokens;
+        const float inv = 1.f / l_sm[slot * 128 + i];
+        __half* orow = p.out + ((size_t)(it.row0 + token) * QH + GROUP * it.g + (i & 7)) * HD;
+        const uint32_t tO = tmem + lane_base + 256u + 128u * t;
+#pragma unroll 1
+        for (int cc = 0; cc < 128; cc += 32) {
+          uint32_t ov[32];
+          tc::tmem_ld32(tO + cc, ov);
+          tc::tmem_wait_ld();
+          if (t == last_t && cc == 96) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free);
+          }
+          if (!store) continue;
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(ov[c + 0]) * inv, __uint_as_float(ov[c + 1]) * inv);
+            w.y = pack_half2(__uint_as_float(ov[c + 2]) * inv, __uint_as_float(ov[c + 3]) * inv);
+            w.z = pack_half2(__uint_as_float(ov[c + 4]) * inv, __uint_as_float(ov[c + 5]) * inv);
+            w.w = pack_half2(__uint_as_float(ov[c + 6]) * inv, __uint_as_float(ov[c + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + cc + c) = w;
+          }
+        }
+      }
+      if (!good) break;
+      x = xn;
+    }
+    if (!good) misc[1] = 1;
   } else {
-    tc::regs_inc<REGS_SOFTMAX>();
+    tc::regs_inc<REGS_SOFTMAX_P>();
     // ------------------------------------------------------ softmax
     const int t = wg;                                // stream of this warpgroup
     const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
@@ -1026,39 +1167,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tO = tmem + lane_base + 256u + 128u * t;
     const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(HD));
     const uint64_t scale2 = f2_pack(scale, scale);
-    uint8_t* qb0 = smem + OFF_Q + t * Q_BYTES;
-    // M-RoPE of this thread's row of stream t's Q tile of item `it` (q_full
-    // phase `ph`), then the q_ready arrival (also for an idle stream)
-    auto rotate = [&](const Item& it, uint32_t ph) -> bool {
-      const uint32_t token = it.tile0[t] + (i >> 3);
-      const bool mine = it.nks[t] > 0 && token < it.tokens;
-      const float* rc = pr.rope_cos[it.pi];
-      const float* rs = pr.rope_sin[it.pi];
-      const uint32_t rr = pr.rope_rows[it.pi];
-      // two chunks (16 dims and their partners) of tables at a time: live state
-      // is high here (the current item's epilogue follows)
-      RowTables<2> rt;
-      if (mine) mrope_tables(rt, rc, rs, rr, token, 0);
-      const bool landed = mbar_wait(q_full, ph);
-      if (landed && mine) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < 8; c0 += 2) {
-          if (c0 > 0) mrope_tables(rt, rc, rs, rr, token, c0);
-          mrope_row(qb0, qb0 + SZ_W, i, rt, c0);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_ready);
-      return landed;
-    };
     uint32_t step_g = 0;     // this stream's steps so far (s_full / p_ready / o_done phases)
-    uint32_t n = 0;
-    uint32_t x = next_item(first_x);
-    bool good = x >= n_items || __all_sync(0xffffffffu, rotate(item_at<MAXB>(x, pr), 0));
-    for (; x < n_items && good; ++n) {
+    uint32_t na = 0;         // this stream's active items so far (l_ready slots)
+    bool good = true;
+    for (uint32_t x = next_item(first_x); x < n_items && good; x = next_item(x + step_x)) {
       const Item it = item_at<MAXB>(x, pr);
       const int my_nk = it.nks[t];
+      if (my_nk == 0) continue;
       const uint32_t token = it.tile0[t] + (i >> 3);
       const uint32_t warp_tok_lo = it.tile0[t] + ((warp & 3) * 32 >> 3);
       float m_run = -CUDART_INF_F, l_run = 0.f;
@@ -1077,48 +1192,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) mbar_arrive(&p_ready[t]);
       }
       if (!good) break;
-      // the next item's Q row first (its QK then runs during this epilogue)
-      const uint32_t xn = next_item(x + step_x);
-#if PVLC_PREFILL_EARLY_ROT
-      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
-        good = false;
-        break;
-      }
-#endif
-      if (my_nk > 0) {
-        // epilogue: this stream's O / l -> all 128 columns of the row
-        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[t], (step_g - 1) & 1))) {
-          good = false;
-          break;
-        }
-        tc::fence_after_sync();
-        const bool store = token < it.tokens;
-        __half* orow = p.out + ((size_t)(it.row0 + token) * QH + GROUP * it.g + (i & 7)) * HD;
-        const float inv = 1.f / l_run;
-#pragma unroll
-        for (int cc = 0; cc < 128; cc += 16) {
-          uint32_t ov[16];
-          tc::tmem_ld16(tO + cc, ov);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(ov[8 * h + 0]) * inv, __uint_as_float(ov[8 * h + 1]) * inv);
-            w.y = pack_half2(__uint_as_float(ov[8 * h + 2]) * inv, __uint_as_float(ov[8 * h + 3]) * inv);
-            w.z = pack_half2(__uint_as_float(ov[8 * h + 4]) * inv, __uint_as_float(ov[8 * h + 5]) * inv);
-            w.w = pack_half2(__uint_as_float(ov[8 * h + 6]) * inv, __uint_as_float(ov[8 * h + 7]) * inv);
-            if (store) *reinterpret_cast<uint4*>(orow + cc + 8 * h) = w;
-          }
-        }
-        tc::fence_before_sync();   // the next item's PV may overwrite O after our arrival
-      }
-#if !PVLC_PREFILL_EARLY_ROT
-      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
-        good = false;
-        break;
-      }
-#endif
-      x = xn;
+      // the row sums for the boundary warpgroup's epilogue
+      const uint32_t slot = 2 * t + (na & 1);
+      l_sm[slot * 128 + i] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_ready[slot]);
+      ++na;
     }
     if (!good) misc[1] = 1;
   }
@@ -1226,6 +1305,7 @@ int launch(const void* q, const void* k, const void* v, uint32_t rows, const Pro
     if (sms <= 0) return PVLC_CUDA_ERROR;
     const uint32_t ctas = umin_host(static_cast<uint32_t>(sms), 2 * grid_y);
     cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(THREADS_P);
     cfg.dynamicSmemBytes = SMEM_BYTES_P;
     if (cudaLaunchKernelEx(&cfg, prefill_persist_kernel<MAXB>, maps, p, pr, persist_items) !=
         cudaSuccess)

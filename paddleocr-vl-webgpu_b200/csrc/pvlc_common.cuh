@@ -221,6 +221,18 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+// acc_lo += low half of h2, acc_hi += high half: each fp16 half widened
+// exactly and added in f32 with one rounding (the sm_100 mixed-precision add,
+// one instruction per value), so the sums equal widen-then-add bit for bit.
+__device__ __forceinline__ void add_f16x2_to_f32(uint32_t h2, float& acc_lo, float& acc_hi) {
+  asm("{\n\t.reg .b16 lo, hi;\n\t"
+      "mov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.f16 %0, lo, %0;\n\t"
+      "add.rn.f32.f16 %1, hi, %1;\n\t}"
+      : "+f"(acc_lo), "+f"(acc_hi)
+      : "r"(h2));
+}
+
 // Packed half-precision 2^x (one MUFU operation for two values).
 __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
   uint32_t y;

@@ -210,7 +210,9 @@ def test_batched_prefill_long_and_short_prompts_vs_oracle(cuda_lib):
 
 def test_batched_prefill_many_prompts_in_groups(cuda_lib):
     """300 short prompts (two launches of at most 256 prompts, odd and even Q-tile counts)
-    match the per-prompt calls: outputs within the fp16 tolerance, caches bit for bit."""
+    match the per-prompt calls, every prompt: outputs within the fp16 tolerance, caches bit
+    for bit (the persistent kernel's work items cross prompt boundaries on every CTA, and an
+    odd prompt's last item leaves one stream idle)."""
     from pvlc_b200 import ops
     rng = np.random.default_rng(4)
     Ts = [int(x) for x in rng.integers(1, 300, size=300)]
@@ -218,7 +220,7 @@ def test_batched_prefill_many_prompts_in_groups(cuda_lib):
     offs, host, host_tables, t, tables, kc, vc = _packed_case(Ts, cap, seed=5)
     out = torch.empty_like(t["q"])
     ops.decoder_prefill_packed(t["q"], t["k"], t["v"], offs, tables, kc, vc, out)
-    for b in (0, 1, 255, 256, 299):
+    for b in range(len(Ts)):
         s, e = int(offs[b]), int(offs[b + 1])
         kc1 = torch.full((cap, KVH, HD), float("nan"), dtype=torch.float16, device="cuda")
         vc1 = torch.full_like(kc1, float("nan"))
