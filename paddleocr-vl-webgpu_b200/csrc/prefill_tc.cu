@@ -109,8 +109,9 @@ constexpr uint32_t EXP_POLY_MASK = PVLC_PREFILL_EXP_POLY_MASK;
 
 struct Maps {
   // q, v: the packed input rows; k: the KV caches (rotated keys) as
-  // {128, 2, capacity, prompts}
-  CUtensorMap q, k, v;
+  // {128, 2, capacity, prompts}; o: the packed output rows (batched kernel's
+  // epilogue, Q-tile boxes)
+  CUtensorMap q, k, v, o;
 };
 
 struct Params {
@@ -782,18 +783,25 @@ inline uint32_t umin_host(uint32_t a, uint32_t b) { return a < b ? a : b; }
 // values in L2: a rank-major order (every prompt's heaviest items first)
 // spread them over the whole launch and measured 13 % slower (3.14 against
 // 2.77 ms for 256 x 1238 tokens).
-constexpr uint32_t OFF_BARS_P = OFF_STAGE_PAIR + PAIR_STAGES * STAGE_BYTES;
+// output staging: one 64-dim half of a Q-tile-shaped output box (128 rows x
+// 128 B, 128B-swizzled), written by the boundary warpgroup, stored by TMA
+constexpr uint32_t OFF_STG_P = OFF_STAGE_PAIR + PAIR_STAGES * STAGE_BYTES;
+constexpr uint32_t OFF_BARS_P = OFF_STG_P + SZ_W;
 // q_full, q_ready, kv_full[2], kv_empty[2], s_full[2], p_ready[2], o_done[2], q_free[2],
 // o_last, o_free, l_ready[2][2]
 constexpr int NBARS_P = 20;
 constexpr uint32_t OFF_L_P = OFF_BARS_P + NBARS_P * 8;       // row sums [2][2][128] f32
 constexpr uint32_t OFF_MISC_P = OFF_L_P + 2 * STREAMS * 128 * 4;
 constexpr uint32_t SMEM_BYTES_P = OFF_MISC_P + 64 + 1024;
-// launch 512 x 128 registers: softmax 152, control 88, boundary 120
+// launch 512 x 128 registers, then per warpgroup: softmax 144, control 88,
+// boundary 136 (set by setmaxnreg .inc / .dec from the launch count; the
+// launch checks that the compiled kernel uses exactly LAUNCH_REGS_P)
 constexpr int THREADS_P = 16 * 32;
-constexpr uint32_t REGS_SOFTMAX_P = 152, REGS_CTRL_P = 88, REGS_BOUND_P = 120;
-static_assert(256 * REGS_SOFTMAX_P + 128 * (REGS_CTRL_P + REGS_BOUND_P) <= THREADS_P * 128,
+constexpr uint32_t LAUNCH_REGS_P = 128;   // 65536 / THREADS_P
+constexpr uint32_t REGS_SOFTMAX_P = 144, REGS_CTRL_P = 88, REGS_BOUND_P = 136;
+static_assert(256 * REGS_SOFTMAX_P + 128 * (REGS_CTRL_P + REGS_BOUND_P) <= THREADS_P * LAUNCH_REGS_P,
               "persistent register split");
+static_assert(LAUNCH_REGS_P * THREADS_P <= 65536, "persistent launch registers");
 static_assert(SMEM_BYTES_P <= 227 * 1024, "persistent prefill shared memory exceeds the limit");
 
 struct Item {
@@ -892,7 +900,7 @@ __global__ void __launch_bounds__(THREADS_P, 1)
 
   const int wg = warp >> 2;
   if (wg == 2) {
-    tc::regs_dec<REGS_CTRL_P>();
+    tc::regs_to<LAUNCH_REGS_P, REGS_CTRL_P>();
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------- TMA producer
       tc::tma_prefetch_desc(&maps.q);
@@ -1048,7 +1056,7 @@ __global__ void __launch_bounds__(THREADS_P, 1)
       }
     }
   } else if (wg == 3) {
-    tc::regs_dec<REGS_BOUND_P>();
+    tc::regs_to<LAUNCH_REGS_P, REGS_BOUND_P>();
     // ------------------------------------------------------ boundary
     const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
@@ -1095,6 +1103,7 @@ __global__ void __launch_bounds__(THREADS_P, 1)
       if (lane == 0) mbar_arrive(q_ready);
       return landed;
     };
+    if (i == 0) tc::tma_prefetch_desc(&maps.o);
     uint32_t n = 0;
     uint32_t na[STREAMS] = {0, 0};   // active items per stream so far (l_ready slots)
     uint32_t x = next_item(first_x);
@@ -1112,12 +1121,16 @@ __global__ void __launch_bounds__(THREADS_P, 1)
         break;
       }
       tc::fence_after_sync();
-      // O of each active stream, 32 columns at a time; the accumulators are
-      // released (o_free) once the last chunk is in registers.  Row sums are
-      // counted per active item of a stream: the warpgroup of a stream that
-      // is idle in an item passes it without waiting for anything, so it may
-      // run one active item ahead.
+      // O of each active stream in two 64-column halves; the accumulators are
+      // released (o_free) once the last half is in registers.  A full Q tile
+      // goes out through the staging buffer and one TMA store per half
+      // (coalesced: each token's 8 heads are 2 KB of contiguous output); the
+      // last tile of a prompt, whose box would reach into the next prompt's
+      // rows, is stored row by row.  Row sums are counted per active item of
+      // a stream: the warpgroup of a stream that is idle in an item passes it
+      // without waiting for anything, so it may run one active item ahead.
       const int last_t = it.nks[1] > 0 ? 1 : 0;
+      uint8_t* stg = smem + OFF_STG_P;
 #pragma unroll 1
       for (int t = 0; t <= last_t && good; ++t) {
         const uint32_t slot = 2 * t + (na[t] & 1);
@@ -1127,38 +1140,58 @@ __global__ void __launch_bounds__(THREADS_P, 1)
         }
         ++na[t];
         const uint32_t token = it.tile0[t] + (i >> 3);
+        const bool full = it.tile0[t] + TOK <= it.tokens;
         const bool store = token < it.tokens;
         const float inv = 1.f / l_sm[slot * 128 + i];
         __half* orow = p.out + ((size_t)(it.row0 + token) * QH + GROUP * it.g + (i & 7)) * HD;
         const uint32_t tO = tmem + lane_base + 256u + 128u * t;
 #pragma unroll 1
-        for (int cc = 0; cc < 128; cc += 32) {
-          uint32_t ov[32];
-          tc::tmem_ld32(tO + cc, ov);
-          tc::tmem_wait_ld();
-          if (t == last_t && cc == 96) {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t ov[32];
+            tc::tmem_ld32(tO + 64 * half + 32 * q, ov);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              pk[16 * q + e] =
+                  pack_half2(__uint_as_float(ov[2 * e]) * inv, __uint_as_float(ov[2 * e + 1]) * inv);
+          }
+          if (t == last_t && half == 1) {
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_free);
           }
-          if (!store) continue;
+          if (full) {
+            // the previous store has read the staging buffer
+            if (i == 0) tc::bulk_wait_read_all();
+            named_bar_sync(1, 128);
 #pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(ov[c + 0]) * inv, __uint_as_float(ov[c + 1]) * inv);
-            w.y = pack_half2(__uint_as_float(ov[c + 2]) * inv, __uint_as_float(ov[c + 3]) * inv);
-            w.z = pack_half2(__uint_as_float(ov[c + 4]) * inv, __uint_as_float(ov[c + 5]) * inv);
-            w.w = pack_half2(__uint_as_float(ov[c + 6]) * inv, __uint_as_float(ov[c + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + cc + c) = w;
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(chunk_addr(stg, i, c)) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            fence_proxy_async_smem();
+            named_bar_sync(1, 128);
+            if (i == 0) {
+              tc::tma_store_3d(&maps.o, stg, 64 * half, GROUP * it.g, it.row0 + it.tile0[t]);
+              tc::bulk_commit_group();
+            }
+          } else if (store) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(orow + 64 * half + 8 * c) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
           }
         }
       }
       if (!good) break;
       x = xn;
     }
+    if (i == 0) tc::bulk_wait_all();   // no store may still read the staging buffer at exit
     if (!good) misc[1] = 1;
   } else {
-    tc::regs_inc<REGS_SOFTMAX_P>();
+    tc::regs_to<LAUNCH_REGS_P, REGS_SOFTMAX_P>();
     // ------------------------------------------------------ softmax
     const int t = wg;                                // stream of this warpgroup
     const int i = (warp & 3) * 32 + lane;            // row == TMEM lane
@@ -1271,6 +1304,13 @@ int launch(const void* q, const void* k, const void* v, uint32_t rows, const Pro
     if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_persist_kernel<MAXB>),
                                 SMEM_BYTES_P) != PVLC_OK)
       return PVLC_CUDA_ERROR;
+    // the warpgroups' setmaxnreg counts assume this launch register count
+    static const int launch_regs = [] {
+      cudaFuncAttributes fa;
+      return cudaFuncGetAttributes(&fa, prefill_persist_kernel<MAXB>) == cudaSuccess ? fa.numRegs
+                                                                                    : -1;
+    }();
+    if (launch_regs != static_cast<int>(LAUNCH_REGS_P)) return PVLC_CUDA_ERROR;
   } else if (set_smem_attribute_once(reinterpret_cast<const void*>(prefill_attn_kernel<MAXB>),
                                      SMEM_BYTES) != PVLC_OK) {
     return PVLC_CUDA_ERROR;
@@ -1281,6 +1321,7 @@ int launch(const void* q, const void* k, const void* v, uint32_t rows, const Pro
   // prompt are masked, rows past the capacity are TMA zero fill; values come
   // from the packed input rows
   if (!make_map(&maps.q, q, rows, QH, GROUP, TOK) ||
+      (persist_items && !make_map(&maps.o, p.out, rows, QH, GROUP, TOK)) ||
       !make_cache_map(&maps.k, p.k_cache, capacity, pr.count, p.cache_stride) ||
       !make_map(&maps.v, v, rows, KVH, 1, BN))
     return PVLC_CUDA_ERROR;
