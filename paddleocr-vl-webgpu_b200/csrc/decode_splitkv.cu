@@ -66,8 +66,7 @@ constexpr int ROW_PITCH = ROW_BYTES + 16; // 528: conflict-free ldmatrix rows
 constexpr int STAGE_BYTES = TILE * ROW_PITCH;
 constexpr int CONSUMER_WARPS = 8;
 constexpr int PRODUCER_WARPS = 2;             // copy warp, sequence warp
-constexpr int MERGE_WARP = CONSUMER_WARPS + PRODUCER_WARPS;
-constexpr int THREADS = (CONSUMER_WARPS + PRODUCER_WARPS + 1) * 32;
+constexpr int THREADS = (CONSUMER_WARPS + PRODUCER_WARPS + 1) * 32;   // + the merge warp
 constexpr int CONSUMER_THREADS = CONSUMER_WARPS * 32;
 constexpr int MAX_BATCH = 2048;
 constexpr int PART_FLOATS = QH * HD + 2 * QH;   // O[16][128], m[16], l[16]

@@ -1107,16 +1107,22 @@ __global__ void __launch_bounds__(THREADS_P, 1)
     uint32_t n = 0;
     uint32_t na[STREAMS] = {0, 0};   // active items per stream so far (l_ready slots)
     uint32_t x = next_item(first_x);
-    bool good = x >= n_items || __all_sync(0xffffffffu, rotate(item_at<MAXB>(x, pr), 0));
+    // The four warps meet on named barrier 1 around every staging-buffer
+    // use, and a bar.sync has no time limit: so every outcome that can end
+    // the loop (a bounded wait, the abort flag) is agreed on by all four
+    // warps through named barrier 2 (bar.red.and) first, and they leave
+    // together.
+    auto agree = [&](bool ok) { return named_bar_and(2, 128, ok); };
+    bool good = x >= n_items || agree(rotate(item_at<MAXB>(x, pr), 0));
     for (; x < n_items && good; ++n) {
       const Item it = item_at<MAXB>(x, pr);
       const uint32_t xn = next_item(x + step_x);
       // the next item's Q first: its first QKs then run during this epilogue
-      if (xn < n_items && !__all_sync(0xffffffffu, rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
+      if (xn < n_items && !agree(rotate(item_at<MAXB>(xn, pr), (n + 1) & 1))) {
         good = false;
         break;
       }
-      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(o_last, n & 1))) {
+      if (!agree(misc[1] == 0 && mbar_wait(o_last, n & 1))) {
         good = false;
         break;
       }
@@ -1134,7 +1140,7 @@ __global__ void __launch_bounds__(THREADS_P, 1)
 #pragma unroll 1
       for (int t = 0; t <= last_t && good; ++t) {
         const uint32_t slot = 2 * t + (na[t] & 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&l_ready[slot], (na[t] >> 1) & 1))) {
+        if (!agree(mbar_wait(&l_ready[slot], (na[t] >> 1) & 1))) {
           good = false;
           break;
         }

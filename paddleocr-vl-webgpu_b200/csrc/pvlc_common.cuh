@@ -297,6 +297,22 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over its `threads` threads: every
+// thread gets the same answer, so warps that go on to meet on other named
+// barriers all take the same branch after it.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t threads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
+
 // Select the M-RoPE axis plane for head dimension d of a 128-wide head:
 // sections [16, 24, 24] repeated on both halves
 // (crates/pvlc-cpu-ref/src/lib.rs:613-643, crates/pvlc-wgsl/src/lib.rs:1218-1220).
