@@ -239,6 +239,19 @@ int pvlc_attn_decode_strided(const pvlc_half* q, uint32_t q_row_stride, const pv
  * PVLC_OK when no flag was set, PVLC_DEVICE_FAULT_FLAG otherwise. */
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
 
+/* Sticky fault word of the vision and prefill kernels on the calling thread's
+ * current device.  It has no counterpart in the reference (its WebGPU
+ * dispatches cannot time out inside a shader).  A launch whose bounded
+ * pipeline wait ran out stops early -- its output is then incomplete -- and
+ * sets its kernel's bit; the bits of every such launch on the device since
+ * the last read accumulate (calls on several streams share the word).
+ * pvlc_attn_fault_flags synchronizes `stream`, then reads and clears the word;
+ * it returns PVLC_OK when no bit was set, PVLC_DEVICE_FAULT_FLAG otherwise. */
+#define PVLC_FAULT_VISION 1u
+#define PVLC_FAULT_PREFILL 2u
+#define PVLC_FAULT_PREFILL_BATCH 4u
+int pvlc_attn_fault_flags(uint32_t* flags_out, void* stream);
+
 /* Allocation-free variant of pvlc_attn_decode.  It has no counterpart in the
  * reference.  It serves callers that can pass input and output buffers but
  * cannot allocate device memory -- a host whose device memory is planned once

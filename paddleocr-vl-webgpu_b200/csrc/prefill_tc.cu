@@ -63,6 +63,11 @@
 namespace pvlc {
 namespace ptc {
 
+// Sticky fault word of this device's prefill launches: a CTA whose bounded
+// wait ran out (misc[1]) ORs in its kernel's bit when it ends.  Read and
+// cleared by pvlc_attn_fault_flags.
+__device__ uint32_t g_faults;
+
 constexpr int HD = 128;
 constexpr int QH = 16;
 constexpr int KVH = 2;
@@ -750,6 +755,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc::fence_before_sync();
   __syncthreads();
+  if (tid == 0 && misc[1]) atomicOr(&g_faults, PVLC_FAULT_PREFILL);
   if (warp == 8) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -1243,6 +1249,7 @@ __global__ void __launch_bounds__(THREADS_P, 1)
 
   tc::fence_before_sync();
   __syncthreads();
+  if (tid == 0 && misc[1]) atomicOr(&g_faults, PVLC_FAULT_PREFILL_BATCH);
   if (warp == 8) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -1364,6 +1371,19 @@ int launch(const void* q, const void* k, const void* v, uint32_t rows, const Pro
 }
 
 }  // namespace ptc
+
+int prefill_fault_word(uint32_t* out, cudaStream_t s) {
+  uint32_t v = 0;
+  const uint32_t zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, ptc::g_faults, 4, 0, cudaMemcpyDeviceToHost, s) !=
+          cudaSuccess ||
+      cudaMemcpyToSymbolAsync(ptc::g_faults, &zero, 4, 0, cudaMemcpyHostToDevice, s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return PVLC_CUDA_ERROR;
+  *out = v;
+  return PVLC_OK;
+}
 
 int prefill_query_tile() { return ptc::QT * ptc::TOK; }
 

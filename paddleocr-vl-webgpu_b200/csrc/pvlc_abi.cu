@@ -479,6 +479,18 @@ int pvlc_attn_decode(const pvlc_half* q, const pvlc_half* k_new, const pvlc_half
                                   stream);
 }
 
+int pvlc_attn_fault_flags(uint32_t* flags_out, void* stream) {
+  if (!flags_out) return PVLC_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t a = 0, b = 0;
+  int st = vision_fault_word(&a, s);
+  if (st != PVLC_OK) return st;
+  st = prefill_fault_word(&b, s);
+  if (st != PVLC_OK) return st;
+  *flags_out = a | b;
+  return (a | b) ? PVLC_DEVICE_FAULT_FLAG : PVLC_OK;
+}
+
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream) {
   if (!workspace || !flags_out) return PVLC_NULL_POINTER;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

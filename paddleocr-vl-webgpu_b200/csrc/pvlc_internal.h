@@ -45,6 +45,10 @@ struct VisionArgs {
   pvlc_half* out;
   uint32_t qkv_stride;   // elements between consecutive tokens' q / k / v rows (heads x 72 packed)
 };
+// Read and clear the calling device's sticky fault word of the vision /
+// prefill kernels (PVLC_FAULT_* bits); synchronizes `s`.
+int vision_fault_word(uint32_t* out, cudaStream_t s);
+int prefill_fault_word(uint32_t* out, cudaStream_t s);
 int vision_query_tile();
 int vision_block_threads();
 // Scratch for the rotated q and k (2 x tokens x heads x 72 fp16).

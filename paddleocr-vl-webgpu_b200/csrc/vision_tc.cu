@@ -58,6 +58,9 @@
 namespace pvlc {
 namespace vtc {
 
+// Sticky fault word of this device's vision launches (see prefill_tc.cu).
+__device__ uint32_t g_faults;
+
 constexpr int HD = 72;
 constexpr int PAIRS = 36;
 constexpr int QUADS = PAIRS / 4;  // rotation pairs in groups of four (16 bytes of table)
@@ -502,6 +505,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   tc::fence_before_sync();
   __syncthreads();
+  if (tid == 0 && misc[1]) atomicOr(&g_faults, PVLC_FAULT_VISION);
   if (warp == CTRL_WARP) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -544,6 +548,19 @@ bool make_map(CUtensorMap* m, const void* base, uint32_t tokens, uint32_t heads,
 }
 
 }  // namespace vtc
+
+int vision_fault_word(uint32_t* out, cudaStream_t s) {
+  uint32_t v = 0;
+  const uint32_t zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, vtc::g_faults, 4, 0, cudaMemcpyDeviceToHost, s) !=
+          cudaSuccess ||
+      cudaMemcpyToSymbolAsync(vtc::g_faults, &zero, 4, 0, cudaMemcpyHostToDevice, s) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return PVLC_CUDA_ERROR;
+  *out = v;
+  return PVLC_OK;
+}
 
 int vision_query_tile() { return vtc::QT * vtc::BM; }
 int vision_block_threads() { return vtc::THREADS; }

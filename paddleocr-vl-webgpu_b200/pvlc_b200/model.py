@@ -653,7 +653,11 @@ class _DecodeGraph:
         return hist, (torch.stack(lg, 0) if record_logits else None)
 
     def check_faults(self):
-        """Raise if any decode launch set a device fault flag (waits for the device)."""
+        """Raise if any decode launch set a device fault flag, or any vision / prefill
+        launch ran out of a bounded wait (waits for the device)."""
         flags = sum(w.errors() for w in self.ws)
         if flags:
             raise abi.PvlcError(abi.DEVICE_FAULT_FLAG, f"decode fault flags {flags:#x}")
+        kf = ops.fault_flags()
+        if kf:
+            raise abi.PvlcError(abi.DEVICE_FAULT_FLAG, f"vision / prefill fault flags {kf:#x}")

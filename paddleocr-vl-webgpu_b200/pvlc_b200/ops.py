@@ -188,6 +188,20 @@ class DecodeWorkspace:
         return int(flags.value)
 
 
+FAULT_VISION, FAULT_PREFILL, FAULT_PREFILL_BATCH = 1, 2, 4
+
+
+def fault_flags() -> int:
+    """Read and clear the current device's sticky fault word of the vision and prefill
+    kernels (FAULT_* bits: a launch whose bounded pipeline wait ran out and whose output
+    is incomplete).  Synchronizes the current stream."""
+    flags = ctypes.c_uint32(0)
+    st = abi.lib().pvlc_attn_fault_flags(ctypes.byref(flags), _stream())
+    if st not in (abi.OK, abi.DEVICE_FAULT_FLAG):
+        abi.check(st, "pvlc_attn_fault_flags")
+    return int(flags.value)
+
+
 def _rows(t, dtype, shape, name):
     """Check a [B, H, 128] tensor whose rows may sit at any 16-byte multiple apart (the
     inner [H, 128] contiguous); returns the row stride in elements."""

@@ -228,3 +228,24 @@ def test_batched_prefill_many_prompts_in_groups(cuda_lib):
                                   t["v"][s:e].contiguous(), tables[b][0], tables[b][1], kc1, vc1)
         assert (out[s:e].float() - ref.float()).abs().max().item() <= ATOL, b
         assert torch.equal(kc[b].nan_to_num(7.0), kc1.nan_to_num(7.0)), b
+
+
+def test_fault_word_clear_after_clean_calls(cuda_lib):
+    """pvlc_attn_fault_flags: after clean vision, single-prompt and batched prefill calls
+    the device's sticky fault word of those kernels reads zero (status OK), and a read
+    clears it."""
+    from pvlc_b200 import ops
+    ops.fault_flags()                         # whatever earlier tests left
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(21)
+    T, H, D = 300, 16, 72
+    qv = [torch.from_numpy(rng.standard_normal((T, H, D)).astype(np.float16)).to(dev)
+          for _ in range(3)]
+    ops.vision_varlen_attention(*qv, np.array([0, 100, 300]))
+    _run_case(list(range(3, 3 + 200)), [], 208, seed=3)
+    Ts = [40, 17]
+    offs, host, host_tables, t, tables, kc, vc = _packed_case(Ts, 48, seed=9)
+    out = torch.empty_like(t["q"])
+    ops.decoder_prefill_packed(t["q"], t["k"], t["v"], offs, tables, kc, vc, out)
+    assert ops.fault_flags() == 0
+    assert ops.fault_flags() == 0
