@@ -11,12 +11,16 @@
 // rule as an argmax pass over the logits buffer
 // (crates/pvlc-runtime-web/src/web/decoder_stack_session.rs:308-350).
 //
-// Work split: one CTA per 256 vocabulary rows (an N tile) and every row of
-// hidden (up to two M tiles of 128).  Per K step of 64 dims the producer warp
-// loads the N tile's 256 x 64 weights (32 KB, TMA, 128B swizzle) and each M
-// tile's 128 x 64 slice of hidden (16 KB; rows past `rows` are TMA zero
-// fill) into a 3-stage ring; the MMA warp issues four M128 N256 K16 MMAs per
-// M tile into TMEM columns [256 m, 256 m + 256).  Epilogue: one warpgroup
+// Work split: one CTA per SM walks the 256-row vocabulary tiles (N tiles
+// blockIdx.x, + gridDim.x, ...) with every row of hidden (up to two M tiles
+// of 128).  Per K step of 64 dims the producer warp loads the N tile's
+// 256 x 64 weights (32 KB, TMA, 128B swizzle) and each M tile's 128 x 64
+// slice of hidden (16 KB; rows past `rows` are TMA zero fill) into a 3-stage
+// ring that runs on across tiles; the MMA warp issues four M128 N256 K16
+// MMAs per M tile into TMEM: with one M tile the accumulators alternate
+// between columns 0 and 256 by tile, so an epilogue overlaps the next tile's
+// MMAs; with two they take columns [256 m, 256 m + 256) and the next tile
+// waits for the epilogue (acc_free).  Epilogue: one warpgroup
 // per M tile, thread = row = TMEM lane; it reads its 256 logits and keeps the
 // largest in total_cmp order (the first, i.e. smallest, index on ties), then
 // folds it into the row's 64-bit key with one atomicMax:
@@ -48,7 +52,7 @@ constexpr uint32_t SZ_B = BN * BK * 2;                 // 32 KB
 constexpr uint32_t SZ_A = BM * BK * 2;                 // 16 KB per M tile
 constexpr uint32_t STAGE_BYTES = SZ_B + MAX_MT * SZ_A; // 64 KB
 constexpr uint32_t OFF_BARS = STAGES * STAGE_BYTES;
-constexpr int NBARS = 2 * STAGES + 1;                  // full, empty, done
+constexpr int NBARS = 2 * STAGES + 4;                  // full, empty, acc_full[2], acc_free[2]
 constexpr uint32_t OFF_MISC = OFF_BARS + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
 static_assert(SMEM_BYTES <= 227 * 1024, "lm-head shared memory exceeds the sm_100 limit");
@@ -77,18 +81,29 @@ __global__ void __launch_bounds__(THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BARS);
   uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2] a tile's accumulators are complete
+  uint64_t* acc_free = acc_full + 2;     // [2] the epilogue has read them
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
   // misc[0]: TMEM base, misc[1]: abort
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t n0 = blockIdx.x * BN;
+  const int ks = static_cast<int>(p.ksteps);
+  const int mt = static_cast<int>(p.mtiles);
+  // accumulator buffers: two (double-buffered tiles) for one M tile, one for two
+  const int nacc = mt == 1 ? 2 : 1;
+  // this CTA's vocabulary tiles: blockIdx.x, + gridDim.x, ...
+  const uint32_t ntile = (p.vocab + BN - 1) / BN;
+  const uint32_t my_tiles =
+      blockIdx.x < ntile ? (ntile - 1 - blockIdx.x) / gridDim.x + 1 : 0u;
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_free[a], 4 * mt);   // every epilogue warp
+    }
     misc[1] = 0;
     fence_mbar_init();
   }
@@ -100,8 +115,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = misc[0];
-  const int ks = static_cast<int>(p.ksteps);
-  const int mt = static_cast<int>(p.mtiles);
 
   if (warp == 8) {
     if (lane == 0) {
@@ -110,20 +123,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc::tma_prefetch_desc(&maps.b);
       // hidden is produced by the kernel ahead (the final norm)
       pdl_wait();
-      int issued = 0;
-      for (int s = 0; s < ks; ++s) {
-        const int st = s % STAGES;
-        if (misc[1] || !mbar_wait(&empty[st], ((s / STAGES) & 1) ^ 1)) { misc[1] = 1; break; }
-        uint8_t* base = smem + st * STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[st], SZ_B + mt * SZ_A);
-        tc::tma_load_2d(base, &maps.b, s * BK, n0, &full[st]);
-        for (int m = 0; m < mt; ++m)
-          tc::tma_load_2d(base + SZ_B + m * SZ_A, &maps.a, s * BK, m * BM, &full[st]);
-        issued = s + 1;
+      uint32_t g = 0;   // k steps issued so far (ring position)
+      for (uint32_t tt = 0; tt < my_tiles && !misc[1]; ++tt) {
+        const uint32_t n0 = (blockIdx.x + tt * gridDim.x) * BN;
+        for (int s = 0; s < ks; ++s, ++g) {
+          const int st = static_cast<int>(g % STAGES);
+          if (misc[1] || !mbar_wait(&empty[st], ((g / STAGES) & 1) ^ 1)) { misc[1] = 1; break; }
+          uint8_t* base = smem + st * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[st], SZ_B + mt * SZ_A);
+          tc::tma_load_2d(base, &maps.b, s * BK, n0, &full[st]);
+          for (int m = 0; m < mt; ++m)
+            tc::tma_load_2d(base + SZ_B + m * SZ_A, &maps.a, s * BK, m * BM, &full[st]);
+        }
       }
       // the last loads must land before the CTA may exit
-      for (int s = (issued > STAGES ? issued - STAGES : 0); s < issued; ++s)
-        mbar_wait(&full[s % STAGES], (s / STAGES) & 1);
+      for (uint32_t g2 = (g > STAGES ? g - STAGES : 0); g2 < g; ++g2)
+        mbar_wait(&full[g2 % STAGES], (g2 / STAGES) & 1);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------- MMA issuer
@@ -132,42 +147,64 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint64_t db = tc::smem_desc(s0, 16, 1024, tc::kSw128);
     const uint64_t da = tc::smem_desc(s0 + SZ_B, 16, 1024, tc::kSw128);
     bool ok = true;
-    int issued = 0;
-    for (int s = 0; s < ks && ok; ++s) {
-      const int st = s % STAGES;
-      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&full[st], (s / STAGES) & 1))) {
+    uint32_t g = 0, done = 0;
+    for (uint32_t tt = 0; tt < my_tiles && ok; ++tt) {
+      const int a = static_cast<int>(tt % nacc);
+      const uint32_t use = tt / nacc;
+      if (use > 0 &&
+          !__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&acc_free[a], (use - 1) & 1))) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
-      const uint64_t so = (uint64_t)st * (STAGE_BYTES >> 4);
-      if (tc::elect_one()) {
-        for (int m = 0; m < mt; ++m) {
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)   // 32 bytes per K16 step: +2 in the address field
-            tc::mma_ss(tmem + (uint32_t)(BN * m), da + so + (uint64_t)m * (SZ_A >> 4) + 2 * kk,
-                       db + so + 2 * kk, idesc, (s > 0 || kk > 0) ? 1u : 0u);
+      const uint32_t acc = tmem + static_cast<uint32_t>(a * BN);
+      for (int s = 0; s < ks; ++s, ++g) {
+        const int st = static_cast<int>(g % STAGES);
+        if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&full[st], (g / STAGES) & 1))) {
+          ok = false;
+          break;
         }
-        tc::commit(&empty[st]);
-        if (s == ks - 1) tc::commit(done);
+        tc::fence_after_sync();
+        const uint64_t so = (uint64_t)st * (STAGE_BYTES >> 4);
+        if (tc::elect_one()) {
+          for (int m = 0; m < mt; ++m) {
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)   // 32 bytes per K16 step: +2 in the address field
+              tc::mma_ss(acc + (uint32_t)(BN * m), da + so + (uint64_t)m * (SZ_A >> 4) + 2 * kk,
+                         db + so + 2 * kk, idesc, (s > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::commit(&empty[st]);
+          if (s == ks - 1) tc::commit(&acc_full[a]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
-      issued = s + 1;
+      if (ok) ++done;
     }
     if (!ok && lane == 0) misc[1] = 1;
     // never exit with MMAs in flight or commit arrivals still pending
-    for (int s = (issued > STAGES ? issued - STAGES : 0); s < issued; ++s)
-      mbar_wait(&empty[s % STAGES], (s / STAGES) & 1);
-    if (issued == ks && ks > 0) mbar_wait(done, 0);
+    for (uint32_t g2 = (g > STAGES ? g - STAGES : 0); g2 < g; ++g2)
+      mbar_wait(&empty[g2 % STAGES], (g2 / STAGES) & 1);
+    if (done > 0) {
+      const uint32_t last = done - 1;
+      mbar_wait(&acc_full[last % nacc], (last / nacc) & 1);
+    }
   } else if (warp / 4 < mt) {
     // ------------------------------------------------------- epilogue
     const int m = warp / 4;
     const int i = (warp & 3) * 32 + lane;            // row within the M tile = TMEM lane
     const uint32_t row = m * BM + i;
-    const uint32_t tD = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + (uint32_t)(BN * m);
-    const bool good = __all_sync(0xffffffffu, mbar_wait(done, 0) && misc[1] == 0);
-    if (good) {
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    bool good = true;
+    for (uint32_t tt = 0; tt < my_tiles && good; ++tt) {
+      const int a = static_cast<int>(tt % nacc);
+      const uint32_t use = tt / nacc;
+      const uint32_t n0 = (blockIdx.x + tt * gridDim.x) * BN;
+      if (!__all_sync(0xffffffffu, misc[1] == 0 && mbar_wait(&acc_full[a], use & 1))) {
+        good = false;
+        break;
+      }
       tc::fence_after_sync();
+      const uint32_t tD = tmem + lane_off + static_cast<uint32_t>(a * BN + BN * m);
       const uint32_t valid = p.vocab - n0 < (uint32_t)BN ? p.vocab - n0 : (uint32_t)BN;
       uint32_t best = 0, best_c = 0xFFFFFFFFu;
 #pragma unroll 1
@@ -186,16 +223,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
+      // the accumulators may take the next tile
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[a]);
       if (row < p.rows && best_c != 0xFFFFFFFFu)
         atomicMax(p.keys + row, ((unsigned long long)best << 32) |
                                     (unsigned long long)(0xFFFFFFFFu - (n0 + best_c)));
-    } else if (lane == 0) {
-      atomicOr(p.flags, kFlagTimeout);
     }
+    if (!good && lane == 0) atomicOr(p.flags, kFlagTimeout);
   }
 
   tc::fence_before_sync();
   __syncthreads();
+  if (tid == 0 && misc[1]) atomicOr(p.flags, kFlagTimeout);
   if (warp == 8) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, TMEM_COLS);
@@ -269,7 +310,11 @@ int lm_head_top1_launch(const LmHeadArgs& a, cudaStream_t stream) {
   if (cudaMemsetAsync(a.workspace, 0, lm_head_workspace_bytes(a.rows), stream) != cudaSuccess)
     return PVLC_CUDA_ERROR;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.vocab + lmh::BN - 1) / lmh::BN);
+  // persistent: one CTA per SM walks the vocabulary tiles (fewer when there are fewer tiles)
+  const int sms = device_sm_count();
+  if (sms <= 0) return PVLC_CUDA_ERROR;
+  const uint32_t ntile = (a.vocab + lmh::BN - 1) / lmh::BN;
+  cfg.gridDim = dim3(ntile < (uint32_t)sms ? ntile : (uint32_t)sms);
   cfg.blockDim = dim3(lmh::THREADS);
   cfg.dynamicSmemBytes = lmh::SMEM_BYTES;
   cfg.stream = stream;
