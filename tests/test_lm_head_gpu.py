@@ -27,8 +27,8 @@ def _ref_top1(logits):
     return np.argmax(logits == m, axis=1)
 
 
-@pytest.mark.parametrize("rows,vocab,K", [(1, 1000, 128), (3, 1000, 128), (129, 5000, 256),
-                                          (256, 2304, 64)])
+@pytest.mark.parametrize("rows,vocab,K", [(1, 1000, 128), (3, 1000, 128), (5, 1000, 192),
+                                          (129, 5000, 256), (256, 2304, 64)])
 def test_integer_logits_match_the_oracle_with_ties(cuda_lib, rows, vocab, K):
     from pvlc_b200 import ops
     rng = np.random.default_rng(rows + vocab)
