@@ -353,6 +353,18 @@ int pvlc_lm_head_top1(const pvlc_half* hidden, uint32_t rows, const pvlc_half* l
                       size_t workspace_bytes, int32_t* tokens, float* logits, void* stream);
 int pvlc_lm_head_top1_errors(void* workspace, uint32_t rows, uint32_t* flags_out, void* stream);
 
+/* ---- model packs: BLAKE3 section digests on the device ----------------- */
+/* BLAKE3 (plain hash mode, 32-byte output) of `bytes` bytes of device memory
+ * at `data`: the checksum every .pvlc pack directory entry carries for its
+ * section (crates/pvlc-pack/src/lib.rs: PackBuilder::build hashes each
+ * section with blake3::hash, PackReader::open recomputes and compares), so a
+ * pack uploaded to HBM is verified where it sits.  `digest` is 32 bytes of
+ * device memory; `workspace` (16-byte aligned) holds
+ * pvlc_blake3_workspace_bytes(bytes) of scratch.  Enqueued on `stream`. */
+size_t pvlc_blake3_workspace_bytes(uint64_t bytes);
+int pvlc_blake3(const void* data, uint64_t bytes, void* workspace, size_t workspace_bytes,
+                uint8_t* digest, void* stream);
+
 /* ----------------------------------------------------------------------------
  * Checkpoint import on the device: BF16 -> IEEE binary16, round to nearest,
  * ties to even.

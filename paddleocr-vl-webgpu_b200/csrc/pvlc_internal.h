@@ -49,6 +49,11 @@ struct VisionArgs {
 // prefill kernels (PVLC_FAULT_* bits); synchronizes `s`.
 int vision_fault_word(uint32_t* out, cudaStream_t s);
 int prefill_fault_word(uint32_t* out, cudaStream_t s);
+// BLAKE3 of a device buffer (blake3.cu): scratch of blake3_workspace_bytes,
+// the 32-byte digest written to device memory.
+size_t blake3_workspace_bytes(uint64_t bytes);
+int blake3_launch(const void* data, uint64_t bytes, void* workspace, uint8_t* digest,
+                  cudaStream_t s);
 int vision_query_tile();
 int vision_block_threads();
 // Scratch for the rotated q and k (2 x tokens x heads x 72 fp16).

@@ -85,6 +85,8 @@ _SIGNATURES = {
                                                 _P, _P]),
     "pvlc_attn_decode_errors": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_uint32), _P]),
     "pvlc_attn_fault_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _P]),
+    "pvlc_blake3_workspace_bytes": (ctypes.c_size_t, [ctypes.c_uint64]),
+    "pvlc_blake3": (ctypes.c_int, [_P, ctypes.c_uint64, _P, ctypes.c_size_t, _P, _P]),
     "pvlc_attn_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32,
                                                 _U32, _U32, _P, _P]),
     "pvlc_image_patches_workspace_bytes": (ctypes.c_size_t, [_U32, _U32, _U32, _U32]),

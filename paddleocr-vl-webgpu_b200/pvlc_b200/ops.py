@@ -188,6 +188,25 @@ class DecodeWorkspace:
         return int(flags.value)
 
 
+def blake3(data, digest=None, workspace=None):
+    """BLAKE3 (plain hash, 32 bytes) of a contiguous CUDA uint8 tensor, computed on the
+    device (pvlc_blake3); returns the [32] uint8 device digest (no host sync)."""
+    if not isinstance(data, torch.Tensor) or not data.is_cuda or data.dtype != torch.uint8:
+        raise TypeError("data must be a CUDA uint8 tensor")
+    if not data.is_contiguous():
+        raise ValueError("data must be contiguous")
+    n = data.numel()
+    need = int(abi.lib().pvlc_blake3_workspace_bytes(n))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=data.device)
+    if digest is None:
+        digest = torch.empty(32, dtype=torch.uint8, device=data.device)
+    st = abi.lib().pvlc_blake3(_ptr(data) if n else None, n, _ptr(workspace), workspace.numel(),
+                               _ptr(digest), _stream())
+    abi.check(st, "pvlc_blake3")
+    return digest
+
+
 FAULT_VISION, FAULT_PREFILL, FAULT_PREFILL_BATCH = 1, 2, 4
 
 

@@ -13,7 +13,7 @@ from pvlc_b200 import abi
 def _header_functions():
     text = open(abi.HEADER_PATH).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(pvlc_(?:attn|plan|image|add_norm|gelu|silu_mul|bf16_to_f16|lm_head)\w*)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(pvlc_(?:attn|plan|image|add_norm|gelu|silu_mul|bf16_to_f16|lm_head|blake3)\w*)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol():
