@@ -356,7 +356,8 @@ def run_gpu(args, rank, world, local_rank, dist):
 
 
 def run_components(args, dev, tf_peak, peak_src,
-                   which=("decode_b1", "vision", "prefill", "prefill_batch", "checkpoint"),
+                   which=("decode_b1", "vision", "prefill", "prefill_batch", "checkpoint",
+                          "pack_blake3"),
                    iters=20, warm=3):
     import torch
     cpu = not args.skip_cpu
@@ -388,6 +389,54 @@ def run_components(args, dev, tf_peak, peak_src,
         res["decoder_prefill_batch"] = bench_prefill_batch(dev, timeit, tf_peak, peak_src)
     if "checkpoint" in which:
         res["checkpoint_import"] = bench_checkpoint(dev, timeit)
+    if "pack_blake3" in which:
+        res["pack_blake3"] = bench_pack_blake3(dev, timeit, cpu)
+    return res
+
+
+def bench_pack_blake3(dev, timeit, cpu):
+    """Model-pack verification: BLAKE3 of a 1 GiB section resident in HBM by pvlc_blake3
+    (the digest PackReader.open checks), timed on the device; checked against the
+    `blake3` package.  CPU baseline: the same package (the reference implementation's
+    SIMD code) on host threads over a 256 MiB sample."""
+    import torch
+
+    from pvlc_b200 import ops
+    n = 1 << 30
+    g = torch.Generator(device=dev)
+    g.manual_seed(6)
+    data = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=g)
+    ws = torch.empty(int(ops.abi.lib().pvlc_blake3_workspace_bytes(n)), dtype=torch.uint8,
+                     device=dev)
+    dig = torch.empty(32, dtype=torch.uint8, device=dev)
+    ms = timeit(lambda: ops.blake3(data, digest=dig, workspace=ws))
+    res = {"workload": "BLAKE3 of one 1 GiB pack section in HBM (uniform random bytes)",
+           "ms": round(ms, 4), "value": round(n / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "kernel": "pvlc::b3::chunk_kernel + parent_kernel",
+           "bound": "integer ALU pipe (the XORs and rotates of the G function; the "
+                    "additions issue to the FMA pipe); HBM traffic is 1 byte per byte"}
+    try:
+        import blake3
+        host = data.cpu().numpy().tobytes()
+        res["checked"] = bytes(dig.cpu().numpy()) == blake3.blake3(
+            host, max_threads=blake3.blake3.AUTO).digest()
+        if cpu:
+            sample = host[:1 << 28]
+            cores = os.cpu_count() or 1
+            t0 = time.perf_counter()
+            reps = 0
+            while time.perf_counter() - t0 < 3.0:
+                blake3.blake3(sample, max_threads=blake3.blake3.AUTO).digest()
+                reps += 1
+            dt = (time.perf_counter() - t0) / reps
+            res["cpu_baseline"] = {"value": round(len(sample) / dt / 1e9, 2), "unit": "GB/s",
+                                   "cores": cores, "kind": "reference",
+                                   "sample": "256 MiB of the same section, the blake3 "
+                                             f"package with all {cores} host threads, "
+                                             f"{reps} passes"}
+    except ImportError as e:
+        res["checked"] = f"not checked: {e}"
+    del data
     return res
 
 
@@ -1012,7 +1061,7 @@ def main():
     ap.add_argument("--e2e-requests", type=int, default=256)
     ap.add_argument("--e2e-tokens", type=int, default=512)
     ap.add_argument("--only", choices=["decode_b1", "vision", "prefill", "prefill_batch",
-                                       "checkpoint", "e2e"],
+                                       "checkpoint", "pack_blake3", "e2e"],
                     default=None,
                     help="time one prefill component alone (profiling runs); prints its line")
     args = ap.parse_args()
