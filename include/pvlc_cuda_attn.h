@@ -239,8 +239,8 @@ int pvlc_attn_decode_strided(const pvlc_half* q, uint32_t q_row_stride, const pv
  * PVLC_OK when no flag was set, PVLC_DEVICE_FAULT_FLAG otherwise. */
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
 
-/* Sticky fault word of the vision and prefill kernels on the calling thread's
- * current device.  It has no counterpart in the reference (its WebGPU
+/* Sticky fault word of the vision, prefill and projection (pvlc_linear)
+ * kernels on the calling thread's current device.  It has no counterpart in the reference (its WebGPU
  * dispatches cannot time out inside a shader).  A launch whose bounded
  * pipeline wait ran out stops early -- its output is then incomplete -- and
  * sets its kernel's bit; the bits of every such launch on the device since
@@ -250,6 +250,7 @@ int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream);
 #define PVLC_FAULT_VISION 1u
 #define PVLC_FAULT_PREFILL 2u
 #define PVLC_FAULT_PREFILL_BATCH 4u
+#define PVLC_FAULT_LINEAR 8u
 int pvlc_attn_fault_flags(uint32_t* flags_out, void* stream);
 
 /* Allocation-free variant of pvlc_attn_decode.  It has no counterpart in the
@@ -352,6 +353,40 @@ int pvlc_lm_head_top1(const pvlc_half* hidden, uint32_t rows, const pvlc_half* l
                       uint32_t vocab, uint32_t hidden_dim, void* workspace,
                       size_t workspace_bytes, int32_t* tokens, float* logits, void* stream);
 int pvlc_lm_head_top1_errors(void* workspace, uint32_t rows, uint32_t* flags_out, void* stream);
+
+/* ----------------------------------------------------------------------------
+ * Decode-step projections (decoder-stack glue beside the attention path).
+ *
+ * Replaces the decoder layer's GEMV/GEMM passes at decode batch sizes -- the
+ * QKV, O, gate-up and down projections of the WebGPU session
+ * (crates/pvlc-wgsl/src/lib.rs:1770-1835, crates/pvlc-runtime-core/src/lib.rs:
+ * 1175-1548) -- and the gated MLP product (crates/pvlc-cpu-ref/src/lib.rs:
+ * 1385-1390) fused into the gate-up projection.
+ *
+ * gate = 0: out[r, f] = fp16(sum_k x[r, k] * w[f, k]) for r < rows, f < n.
+ * gate = 1: w's rows come in blocks of 128: 64 gate rows, then the 64 up rows
+ *   of the same output columns (row 128 b + j gates column 64 b + j, row
+ *   128 b + 64 + j is its up row); out[r, c] = fp16(silu(fp16(g)) * fp16(u))
+ *   for c < n / 2, with g, u the two projections of column c.
+ * fp16 operands, f32 accumulation.  x: device [rows, k] with row pitch ldx
+ * elements; w: device [n, k] contiguous; out: device with row pitch ldo.
+ * rows 1..PVLC_LINEAR_MAX_ROWS, n a multiple of 128, k a multiple of 64, ldx
+ * and ldo multiples of 8, pointers 16-byte aligned.  split: the K slices per
+ * 128-feature tile (1, 2, 4, 8 or 16, at most k / 64), 0 for the library's
+ * choice; the slices of a tile run as one thread-block cluster and their
+ * partial sums are added in slice order, so results are reproducible.  No
+ * device memory is allocated and no scratch is needed.
+ * The call is launched with programmatic dependent launch: the weight tiles
+ * are read before the kernel waits for the work ahead of it on `stream`, so
+ * `w` must not be written by that work; x and out are ordered as usual.  A pipeline timeout sets PVLC_FAULT_LINEAR in the sticky fault word
+ * (pvlc_attn_fault_flags).
+ */
+#define PVLC_LINEAR_MAX_ROWS 256u
+#define PVLC_LINEAR_MAX_K 16384u
+#define PVLC_LINEAR_MAX_N 65536u
+int pvlc_linear(const pvlc_half* x, uint32_t rows, uint32_t ldx, const pvlc_half* w, uint32_t n,
+                uint32_t k, uint32_t gate, uint32_t split, pvlc_half* out, uint32_t ldo,
+                void* stream);
 
 /* ---- model packs: BLAKE3 section digests on the device ----------------- */
 /* BLAKE3 (plain hash mode, 32-byte output) of `bytes` bytes of device memory

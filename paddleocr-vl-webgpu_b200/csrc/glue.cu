@@ -216,12 +216,6 @@ bool launch_row_kernel(float* h, const __half* d, uint32_t rows, uint32_t width,
   return false;
 }
 
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 // 0.5 x (1 + tanh(u)), u = sqrt(2 / pi) (x + 0.044715 x^3)
 // (crates/pvlc-cpu-ref/src/lib.rs:359-362), as x / (1 + 2^(-2u log2 e)).
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -232,11 +226,6 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 
 // crates/pvlc-cpu-ref/src/lib.rs:364-367
 __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.70710677f)); }
-
-// crates/pvlc-cpu-ref/src/lib.rs:354-357: g / (1 + e^(-g))
-__device__ __forceinline__ float silu(float g) {
-  return g * rcp_approx(1.f + fast_exp2(g * -1.4426950408889634f));
-}
 
 template <int KIND>
 __device__ __forceinline__ uint32_t gelu_h2(uint32_t w) {

@@ -71,11 +71,9 @@ int device_sm_count() {
   return n;
 }
 
-namespace {
-
 constexpr int kDefaultSms = 148;  // B200; used by plans when no GPU is visible
 
-int sms_or_default() {
+int sms_or_default_count() {
   int dev_count = 0;
   if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0) {
     cudaGetLastError();
@@ -84,6 +82,10 @@ int sms_or_default() {
   const int n = device_sm_count();
   return n > 0 ? n : kDefaultSms;
 }
+
+namespace {
+
+int sms_or_default() { return sms_or_default_count(); }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -487,8 +489,11 @@ int pvlc_attn_fault_flags(uint32_t* flags_out, void* stream) {
   if (st != PVLC_OK) return st;
   st = prefill_fault_word(&b, s);
   if (st != PVLC_OK) return st;
-  *flags_out = a | b;
-  return (a | b) ? PVLC_DEVICE_FAULT_FLAG : PVLC_OK;
+  uint32_t c = 0;
+  st = linear_fault_word(&c, s);
+  if (st != PVLC_OK) return st;
+  *flags_out = a | b | c;
+  return (a | b | c) ? PVLC_DEVICE_FAULT_FLAG : PVLC_OK;
 }
 
 int pvlc_attn_decode_errors(void* workspace, uint32_t* flags_out, void* stream) {

@@ -194,6 +194,20 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// SiLU of the decoder MLP gate, g / (1 + e^(-g))
+// (crates/pvlc-cpu-ref/src/lib.rs:354-357), with the hardware base-2
+// exponential and reciprocal; shared by the SiLU-gate glue kernel and the
+// fused gate epilogue of the decode-step projections.
+__device__ __forceinline__ float silu(float g) {
+  return g * rcp_approx(1.f + fast_exp2(g * -1.4426950408889634f));
+}
+
 // Packed f32x2 arithmetic (one instruction for two lanes of a pair).
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
   uint64_t r;

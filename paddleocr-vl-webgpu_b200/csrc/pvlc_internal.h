@@ -110,7 +110,25 @@ size_t lm_head_workspace_bytes(uint32_t rows);
 size_t lm_head_flags_offset(uint32_t rows);
 int lm_head_top1_launch(const LmHeadArgs& a, cudaStream_t stream);
 
+// Decode-step projections (linear.cu).
+struct LinearArgs {
+  const pvlc_half* x;    // [rows, k], row pitch ldx
+  uint32_t rows, ldx;
+  const pvlc_half* w;    // [n, k] contiguous
+  uint32_t n, k;
+  uint32_t gate;         // 1: fused SiLU gate, out has n / 2 columns
+  uint32_t split;        // K slices per feature tile (power of two <= 16)
+  pvlc_half* out;
+  uint32_t ldo;
+};
+uint32_t linear_auto_split(uint32_t rows, uint32_t n, uint32_t k, int sms);
+bool linear_split_fits(uint32_t rows, uint32_t k, uint32_t split);
+int linear_launch(const LinearArgs& a, cudaStream_t stream);
+int linear_fault_word(uint32_t* out, cudaStream_t s);
+
 int device_sm_count();
+// The current device's SM count, or the B200's 148 when no GPU is visible.
+int sms_or_default_count();
 // cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, smem_bytes) once per
 // kernel, device and context (thread-safe); a PVLC_* status.
 int set_smem_attribute_once(const void* kernel, int smem_bytes);

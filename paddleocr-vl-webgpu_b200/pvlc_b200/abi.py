@@ -100,6 +100,7 @@ _SIGNATURES = {
     "pvlc_lm_head_top1": (ctypes.c_int, [_P, _U32, _P, _U32, _U32, _P, ctypes.c_size_t, _P, _P,
                                          _P]),
     "pvlc_lm_head_top1_errors": (ctypes.c_int, [_P, _U32, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "pvlc_linear": (ctypes.c_int, [_P, _U32, _U32, _P, _U32, _U32, _U32, _U32, _P, _U32, _P]),
     "pvlc_plan_vision_varlen": (ctypes.c_int, [_P, _U32, _U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_prefill": (ctypes.c_int, [_U32, _U32, _U32, ctypes.POINTER(Plan)]),
     "pvlc_plan_decoder_kv_session": (ctypes.c_int, [_U32, _U32, _U32, _U32, _U32,

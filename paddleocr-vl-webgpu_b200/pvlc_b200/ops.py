@@ -207,12 +207,12 @@ def blake3(data, digest=None, workspace=None):
     return digest
 
 
-FAULT_VISION, FAULT_PREFILL, FAULT_PREFILL_BATCH = 1, 2, 4
+FAULT_VISION, FAULT_PREFILL, FAULT_PREFILL_BATCH, FAULT_LINEAR = 1, 2, 4, 8
 
 
 def fault_flags() -> int:
-    """Read and clear the current device's sticky fault word of the vision and prefill
-    kernels (FAULT_* bits: a launch whose bounded pipeline wait ran out and whose output
+    """Read and clear the current device's sticky fault word of the vision, prefill and
+    projection kernels (FAULT_* bits: a launch whose bounded pipeline wait ran out and whose output
     is incomplete).  Synchronizes the current stream."""
     flags = ctypes.c_uint32(0)
     st = abi.lib().pvlc_attn_fault_flags(ctypes.byref(flags), _stream())
@@ -333,6 +333,55 @@ def silu_mul(gate_up, out=None):
     _need(out, torch.float16, (rows, w2 // 2), "out")
     abi.check(abi.lib().pvlc_silu_mul(_ptr(gate_up), rows, w2 // 2, _ptr(out), _stream()),
               "pvlc_silu_mul")
+    return out
+
+
+LINEAR_MAX_ROWS = 256           # PVLC_LINEAR_MAX_ROWS
+
+
+def _rows_view(t, name):
+    """A 2-D fp16 CUDA tensor whose rows may be pitched (stride(1) == 1)."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float16:
+        raise TypeError(f"{name} must be torch.float16, got {t.dtype}")
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be 2-D with unit column stride")
+    return t.stride(0) if t.shape[0] > 1 else max(t.stride(0), t.shape[1])
+
+
+def gate_up_blocks(gate_w, up_w):
+    """The gate-up weight of the fused SiLU projection: 128-row blocks of 64 gate rows
+    followed by the 64 up rows of the same output columns ([2I, K] from two [I, K])."""
+    i, k = gate_w.shape
+    if up_w.shape != (i, k) or i % 64:
+        raise ValueError("gate and up weights must both be [I, K] with I a multiple of 64")
+    return torch.stack((gate_w.view(i // 64, 64, k), up_w.view(i // 64, 64, k)),
+                       dim=1).reshape(2 * i, k).contiguous()
+
+
+def linear(x, w, out=None, gate=False, split=0):
+    """Decode-step projection on the tensor cores (pvlc_linear): x [rows, K] fp16 (rows
+    may be pitched) times w [N, K] fp16 -> out [rows, N] fp16 with f32 accumulation, or
+    with gate=True (w laid out by gate_up_blocks) out [rows, N / 2] =
+    fp16(silu(fp16(gate)) * fp16(up)).  Rows beyond 256 are taken in groups of 256.
+    split: K slices per 128-feature tile (0: the library's choice)."""
+    rows, K = x.shape
+    ldx = _rows_view(x, "x")
+    N = w.shape[0]
+    _need(w, torch.float16, (N, K), "w")
+    width = N // 2 if gate else N
+    if out is None:
+        out = torch.empty((rows, width), dtype=torch.float16, device=x.device)
+    ldo = _rows_view(out, "out")
+    if tuple(out.shape) != (rows, width):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(rows, width)}")
+    for r0 in range(0, rows, LINEAR_MAX_ROWS):
+        r1 = min(rows, r0 + LINEAR_MAX_ROWS)
+        st = abi.lib().pvlc_linear(
+            _ptr(x[r0:r1]), r1 - r0, ldx, _ptr(w), N, K, int(bool(gate)), split,
+            _ptr(out[r0:r1]), ldo, _stream())
+        abi.check(st, "pvlc_linear")
     return out
 
 

@@ -13,7 +13,7 @@ from pvlc_b200 import abi
 def _header_functions():
     text = open(abi.HEADER_PATH).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(pvlc_(?:attn|plan|image|add_norm|gelu|silu_mul|bf16_to_f16|lm_head|blake3)\w*)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(pvlc_(?:attn|plan|image|add_norm|gelu|silu_mul|bf16_to_f16|lm_head|blake3|linear)\w*)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol():
@@ -149,3 +149,21 @@ def test_batched_prefill_host_validation():
     assert call([0, 10, 10], 2) == abi.INVALID_SEQUENCE_BOUNDARIES     # empty prompt
     assert call([0, 10, 90], 2) == abi.CAPACITY_EXHAUSTED               # 80 tokens > 64
     assert call([0, 10, 20], 2, stride=64 * 256 - 8) == abi.LENGTH_MISMATCH
+
+
+def test_linear_host_validation():
+    """pvlc_linear rejects bad geometry and splits before any device call."""
+    lib = abi.lib()
+    p = ctypes.c_void_p(1 << 20)     # aligned, never dereferenced: every case fails first
+    def call(rows=32, ldx=1024, n=2560, k=1024, gate=0, split=8, ldo=2560, x=p, w=p, out=p):
+        return lib.pvlc_linear(x, rows, ldx, w, n, k, gate, split, out, ldo, None)
+    assert call(rows=0) == abi.ZERO_DIMENSION
+    assert call(n=0) == abi.ZERO_DIMENSION
+    for bad in (dict(rows=257), dict(n=2500, ldo=2500), dict(k=1000, ldx=1000), dict(ldx=1020),
+                dict(ldo=2552), dict(ldo=2564), dict(gate=2), dict(split=3), dict(split=32),
+                dict(k=128, ldx=128, split=4), dict(gate=1, n=6144, ldo=3068)):
+        assert call(**bad) == abi.INVALID_DECODER_GEOMETRY, bad
+    assert call(x=None) == abi.NULL_POINTER
+    assert call(out=None) == abi.NULL_POINTER
+    assert call(w=ctypes.c_void_p((1 << 20) + 8)) == abi.MISALIGNED_POINTER
+    assert call(out=ctypes.c_void_p((1 << 20) + 2)) == abi.MISALIGNED_POINTER
