@@ -381,6 +381,8 @@ def run_components(args, dev, tf_peak, peak_src,
 
     if "decode_b1" in which:
         res["decode_b1"] = bench_decode_b1(dev, timeit)
+        if cpu:
+            res["decode_b1"]["cpu_baseline"] = cpu_decode_b1_baseline()
     if "vision" in which:
         res["vision_prefill"] = bench_vision(dev, timeit, tf_peak, peak_src, cpu)
     if "prefill" in which:
@@ -393,6 +395,8 @@ def run_components(args, dev, tf_peak, peak_src,
         res["pack_blake3"] = bench_pack_blake3(dev, timeit, cpu)
     if "decode_linear" in which:
         res["decode_linear"] = bench_decode_linear(dev)
+        if cpu:
+            res["decode_linear"]["cpu_baseline"] = cpu_linear_baseline()
     return res
 
 
@@ -684,6 +688,57 @@ def bench_decode_b1(dev, timeit):
             "note": "device time per call from a CUDA graph of 256 calls; 1 MB per call, so "
                     "launch and pipeline latency, not bandwidth, set the time",
             "kernel": "pvlc::decode::decode_kernel"}
+
+
+def cpu_decode_b1_baseline(seconds: float = 1.0):
+    """configs[0] on the host: the oracle's decode step (C++ restatement of pvlc-cpu-ref:
+    M-RoPE of q and the new key, append, GQA attention over 1024 rows) repeated for about a
+    second; GB/s of the same algorithmic bytes as the device component."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    from pvlc_b200 import positions
+    L, cap = 1023, 1040
+    cos, sin = positions.linear_rope_tables(cap)
+    rng = np.random.default_rng(0)
+    kc = rng.standard_normal((cap, KVH, HD)).astype(np.float16).astype(np.float32)
+    vc = rng.standard_normal((cap, KVH, HD)).astype(np.float16).astype(np.float32)
+    q = rng.standard_normal((QH * HD,)).astype(np.float32)
+    kn = rng.standard_normal((KVH * HD,)).astype(np.float32)
+    vn = rng.standard_normal((KVH * HD,)).astype(np.float32)
+    nbytes = 2 * (L + 1) * KVH * HD * 2 + 2 * QH * HD * 2
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        O.decode_step(q, kn, vn, cos, sin, L, kc, vc, L)
+        calls += 1
+    el = time.perf_counter() - t0
+    return {"value": round(nbytes * calls / el / 1e9, 3), "unit": "GB/s", "cores": O.threads(),
+            "kind": "port",
+            "sample": f"{calls} batch-1 decode calls at 1024 rows, {el:.2f} s"}
+
+
+def cpu_linear_baseline(rows: int = 32, reps: int = 3):
+    """The decode layer's four projections at `rows` rows through the oracle's linear (the
+    reference's linear_f32 order, f32) on the host cores; GB/s of the fp16 weight bytes
+    the device component reads."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pvlc_oracle as O
+    rng = np.random.default_rng(8)
+    shapes = [(1024, 2560), (2048, 1024), (1024, 6144), (3072, 1024)]
+    mats = [(rng.standard_normal((rows, k)).astype(np.float32),
+             (rng.standard_normal((n, k)) * k ** -0.5).astype(np.float32)) for k, n in shapes]
+    wbytes = sum(n * k * 2 for k, n in shapes)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for x, w in mats:
+            O.linear(x, w)
+    el = (time.perf_counter() - t0) / reps
+    return {"value": round(wbytes / el / 1e9, 3), "unit": "GB/s", "cores": O.threads(),
+            "kind": "port", "layer_us": round(el * 1e6, 1),
+            "sample": f"one decoder layer's four projections at {rows} rows, {reps} passes"}
 
 
 def cpu_attention_baseline(kind, args_np, flops):
