@@ -105,9 +105,13 @@ constexpr int SM_COST_OFF = SM_TILE_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16; 
 constexpr int Q_PITCH = HD + 8;          // 272-byte rows: conflict-free fragment reads
 constexpr int SM_Q = SM_COST_OFF + ((MAX_BATCH + 1) * 4 + 15) / 16 * 16;
 constexpr int SM_BARS = SM_Q + 2 * QH * Q_PITCH * 2;
-// full[STAGES], empty[STAGES], q_full[2], q_empty[2], app_free[2], merge_full, merge_empty,
-// app_done[2]
-constexpr int SM_MISC = SM_BARS + (2 * STAGES + 10) * 8;
+// full[STAGES], empty[STAGES], q_full[2], q_empty[2], merge_full, merge_empty,
+// app_stage[APP_SLOTS]
+// Append handshakes in flight: every claimed append stage waits for the
+// sequence warp before it can be consumed, so at most STAGES are open at once.
+constexpr int APP_SLOTS = 8;
+static_assert(APP_SLOTS > STAGES, "append handshake slots must outnumber the ring stages");
+constexpr int SM_MISC = SM_BARS + (2 * STAGES + 6 + APP_SLOTS) * 8;
 constexpr int SMEM_BYTES = SM_MISC + 64;
 
 static_assert(SMEM_BYTES <= 227 * 1024, "decode shared memory exceeds the sm_100 limit");
@@ -253,16 +257,16 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
   uint32_t* cost_off = reinterpret_cast<uint32_t*>(smem + SM_COST_OFF);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + SM_BARS);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* q_full = empty_bar + STAGES;   // [2] rotated q (and the append) of a sequence are done
+  uint64_t* q_full = empty_bar + STAGES;   // [2] the rotated q of a sequence is in its slot
   uint64_t* q_empty = q_full + 2;          // [2] every consumer warp has read the slot
-  uint64_t* app_free = q_empty + 2;        // [2] the copy warp has left the slot's sequence
-  uint64_t* merge_full = app_free + 2;     // every consumer warp wrote its (O, m, l)
+  uint64_t* merge_full = q_empty + 2;      // every consumer warp wrote its (O, m, l)
   uint64_t* merge_empty = merge_full + 1;  // the merge warp has read the merge buffer
-  uint64_t* app_done = merge_empty + 1;    // [2] the KV append of a sequence is visible
+  uint64_t* app_stage = merge_empty + 1;   // [APP_SLOTS] a sequence's append tile has its ring stage
   __half* qs = reinterpret_cast<__half*>(smem + SM_Q);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   // misc[0]: abort flag, misc[1]: "this CTA combines" flag, misc[2..3]: the
-  // combine's CTA range, misc[4]: the sequence warp's opening loads are issued
+  // combine's CTA range, misc[4]: the sequence warp's opening loads are issued,
+  // misc[8..15]: the ring stage of the append tile of sequence n, at 8 + n % APP_SLOTS
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -289,15 +293,18 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     misc[1] = 0;
     misc[4] = 0;
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 32);   // the copy warp's lanes
+      // the copy warp's lanes twice: once when their copies land, once more
+      // from the lanes that fill the tile's last row -- the copy warp's own,
+      // or, for the tile holding a sequence's appended row, the sequence
+      // warp's, which write that row straight into the stage
+      mbar_init(&full_bar[s], 64);
       mbar_init(&empty_bar[s], 4);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 32);     // the sequence warp's lanes
       mbar_init(&q_empty[s], CONSUMER_WARPS);
-      mbar_init(&app_free[s], 1);
-      mbar_init(&app_done[s], 32);   // the sequence warp's lanes
     }
+    for (int s = 0; s < APP_SLOTS; ++s) mbar_init(&app_stage[s], 1);   // the copy warp's lane 0
     mbar_init(merge_full, CONSUMER_WARPS);
     mbar_init(merge_empty, 1);
     fence_mbar_init();
@@ -422,14 +429,17 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
     // but free ring stages, so the ring stays full across sequence changes.
     // Warp 9, the sequence warp, does the per-sequence work ahead of the
     // stream: for each sequence of the CTA's range, in order, it writes the
-    // decode-M-RoPE-rotated q into a double-buffered shared-memory slot and,
+    // decode-M-RoPE-rotated q into a double-buffered shared-memory slot and
     // announces the slot to the consumers (q_full); then, when the range
-    // holds the sequence's appended row, it stores the rotated new key and
-    // the new value in cache row cache_tokens[b] (the KV append) and announces
-    // that (app_done), so the append never delays the consumers' start.  The
-    // copy warp waits for app_done before copying the tile that holds the
-    // appended row, and releases the slot's append (app_free) when it leaves
-    // the sequence, which keeps the slot's barrier phases in step.
+    // holds the sequence's appended row (the last row of its last tile), it
+    // writes the rotated new key and the new value straight into that tile's
+    // ring stage -- which the copy warp claims, fills with the tile's other
+    // rows and names (app_stage) without waiting -- completes the stage's
+    // full barrier, and stores the row in cache row cache_tokens[b] (the KV
+    // append) for the steps to come.  So neither the stream nor the consumers
+    // wait for the append to reach memory and come back, and the copy warp
+    // never waits for the sequence warp: it may run ahead of it by as many
+    // sequences as the ring has stages.
     bool aborted = false;
     uint32_t b = seq_of(t0);
     if (warp == CONSUMER_WARPS) {
@@ -449,7 +459,6 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       for (uint64_t it = 0; it < t1 - t0; ++it) {
         const uint64_t gt = t0 + it;
         if (gt >= tile_off[b + 1]) {
-          if (lane == 0) mbar_arrive(&app_free[nseq & 1u]);
           ++nseq;
           while (gt >= tile_off[b + 1]) ++b;
           kc = reinterpret_cast<uint8_t*>(p.k_cache[b]);
@@ -464,19 +473,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           aborted = true;
           break;
         }
-        if (row0 + n == L &&   // the tile that holds the appended row L - 1
-            (misc[0] || !mbar_wait(&app_done[nseq & 1u], (nseq >> 1) & 1u))) {
-          aborted = true;
-          break;
+        // the tile that holds the appended row L - 1: the sequence warp
+        // writes that row into this stage
+        const bool append = row0 + n == L;
+        if (append) {
+          __syncwarp();
+          if (lane == 0) {
+            misc[8 + nseq % APP_SLOTS] = static_cast<uint32_t>(stage);
+            mbar_arrive(&app_stage[nseq % APP_SLOTS]);
+          }
         }
         const uint32_t ks = smem_u32(smem + SM_K + stage * STAGE_BYTES) + lane * 16;
         const uint32_t vs = smem_u32(smem + SM_V + stage * STAGE_BYTES) + lane * 16;
-        for (uint32_t r = 0; r < n; ++r) {
+        const uint32_t nc = append ? n - 1 : n;
+        for (uint32_t r = 0; r < nc; ++r) {
           const size_t src = (size_t)(row0 + r) * ROW_BYTES + lane * 16;
           cp_async_16(ks + r * ROW_PITCH, kc + src);
           cp_async_16(vs + r * ROW_PITCH, vc + src);
         }
         cp_async_arrive_noinc(&full_bar[stage]);
+        if (!append) mbar_arrive(&full_bar[stage]);
       }
     } else if (warp == CONSUMER_WARPS + 1) {
       // sequence warp: lane l rotates query head l/2, dims 32(l%2)..+31 and
@@ -490,8 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
       uint32_t nseq = 0;
       while (true) {
         const uint32_t slot = nseq & 1u, round = nseq >> 1;
-        if (misc[0] || !mbar_wait(&q_empty[slot], (round & 1u) ^ 1u) ||
-            !mbar_wait(&app_free[slot], (round & 1u) ^ 1u)) {
+        if (misc[0] || !mbar_wait(&q_empty[slot], (round & 1u) ^ 1u)) {
           aborted = true;
           break;
         }
@@ -514,7 +529,6 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         if (append_tile >= t0 && append_tile < t1) {
           // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
           // 8(l%16)..+7; the M-RoPE partners (d +- 64) sit in lane l ^ 8
-          const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
           const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)b * p.kv_stride) + lane);
           const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)b * p.kv_stride) + lane);
           uint4 ky;
@@ -522,12 +536,27 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           ky.y = __shfl_xor_sync(0xffffffffu, kx.y, 8);
           ky.z = __shfl_xor_sync(0xffffffffu, kx.z, 8);
           ky.w = __shfl_xor_sync(0xffffffffu, kx.w, 8);
-          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.k_cache[b]) + off) =
-              mrope8(kx, ky, (lane & 15) * 8, p, rrow);
+          const uint4 kr = mrope8(kx, ky, (lane & 15) * 8, p, rrow);
+          // into the append tile's ring stage, once the copy warp has claimed it.
+          // The copy warp may run up to STAGES sequences ahead, so the
+          // handshake has APP_SLOTS slots by sequence number; every sequence
+          // but possibly the range's last has its append here, so a slot's
+          // phases advance once per APP_SLOTS sequences
+          if (misc[0] ||
+              !mbar_wait(&app_stage[nseq % APP_SLOTS], (nseq / APP_SLOTS) & 1u)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t stage = misc[8 + nseq % APP_SLOTS];
+          const uint32_t r = ct % TILE;
+          *reinterpret_cast<uint4*>(smem + SM_K + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = kr;
+          *reinterpret_cast<uint4*>(smem + SM_V + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = vx;
+          mbar_arrive(&full_bar[stage]);
+          // and into the cache for the steps to come (a later launch reads it)
+          const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.k_cache[b]) + off) = kr;
           *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.v_cache[b]) + off) = vx;
-          __threadfence();   // visible before the copy warp reads the row back
         }
-        mbar_arrive(&app_done[slot]);
         ++nseq;
         const uint64_t s1 = umin64(t1, tile_off[b + 1]);
         if (s1 >= t1) break;
