@@ -190,14 +190,54 @@ __device__ __forceinline__ uint4 mrope8(uint4 x, uint4 y, uint32_t d0, const Par
 
 // Final combine of a sequence split over CTAs first..last (CTA = token order):
 // out = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the partial records
-// of query head hq, dims d0 .. d0 + 8 NCH - 1.  The records are read in groups
-// of eight with independent loads, so a combine costs two dependent L2 rounds
-// per group (the maxima, then m, l and O together) instead of a round per
-// record and pass; the sums still run record by record in CTA order.
+// of query head hq, dims d0 .. d0 + 8 NCH - 1.  With eight records or fewer
+// and eight dims a thread (the consumers' combine, on the launch's critical
+// path) every m, l and O is loaded in one round of independent loads.
+// Otherwise the records are read in groups of eight with independent loads:
+// two dependent L2 rounds per group (the maxima, then m, l and O together)
+// instead of a round per record and pass.  Either way the sums run record by
+// record in CTA order.
 template <int NCH>
 __device__ __forceinline__ void combine_split(const Params& p, uint32_t b, uint32_t first,
                                               uint32_t last, int hq, int d0) {
   const float* base = p.partials + (size_t)b * PART_FLOATS;
+  if (NCH == 1 && last - first < 8) {
+    // up to eight records (the common case): m, l and O of every record in
+    // one round of independent loads, then the same sums in CTA order
+    float mv[8], lv[8];
+    float4 u[8], w[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (first + e <= last) {
+        const float* r = base + (size_t)(first + e) * PART_FLOATS;
+        mv[e] = __ldcg(r + QH * HD + hq);
+        lv[e] = __ldcg(r + QH * HD + QH + hq);
+        u[e] = __ldcg(reinterpret_cast<const float4*>(r + hq * HD + d0));
+        w[e] = __ldcg(reinterpret_cast<const float4*>(r + hq * HD + d0 + 4));
+      }
+    }
+    float Mc = -CUDART_INF_F;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (first + e <= last) Mc = fmaxf(Mc, mv[e]);
+    float Lc = 0.f, A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (first + e <= last) {
+        const float f = mv[e] == -CUDART_INF_F ? 0.f : fast_exp2(mv[e] - Mc);
+        Lc += lv[e] * f;
+        A[0] += u[e].x * f; A[1] += u[e].y * f; A[2] += u[e].z * f; A[3] += u[e].w * f;
+        A[4] += w[e].x * f; A[5] += w[e].y * f; A[6] += w[e].z * f; A[7] += w[e].w * f;
+      }
+    }
+    const float inv = 1.f / Lc;
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __float2half_rn(A[e] * inv);
+    *reinterpret_cast<uint4*>(p.out + ((size_t)b * QH + hq) * HD + d0) =
+        *reinterpret_cast<uint4*>(o);
+    return;
+  }
   float Mc = -CUDART_INF_F;
   for (uint32_t i0 = first; i0 <= last; i0 += 8) {
     float mv[8];
