@@ -551,7 +551,10 @@ int linear_launch(const LinearArgs& a, cudaStream_t stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = S > 1 ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, lin::linear_kernel, maps, p) != cudaSuccess) return PVLC_CUDA_ERROR;
+  if (cudaLaunchKernelEx(&cfg, lin::linear_kernel, maps, p) != cudaSuccess) {
+    cudaGetLastError();   // a refused launch (e.g. no room for the cluster) is not sticky
+    return PVLC_CUDA_ERROR;
+  }
   return PVLC_OK;
 }
 
