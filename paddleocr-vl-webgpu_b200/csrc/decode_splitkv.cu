@@ -91,6 +91,15 @@ constexpr uint64_t MIN_TILES_PER_CTA = PVLC_DECODE_MIN_TILES_PER_CTA;
 #define PVLC_DECODE_PREFETCH_TILES 0
 #endif
 constexpr uint64_t PREFETCH_TILES = PVLC_DECODE_PREFETCH_TILES;
+// A sequence piece of at most this many tiles has its append written before
+// the next sequence's q (the consumers reach its last tile soon); longer
+// pieces get the next q first.  Swept on B200 (2, 4, 6, 8, 12): 6 keeps the
+// 64-sequence gain and 32 sequences of ~1250 rows at their earlier time (2:
+// +8 % there).
+#ifndef PVLC_DECODE_APPEND_FIRST_TILES
+#define PVLC_DECODE_APPEND_FIRST_TILES 6
+#endif
+constexpr uint64_t APPEND_FIRST_TILES = PVLC_DECODE_APPEND_FIRST_TILES;
 
 // shared memory map (bytes)
 constexpr int SM_K = 0;
@@ -543,17 +552,26 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
         asm volatile("" ::: "memory");
         misc[4] = 1;
       }
-      uint32_t nseq = 0;
-      while (true) {
-        const uint32_t slot = nseq & 1u, round = nseq >> 1;
-        if (misc[0] || !mbar_wait(&q_empty[slot], (round & 1u) ^ 1u)) {
-          aborted = true;
-          break;
-        }
-        const uint32_t ct = __ldg(p.cache_tokens + b);
-        const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + b) : ct;
+      // Sequence n of the range takes q slot n % 2; its rotated q is written
+      // one sequence ahead of its append, so the consumers find the next
+      // sequence's q ready when they reach it (the append of sequence n
+      // waits for the copy warp to reach that sequence's last tile).  When
+      // the range holds at most two tiles of sequence n, its append comes
+      // first: the consumers reach that tile almost at once.
+      auto next_seq = [&](uint32_t bb) -> uint32_t {   // the range's sequence after bb, or B
+        const uint64_t s1 = umin64(t1, tile_off[bb + 1]);
+        if (s1 >= t1) return B;
+        ++bb;
+        while (tile_off[bb + 1] <= s1) ++bb;   // skip sequences with no tiles
+        return bb;
+      };
+      auto produce_q = [&](uint32_t n, uint32_t bb) -> bool {
+        const uint32_t slot = n & 1u, round = n >> 1;
+        if (misc[0] || !mbar_wait(&q_empty[slot], (round & 1u) ^ 1u)) return false;
+        const uint32_t ct = __ldg(p.cache_tokens + bb);
+        const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + bb) : ct;
         const int h = lane >> 1;
-        const __half* qrow = p.q + (size_t)b * p.q_stride + (size_t)h * HD;
+        const __half* qrow = p.q + (size_t)bb * p.q_stride + (size_t)h * HD;
         __half* qdst = qs + (slot * QH + h) * Q_PITCH;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
@@ -563,45 +581,55 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(const Params p) {
           *reinterpret_cast<uint4*>(qdst + d) = mrope8(lo, hi, d, p, rrow);
           *reinterpret_cast<uint4*>(qdst + d + 64) = mrope8(hi, lo, d + 64, p, rrow);
         }
-        // the consumers need only the rotated q: announce it before the append
         mbar_arrive(&q_full[slot]);
-        const uint64_t append_tile = tile_off[b] + ct / TILE;
-        if (append_tile >= t0 && append_tile < t1) {
-          // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
-          // 8(l%16)..+7; the M-RoPE partners (d +- 64) sit in lane l ^ 8
-          const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)b * p.kv_stride) + lane);
-          const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)b * p.kv_stride) + lane);
-          uint4 ky;
-          ky.x = __shfl_xor_sync(0xffffffffu, kx.x, 8);
-          ky.y = __shfl_xor_sync(0xffffffffu, kx.y, 8);
-          ky.z = __shfl_xor_sync(0xffffffffu, kx.z, 8);
-          ky.w = __shfl_xor_sync(0xffffffffu, kx.w, 8);
-          const uint4 kr = mrope8(kx, ky, (lane & 15) * 8, p, rrow);
-          // into the append tile's ring stage, once the copy warp has claimed it.
-          // The copy warp may run up to STAGES sequences ahead, so the
-          // handshake has APP_SLOTS slots by sequence number; every sequence
-          // but possibly the range's last has its append here, so a slot's
-          // phases advance once per APP_SLOTS sequences
-          if (misc[0] ||
-              !mbar_wait(&app_stage[nseq % APP_SLOTS], (nseq / APP_SLOTS) & 1u)) {
-            aborted = true;
-            break;
-          }
-          const uint32_t stage = misc[8 + nseq % APP_SLOTS];
-          const uint32_t r = ct % TILE;
-          *reinterpret_cast<uint4*>(smem + SM_K + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = kr;
-          *reinterpret_cast<uint4*>(smem + SM_V + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = vx;
-          mbar_arrive(&full_bar[stage]);
-          // and into the cache for the steps to come (a later launch reads it)
-          const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
-          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.k_cache[b]) + off) = kr;
-          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.v_cache[b]) + off) = vx;
+        return true;
+      };
+      auto append = [&](uint32_t n, uint32_t bb) -> bool {
+        const uint32_t ct = __ldg(p.cache_tokens + bb);
+        const uint64_t append_tile = tile_off[bb] + ct / TILE;
+        if (append_tile < t0 || append_tile >= t1) return true;
+        const uint32_t rrow = p.rope_row ? __ldg(p.rope_row + bb) : ct;
+        // appended row: lane l holds bytes 16l..16l+15 = head l/16, dims
+        // 8(l%16)..+7; the M-RoPE partners (d +- 64) sit in lane l ^ 8
+        const uint4 kx = __ldg(reinterpret_cast<const uint4*>(p.k_new + (size_t)bb * p.kv_stride) + lane);
+        const uint4 vx = __ldg(reinterpret_cast<const uint4*>(p.v_new + (size_t)bb * p.kv_stride) + lane);
+        uint4 ky;
+        ky.x = __shfl_xor_sync(0xffffffffu, kx.x, 8);
+        ky.y = __shfl_xor_sync(0xffffffffu, kx.y, 8);
+        ky.z = __shfl_xor_sync(0xffffffffu, kx.z, 8);
+        ky.w = __shfl_xor_sync(0xffffffffu, kx.w, 8);
+        const uint4 kr = mrope8(kx, ky, (lane & 15) * 8, p, rrow);
+        // into the append tile's ring stage, once the copy warp has claimed it.
+        // The copy warp may run up to STAGES sequences ahead, so the
+        // handshake has APP_SLOTS slots by sequence number; every sequence
+        // but possibly the range's last has its append here, so a slot's
+        // phases advance once per APP_SLOTS sequences
+        if (misc[0] || !mbar_wait(&app_stage[n % APP_SLOTS], (n / APP_SLOTS) & 1u)) return false;
+        const uint32_t stage = misc[8 + n % APP_SLOTS];
+        const uint32_t r = ct % TILE;
+        *reinterpret_cast<uint4*>(smem + SM_K + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = kr;
+        *reinterpret_cast<uint4*>(smem + SM_V + stage * STAGE_BYTES + r * ROW_PITCH + lane * 16) = vx;
+        mbar_arrive(&full_bar[stage]);
+        // and into the cache for the steps to come (a later launch reads it)
+        const size_t off = (size_t)ct * ROW_BYTES + lane * 16;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.k_cache[bb]) + off) = kr;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.v_cache[bb]) + off) = vx;
+        return true;
+      };
+      uint32_t nseq = 0;
+      aborted = !produce_q(0, b);
+      while (!aborted) {
+        const uint32_t bn = next_seq(b);
+        // tiles of sequence b in the range: a short piece's append goes first
+        const uint64_t pc = umin64(t1, tile_off[b + 1]) - umax64(t0, tile_off[b]);
+        if (pc <= APPEND_FIRST_TILES) {
+          if (!append(nseq, b) || (bn < B && !produce_q(nseq + 1, bn))) aborted = true;
+        } else {
+          if ((bn < B && !produce_q(nseq + 1, bn)) || !append(nseq, b)) aborted = true;
         }
+        if (aborted || bn >= B) break;
         ++nseq;
-        const uint64_t s1 = umin64(t1, tile_off[b + 1]);
-        if (s1 >= t1) break;
-        ++b;
-        while (tile_off[b + 1] <= s1) ++b;   // skip sequences with no tiles
+        b = bn;
       }
     } else {
       // merge warp: per sequence of the range except the last, in order,
