@@ -23,3 +23,22 @@ def test_prompt_ids_hold_one_placeholder_per_merged_patch():
     assert sum(1 for t in ids if t == cfg.image_token_id) == 1225
     assert len(ids) == 1238
     assert np.asarray(ids).dtype.kind == "i"
+
+
+def test_gate_up_blocks_layout():
+    """The fused SiLU-gate projection's weight: 128-row blocks of 64 gate rows followed by
+    the 64 up rows of the same output columns (pvlc_linear with gate = 1)."""
+    from pvlc_b200 import ops
+    i, k = 192, 8
+    g = torch.arange(i * k, dtype=torch.float32).reshape(i, k)
+    u = -torch.arange(i * k, dtype=torch.float32).reshape(i, k) - 1
+    w = ops.gate_up_blocks(g, u)
+    assert w.shape == (2 * i, k) and w.is_contiguous()
+    for blk in range(i // 64):
+        assert torch.equal(w[128 * blk:128 * blk + 64], g[64 * blk:64 * blk + 64])
+        assert torch.equal(w[128 * blk + 64:128 * blk + 128], u[64 * blk:64 * blk + 64])
+    import pytest
+    with pytest.raises(ValueError):
+        ops.gate_up_blocks(g[:100], u[:100])
+    with pytest.raises(ValueError):
+        ops.gate_up_blocks(g, u[:64])
