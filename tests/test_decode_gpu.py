@@ -86,6 +86,11 @@ def test_decode_config1_single_sequence(cuda_lib):
 @pytest.mark.parametrize("lengths", [
     [0, 1, 15, 16, 31, 32, 33, 63],          # tile and half-tile boundaries
     [700, 3, 1500, 64, 65, 4000],            # ragged batch, multi-CTA sequences
+    # forty one-tile sequences, ~4 per CTA: the copy warp runs several
+    # sequences ahead of the sequence warp's appends
+    [(7 * i) % 31 for i in range(40)],
+    # one-tile sequences between long ones: append-first and q-first pieces
+    [5, 900, 2, 0, 30, 1300, 17, 3, 640, 1],
 ])
 def test_decode_ragged_batch_with_poisoned_tails(cuda_lib, lengths):
     cap = max(lengths) + 7
