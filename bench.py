@@ -46,7 +46,7 @@ UNIT = "GB/s"
 # profiles/vision_tc_kernel_config1.txt, profiles/prefill_attn_kernel_config2.txt).
 # The decode capture is one 64-sequence launch: its traffic / algorithmic-bytes
 # ratio scales the figure to the bench's average launch.
-DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 282.62e6 / 278.20e6
+DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE = 283.20e6 / 278.20e6
 VISION_TC_TRAFFIC_BYTES = 61.00e6
 PREFILL_ATTN_TRAFFIC_BYTES = 11.37e6
 # checkpoint conversion, one launch over the whole payload
